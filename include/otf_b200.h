@@ -1,0 +1,136 @@
+/*
+ * otf_b200.h -- C ABI of the B200 (sm_100a) quantized-decode library.
+ *
+ * Every entry point takes plain device pointers, element strides, sizes and a
+ * cudaStream_t passed as void*, launches asynchronously on that stream and
+ * returns an int status (OTF_OK == 0).  Nothing allocates device memory;
+ * outputs are caller-owned.  Half-precision tensors are IEEE binary16 bit
+ * patterns (uint16_t).  No exceptions cross this boundary.
+ *
+ * Layouts are the reference package's own (otf_llm, GT-Labs-AI/otf-llm-engine):
+ *   packed  uint8 [N, K/4]   code k of row n at bits 2*(k%4) of byte k/4
+ *                            (pack_2bit_uint8, otf_llm/symmetric_2bit_engine.py:100-107)
+ *   scales  fp16  [N, K/G]   per-group scale (symmetric_2bit_engine.py:190)
+ *   zeros   fp16  [N, K/G]   per-group offset, asymmetric layers only
+ *                            (otf_llm/otf_2bit_quantizer.py:65-71)
+ *   outlier_vals fp16 [N, k] and outlier_idx int64 [k]: fp16 anchor columns
+ *                            (symmetric_2bit_engine.py:200-206, :230-232)
+ *   weight_int8 int8 [V, D], scales fp16 [V, 1] (symmetric_2bit_engine.py:17-91)
+ */
+#ifndef OTF_B200_H
+#define OTF_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define OTF_API __attribute__((visibility("default")))
+#else
+#define OTF_API
+#endif
+
+/* Status codes. */
+#define OTF_OK 0
+#define OTF_ERR_INVALID 1      /* bad pointer, size, stride or alignment */
+#define OTF_ERR_UNSUPPORTED 2  /* shape/codebook this build cannot run */
+#define OTF_ERR_CUDA 3         /* a CUDA runtime call failed (see otf_last_cuda_error) */
+#define OTF_ERR_DEVICE 4       /* current device is not sm_100 */
+
+/* Flags for otf2b_linear. */
+#define OTF_FLAG_CLAMP 1u          /* clamp output to [-65504, 65504] (SymmetricOTF2BitLinear) */
+#define OTF_FLAG_FORCE_GENERIC 2u  /* use the portable CUDA-core kernel (testing) */
+
+/* Library version as 10000*major + 100*minor + patch. */
+OTF_API int otf_version(void);
+
+/* Human-readable name of a status code. */
+OTF_API const char* otf_status_string(int status);
+
+/* Last CUDA error code seen by this thread inside the library (cudaError_t as int). */
+OTF_API int otf_last_cuda_error(void);
+
+/*
+ * One 2-bit quantized linear layer:
+ *   y[m,n] = sum_k fp16(x[m,k]*mask[k]) * (codebook[q[n,k]] * scales[n,k/G] + zeros[n,k/G])
+ *            + bias[n] + sum_j x[m, outlier_idx[j]] * outlier_vals[n,j] + residual[m,n]
+ * accumulated in fp32 and stored as fp16, clamped to +-65504 when OTF_FLAG_CLAMP is set.
+ *
+ * Replaces the reference's whole forward for this layer: the mask multiply and
+ * dispatch of triton_symmetric_2bit_gemm (otf_llm/otf_triton_2bit_kernel.py:164-194),
+ * its native op sym2bit_gemv_cuda / sym2bit_gemv_warp_kernel (:23-113), the LUT
+ * fallback (:146-161, :188-194), and the bias / outlier / clamp tail of
+ * SymmetricOTF2BitLinear.forward (otf_llm/symmetric_2bit_engine.py:214-235) and
+ * OTF2BitLinear.forward (otf_llm/otf_2bit_quantizer.py:193-221, zeros honoured).
+ *
+ * x: fp16 [M, ldx]; y: fp16 [M, ldy]; codebook: HOST pointer to 4 floats.
+ * zeros, mask, outlier_idx/outlier_vals (n_outliers may be 0), bias and residual may be
+ * NULL.  residual (fp16 [M, ld_residual]) is this package's fusion of the decoder's
+ * skip connection; the reference added it in a separate torch op.
+ * The fast path needs a codebook with c0 + c3 == c1 + c2 (every symmetric one),
+ * G a multiple of 32, K a multiple of G and 16-byte aligned packed rows;
+ * other shapes run a portable CUDA-core kernel.
+ */
+OTF_API int otf2b_linear(const void* x, int64_t ldx,
+                         const uint8_t* packed, int64_t ld_packed,
+                         const void* scales, int64_t ld_scales,
+                         const void* zeros, int64_t ld_zeros,
+                         const float* codebook,
+                         const void* mask,
+                         const int64_t* outlier_idx, int64_t n_outliers,
+                         const void* outlier_vals, int64_t ld_outlier_vals,
+                         const void* bias,
+                         const void* residual, int64_t ld_residual,
+                         void* y, int64_t ldy,
+                         int64_t M, int64_t N, int64_t K, int64_t group_size,
+                         uint32_t flags, void* stream);
+
+/*
+ * Unpack 2-bit codes to one byte per code: codes[n,k] = q[n,k] in {0..3}.
+ * The inverse of pack_2bit_uint8 (otf_llm/symmetric_2bit_engine.py:100-107) and the
+ * code-extraction step of unpack_2bit_uint8 (otf_llm/otf_2bit_quantizer.py:58-63).
+ * Used to prove bit-exact unpacking.  codes: uint8 [N, ld_codes].
+ */
+OTF_API int otf2b_unpack_codes(const uint8_t* packed, int64_t ld_packed, int64_t N, int64_t K,
+                               uint8_t* codes, int64_t ld_codes, void* stream);
+
+/*
+ * INT8 shared-vocabulary LM head:
+ *   logits[m,v] = scales[v] * sum_d x[m,d] * w[v,d]   (fp32, NaN -> 0, clamped to +-65504)
+ * Replaces QuantizedLinearHead.forward (otf_llm/symmetric_2bit_engine.py:75-91).
+ * x: fp16 [M, ldx]; w: int8 [V, ldw]; scales: fp16 [V]; logits: fp32 [M, ldl].
+ */
+OTF_API int otf_i8_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scales,
+                        float* logits, int64_t ldl, int64_t M, int64_t V, int64_t D, void* stream);
+
+/*
+ * INT8 embedding gather: out[t,:] = fp16(w[ids[t],:]) * scales[ids[t]] in fp16,
+ * bit-identical to QuantizedEmbedding.forward (otf_llm/symmetric_2bit_engine.py:41-47).
+ * Ids outside [0, V) produce a zero row and set *bad_ids (device int32, may be NULL) to 1.
+ * ids: int64 [n]; out: fp16 [n, ldo].
+ */
+OTF_API int otf_i8_embed(const int64_t* ids, int64_t n, const int8_t* w, int64_t ldw, const void* scales,
+                         void* out, int64_t ldo, int64_t V, int64_t D, int32_t* bad_ids, void* stream);
+
+/*
+ * RMSNorm over the last dimension, Llama semantics (transformers LlamaRMSNorm, the norm
+ * the reference runner keeps from HF, otf_llm/run_symmetric_2bit.py:139-147):
+ *   out[m,:] = w * fp16( x[m,:] * rsqrt(mean(x[m,:]^2) + eps) )   (statistics in fp32)
+ * x, w, out: fp16.  w may be NULL (all ones).
+ */
+OTF_API int otf_rmsnorm(const void* x, int64_t ldx, const void* w, float eps, void* out, int64_t ldo,
+                        int64_t M, int64_t K, void* stream);
+
+/*
+ * Gated activation of the Llama MLP: out = fp16( fp16(silu(g)) * u ), elementwise over n
+ * fp16 values (act_fn(gate_proj(x)) * up_proj(x) in transformers LlamaMLP).
+ */
+OTF_API int otf_silu_mul(const void* g, const void* u, void* out, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OTF_B200_H */

@@ -1,0 +1,276 @@
+"""ctypes binding of libotfb200.so, the sm_100a kernels behind this package.
+
+Every wrapper takes torch CUDA tensors, checks device, dtype, shape and strides,
+passes raw pointers plus the current CUDA stream across the C ABI declared in
+``include/otf_b200.h``, and turns a nonzero status into ``RuntimeError``.  There
+is no CPU or pure-PyTorch fallback: a missing library or a non-CUDA tensor is an
+error.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional, Sequence
+
+import torch
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libotfb200.so")
+_lib: Optional[ctypes.CDLL] = None
+
+OTF_FLAG_CLAMP = 1
+OTF_FLAG_FORCE_GENERIC = 2
+
+# Names exported by the library; kept in step with include/otf_b200.h.
+EXPORTS = (
+    "otf_version",
+    "otf_status_string",
+    "otf_last_cuda_error",
+    "otf2b_linear",
+    "otf2b_unpack_codes",
+    "otf_i8_head",
+    "otf_i8_embed",
+    "otf_rmsnorm",
+    "otf_silu_mul",
+)
+
+
+def library_path() -> str:
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """Load the native library once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_LIB_PATH):
+        raise RuntimeError(
+            f"libotfb200.so not found at {_LIB_PATH}; build it with `make -C otf-llm-engine_b200/csrc` "
+            "(or __graft_entry__.build()). There is no fallback path.")
+    L = ctypes.CDLL(_LIB_PATH)
+    i64, vp, u32, i32 = ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int
+    L.otf_version.restype = i32
+    L.otf_status_string.argtypes = [i32]
+    L.otf_status_string.restype = ctypes.c_char_p
+    L.otf_last_cuda_error.restype = i32
+    L.otf2b_linear.argtypes = [vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, vp, i64, vp, vp, i64, vp, i64,
+                               i64, i64, i64, i64, u32, vp]
+    L.otf2b_linear.restype = i32
+    L.otf2b_unpack_codes.argtypes = [vp, i64, i64, i64, vp, i64, vp]
+    L.otf2b_unpack_codes.restype = i32
+    L.otf_i8_head.argtypes = [vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, vp]
+    L.otf_i8_head.restype = i32
+    L.otf_i8_embed.argtypes = [vp, i64, vp, i64, vp, vp, i64, i64, i64, vp, vp]
+    L.otf_i8_embed.restype = i32
+    L.otf_rmsnorm.argtypes = [vp, i64, vp, ctypes.c_float, vp, i64, i64, i64, vp]
+    L.otf_rmsnorm.restype = i32
+    L.otf_silu_mul.argtypes = [vp, vp, vp, i64, vp]
+    L.otf_silu_mul.restype = i32
+    _lib = L
+    return L
+
+
+def _check(status: int, what: str) -> None:
+    if status != 0:
+        L = lib()
+        msg = L.otf_status_string(status).decode()
+        if status == 3:
+            msg += f" (cudaError {L.otf_last_cuda_error()})"
+        raise RuntimeError(f"{what} failed: {msg}")
+
+
+def _stream(dev: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[ctypes.c_void_p]:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _need_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor: this package runs its hot path on B200 GPUs only "
+                           "and has no CPU fallback")
+
+
+def _rows(t: torch.Tensor, name: str, dtype: torch.dtype, cols: int) -> int:
+    """Check a row-major 2-D tensor with unit inner stride; return its row stride."""
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.dim() != 2 or t.shape[1] != cols or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a row-major [*, {cols}] tensor with unit inner stride, got "
+                         f"shape {tuple(t.shape)} strides {t.stride()}")
+    return t.stride(0) if t.shape[0] > 1 else max(t.stride(0), cols)
+
+
+_CB_CACHE: dict = {}
+
+
+def codebook_floats(codebook) -> Sequence[float]:
+    """The 4 codebook values as Python floats (the kernel takes them by value).
+
+    Device tensors are read once per (storage, version) and cached, so steady-state
+    calls neither synchronise nor copy (which also keeps forward graph-capturable).
+    """
+    if codebook is None:
+        from .symmetric_2bit_engine import LLOYD_MAX_SYMMETRIC_CENTROIDS
+        return [float(torch.tensor(c, dtype=torch.float16)) for c in LLOYD_MAX_SYMMETRIC_CENTROIDS]
+    if isinstance(codebook, torch.Tensor):
+        key = (codebook.data_ptr(), codebook._version, codebook.numel(), codebook.dtype, str(codebook.device))
+        vals = _CB_CACHE.get(key)
+        if vals is None:
+            vals = [float(v) for v in codebook.detach().float().cpu().tolist()]
+            if len(_CB_CACHE) > 4096:
+                _CB_CACHE.clear()
+            _CB_CACHE[key] = vals
+    else:
+        vals = [float(v) for v in codebook]
+    if len(vals) != 4:
+        raise ValueError("a 2-bit codebook has exactly 4 entries")
+    return vals
+
+
+def linear_2bit(x2d: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, group_size: int, codebook4,
+                *, zeros: Optional[torch.Tensor] = None, mask: Optional[torch.Tensor] = None,
+                outlier_idx: Optional[torch.Tensor] = None, outlier_vals: Optional[torch.Tensor] = None,
+                bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None, clamp: bool = True,
+                out: Optional[torch.Tensor] = None, force_generic: bool = False) -> torch.Tensor:
+    """y[M, N] fp16 = fused 2-bit linear over x2d [M, K] fp16 (see otf2b_linear)."""
+    _need_cuda(x2d, "x")
+    dev = x2d.device
+    M, K = x2d.shape
+    N = packed.shape[0]
+    if packed.shape[1] * 4 != K:
+        raise ValueError(f"packed has {packed.shape[1]} bytes per row, expected K/4 = {K // 4}")
+    if K % group_size:
+        raise ValueError(f"K={K} is not a multiple of group_size={group_size}")
+    for name, t in (("packed", packed), ("scales", scales), ("zeros", zeros), ("mask", mask),
+                    ("outlier_idx", outlier_idx), ("outlier_vals", outlier_vals), ("bias", bias),
+                    ("residual", residual)):
+        if t is not None:
+            _need_cuda(t, name)
+            if t.device != dev:
+                raise ValueError(f"{name} is on {t.device}, x on {dev}")
+    ldx = _rows(x2d, "x", torch.float16, K)
+    ldp = _rows(packed, "packed", torch.uint8, K // 4)
+    lds = _rows(scales, "scales", torch.float16, K // group_size)
+    ldz = _rows(zeros, "zeros", torch.float16, K // group_size) if zeros is not None else 0
+    if mask is not None and (mask.dtype != torch.float16 or mask.numel() != K or not mask.is_contiguous()):
+        raise ValueError("mask must be a contiguous fp16 vector of length K")
+    n_out = 0
+    ldo = 0
+    if outlier_idx is not None and outlier_vals is not None and outlier_idx.numel() > 0:
+        if outlier_idx.dtype != torch.int64 or not outlier_idx.is_contiguous():
+            raise ValueError("outlier_idx must be a contiguous int64 vector")
+        n_out = outlier_idx.numel()
+        ldo = _rows(outlier_vals, "outlier_vals", torch.float16, n_out)
+        if outlier_vals.shape[0] != N:
+            raise ValueError("outlier_vals must have one row per output feature")
+    else:
+        outlier_idx = outlier_vals = None
+    if bias is not None and (bias.dtype != torch.float16 or bias.numel() != N or not bias.is_contiguous()):
+        raise ValueError("bias must be a contiguous fp16 vector of length N")
+    ldr = 0
+    if residual is not None:
+        if residual.shape[0] != M:
+            raise ValueError("residual must have one row per activation row")
+        ldr = _rows(residual, "residual", torch.float16, N)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=dev)
+    ldy = _rows(out, "out", torch.float16, N)
+    cb = (ctypes.c_float * 4)(*codebook_floats(codebook4))
+    flags = (OTF_FLAG_CLAMP if clamp else 0) | (OTF_FLAG_FORCE_GENERIC if force_generic else 0)
+    with torch.cuda.device(dev):
+        st = lib().otf2b_linear(_ptr(x2d), ldx, _ptr(packed), ldp, _ptr(scales), lds, _ptr(zeros), ldz, cb,
+                                _ptr(mask), _ptr(outlier_idx), n_out, _ptr(outlier_vals), ldo, _ptr(bias),
+                                _ptr(residual), ldr, _ptr(out), ldy, M, N, K, group_size, flags, _stream(dev))
+    _check(st, "otf2b_linear")
+    return out
+
+
+def unpack_codes(packed: torch.Tensor, K: int) -> torch.Tensor:
+    """uint8 [N, K] codes in {0..3} from packed [N, K/4] (bit-exact unpack)."""
+    _need_cuda(packed, "packed")
+    ldp = _rows(packed, "packed", torch.uint8, K // 4)
+    N = packed.shape[0]
+    codes = torch.empty((N, K), dtype=torch.uint8, device=packed.device)
+    with torch.cuda.device(packed.device):
+        st = lib().otf2b_unpack_codes(_ptr(packed), ldp, N, K, _ptr(codes), K, _stream(packed.device))
+    _check(st, "otf2b_unpack_codes")
+    return codes
+
+
+def i8_head(x2d: torch.Tensor, w_i8: torch.Tensor, scales: torch.Tensor,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp32 logits [M, V] = (x2d @ w_i8.T) * scales (see otf_i8_head)."""
+    _need_cuda(x2d, "x")
+    M, D = x2d.shape
+    V = w_i8.shape[0]
+    ldx = _rows(x2d, "x", torch.float16, D)
+    ldw = _rows(w_i8, "weight_int8", torch.int8, D)
+    s = scales.reshape(-1)
+    if s.dtype != torch.float16 or s.numel() != V or not s.is_contiguous():
+        raise ValueError("scales must hold V contiguous fp16 values")
+    for name, t in (("weight_int8", w_i8), ("scales", s)):
+        _need_cuda(t, name)
+    if out is None:
+        out = torch.empty((M, V), dtype=torch.float32, device=x2d.device)
+    ldl = _rows(out, "logits", torch.float32, V)
+    with torch.cuda.device(x2d.device):
+        st = lib().otf_i8_head(_ptr(x2d), ldx, _ptr(w_i8), ldw, _ptr(s), _ptr(out), ldl, M, V, D,
+                               _stream(x2d.device))
+    _check(st, "otf_i8_head")
+    return out
+
+
+def i8_embed(ids: torch.Tensor, w_i8: torch.Tensor, scales: torch.Tensor,
+             bad_flag: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp16 [n, D] rows of the INT8 embedding (bit-identical to the reference gather)."""
+    _need_cuda(ids, "input_ids")
+    flat = ids.reshape(-1)
+    if flat.dtype != torch.int64:
+        flat = flat.to(torch.int64)
+    flat = flat.contiguous()
+    V, D = w_i8.shape
+    ldw = _rows(w_i8, "weight_int8", torch.int8, D)
+    s = scales.reshape(-1)
+    if s.dtype != torch.float16 or s.numel() != V or not s.is_contiguous():
+        raise ValueError("scales must hold V contiguous fp16 values")
+    out = torch.empty((flat.numel(), D), dtype=torch.float16, device=ids.device)
+    with torch.cuda.device(ids.device):
+        st = lib().otf_i8_embed(_ptr(flat), flat.numel(), _ptr(w_i8), ldw, _ptr(s), _ptr(out), D, V, D,
+                                _ptr(bad_flag), _stream(ids.device))
+    _check(st, "otf_i8_embed")
+    return out
+
+
+def rmsnorm(x2d: torch.Tensor, weight: Optional[torch.Tensor], eps: float,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Llama RMSNorm over rows of x2d (fp16), see otf_rmsnorm."""
+    _need_cuda(x2d, "x")
+    M, K = x2d.shape
+    ldx = _rows(x2d, "x", torch.float16, K)
+    if weight is not None and (weight.dtype != torch.float16 or weight.numel() != K or not weight.is_contiguous()):
+        raise ValueError("weight must be a contiguous fp16 vector of length K")
+    if out is None:
+        out = torch.empty_like(x2d)
+    ldo = _rows(out, "out", torch.float16, K)
+    with torch.cuda.device(x2d.device):
+        st = lib().otf_rmsnorm(_ptr(x2d), ldx, _ptr(weight), float(eps), _ptr(out), ldo, M, K, _stream(x2d.device))
+    _check(st, "otf_rmsnorm")
+    return out
+
+
+def silu_mul(g: torch.Tensor, u: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp16(silu(g)) * u elementwise (fp16), see otf_silu_mul."""
+    _need_cuda(g, "gate")
+    if g.shape != u.shape or g.dtype != torch.float16 or u.dtype != torch.float16:
+        raise ValueError("gate and up must be fp16 tensors of the same shape")
+    if not (g.is_contiguous() and u.is_contiguous()):
+        raise ValueError("gate and up must be contiguous")
+    if out is None:
+        out = torch.empty_like(g)
+    with torch.cuda.device(g.device):
+        st = lib().otf_silu_mul(_ptr(g), _ptr(u), _ptr(out), g.numel(), _stream(g.device))
+    _check(st, "otf_silu_mul")
+    return out

@@ -1,0 +1,66 @@
+"""GPU parity of the INT8 embedding (bit-exact) and LM head (max rel err 1e-3)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden, rel_err
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def test_embedding_golden_bit_exact(cuda_dev):
+    from otf_llm.symmetric_2bit_engine import QuantizedEmbedding
+    gd = load_golden("int8_v1000_d256")
+    emb = QuantizedEmbedding(*gd["weight_int8"].shape).to(cuda_dev)
+    emb.weight_int8.copy_(torch.from_numpy(gd["weight_int8"]))
+    emb.scales.copy_(torch.from_numpy(gd["scales"]))
+    out = emb(torch.from_numpy(gd["ids"]).to(cuda_dev)).cpu().numpy()
+    assert out.shape == gd["emb_out"].shape
+    assert np.array_equal(out.view(np.uint16), gd["emb_out"].view(np.uint16))
+
+
+def test_embedding_large_vocab_bit_exact(cuda_dev):
+    from otf_llm import _native
+    V, D = 128256, 3072
+    g = torch.Generator().manual_seed(11)
+    w = torch.randint(-127, 128, (V, D), generator=g, dtype=torch.int32).to(torch.int8)
+    s = (torch.rand(V, 1, generator=g) * 2e-4 + 1e-5).half()
+    ids = torch.randint(0, V, (64,), generator=g)
+    bad = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    out = _native.i8_embed(ids.to(cuda_dev), w.to(cuda_dev), s.to(cuda_dev), bad).cpu().numpy()
+    ref = oracle.i8_embed(ids.numpy(), w.numpy(), s.numpy())
+    assert np.array_equal(out.view(np.uint16), ref.view(np.uint16))
+    assert int(bad.item()) == 0
+    bad_ids = torch.tensor([0, V, -1], dtype=torch.int64, device=cuda_dev)
+    out = _native.i8_embed(bad_ids, w.to(cuda_dev), s.to(cuda_dev), bad)
+    assert int(bad.item()) == 1 and bool((out[1:] == 0).all())
+
+
+def test_head_golden(cuda_dev):
+    from otf_llm.symmetric_2bit_engine import QuantizedEmbedding, QuantizedLinearHead
+    gd = load_golden("int8_v1000_d256")
+    V, D = gd["weight_int8"].shape
+    emb = QuantizedEmbedding(V, D).to(cuda_dev)
+    emb.weight_int8.copy_(torch.from_numpy(gd["weight_int8"]))
+    emb.scales.copy_(torch.from_numpy(gd["scales"]))
+    head = QuantizedLinearHead(D, V).to(cuda_dev)
+    head.weight_int8 = emb.weight_int8
+    head.scales = emb.scales
+    for M in (1, 5):
+        lg = head(torch.from_numpy(gd[f"x_m{M}"]).to(cuda_dev).view(1, M, D)).view(M, V).cpu().numpy()
+        assert lg.dtype == np.float32
+        assert rel_err(lg, gd[f"logits_f64_m{M}"]) < 1e-3
+        assert rel_err(lg, gd[f"logits_m{M}"]) < 1.5e-3
+
+
+@pytest.mark.parametrize("V,D,M", [(128256, 3072, 1), (128256, 8192, 1), (1000, 200, 2), (4097, 64, 3)])
+def test_head_shapes(V, D, M, cuda_dev):
+    from otf_llm import _native
+    g = torch.Generator().manual_seed(V + D)
+    w = torch.randint(-127, 128, (V, D), generator=g, dtype=torch.int32).to(torch.int8)
+    s = (torch.rand(V, 1, generator=g) * 2e-4 + 1e-5).half()
+    x = torch.randn(M, D, generator=g).half()
+    lg = _native.i8_head(x.to(cuda_dev), w.to(cuda_dev), s.to(cuda_dev)).cpu().numpy()
+    ref = oracle.i8_head(x.numpy(), w.numpy(), s.numpy())
+    assert rel_err(lg, ref) < 1e-3
