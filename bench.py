@@ -303,8 +303,49 @@ def run_b200(args, cfg):
         print(json.dumps(line), flush=True)
 
 
+def run_case(args):
+    """Time (or let a profiler capture) one kernel on one shape: --case gemv:N:K or head:V:D."""
+    import torch
+    from otf_llm import _native
+    from otf_llm.decoder_stack import StackConfig, linear_bytes, random_quantized_linear
+    kind, a, b = args.case.split(":")
+    a, b = int(a), int(b)
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    if kind == "gemv":
+        cfg = StackConfig()
+        lay = random_quantized_linear(a, b, cfg, seed=3, device=dev)
+        x = torch.randn(1, b, device=dev).half()
+        y = torch.empty(1, a, dtype=torch.float16, device=dev)
+        n_out = lay.outlier_indices.numel()
+        fn = lambda: _native.linear_2bit(x, lay.packed_uint8, lay.scales, 64, lay.codebook,
+                                         mask=lay.outlier_mask_vector, outlier_idx=lay.outlier_indices,
+                                         outlier_vals=lay.outliers_fp16, out=y)
+        nbytes = linear_bytes(a, b, 64, n_out)
+    else:
+        w = torch.randint(-127, 128, (a, b), dtype=torch.int8, device=dev)
+        s = (torch.rand(a, 1, device=dev) * 1e-3).half()
+        x = torch.randn(1, b, device=dev).half()
+        out = torch.empty(1, a, device=dev)
+        fn = lambda: _native.i8_head(x, w, s, out)
+        nbytes = a * b + a * 2 + b * 2 + a * 4
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    print(json.dumps({"case": args.case, "us_per_launch": round(us, 3), "bytes": nbytes,
+                      "GBps_l2_warm": round(nbytes / us / 1e3, 1)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default=None, help="single-kernel timing/profiling case, e.g. gemv:11008:4096")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
@@ -315,7 +356,9 @@ def main():
     args = ap.parse_args()
     from otf_llm.decoder_stack import StackConfig
     cfg = StackConfig(layers=args.layers)
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args, cfg)
     else:
         run_b200(args, cfg)

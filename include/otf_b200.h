@@ -53,6 +53,14 @@ OTF_API const char* otf_status_string(int status);
 OTF_API int otf_last_cuda_error(void);
 
 /*
+ * Device-side failure flag of the pipelined kernels (synchronous).  Every wait inside a
+ * kernel is bounded; if one gives up (a pipeline that never completes), the kernel sets
+ * this flag instead of hanging.  Returns 1 if set, 0 if not, -1 on a CUDA error; with
+ * clear != 0 the flag is reset.  No counterpart in the reference (it has no pipelines).
+ */
+OTF_API int otf_device_error(int clear);
+
+/*
  * One 2-bit quantized linear layer:
  *   y[m,n] = sum_k fp16(x[m,k]*mask[k]) * (codebook[q[n,k]] * scales[n,k/G] + zeros[n,k/G])
  *            + bias[n] + sum_j x[m, outlier_idx[j]] * outlier_vals[n,j] + residual[m,n]

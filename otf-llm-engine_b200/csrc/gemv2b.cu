@@ -15,26 +15,36 @@
 //    flush recombines 64*C0 + 16*C1 + 4*C2 + C3 (exact) and 256*hi + lo, converts once
 //    and applies 2^-E, the group scale, c0*sum(x) and the optional zero point.
 //
-// Work split: persistent CTAs walk 16-row tiles; warp w of every CTA owns the same
-// contiguous K slice (its chunks of 4 blocks) for every tile, so it quantises only its
-// own slice of the activation table, once.  Each warp streams its (tile, chunk) items
-// through a 4-deep register ring of code words and scales, folds its share of the fp16
-// outlier anchors into its partial sums, and the eight K-partials of a tile meet in a
-// double-buffered shared array behind one barrier per tile.
+// Work split: a thread-block cluster of S CTAs covers one group of row tiles; CTA s of
+// the cluster owns K slice s, so it quantises only that slice of the activation table.
+// Each warp owns whole 16-row tiles inside its CTA's slice and streams its (tile, chunk)
+// items through a 4-deep register ring of code words and scales -- no CTA barrier in the
+// main loop.  The S K-partials of every row meet once, over distributed shared memory,
+// where the fused epilogue adds the fp16 outlier anchors (dot products computed in the
+// prologue while the weights are in flight), bias and residual, clamps and stores fp16.
 //
 // Reference behaviour replaced: otf_llm/otf_triton_2bit_kernel.py:164-194 (dispatch,
 // mask multiply, LUT path), :23-113 (warp GEMV), otf_llm/symmetric_2bit_engine.py:
 // 214-235 (bias, outlier anchors, clamp), otf_llm/otf_2bit_quantizer.py:193-221.
+#include <cuda.h>
+
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "otf_common.cuh"
 
 namespace otf {
 
-constexpr int kWarps = 8;      // warps per CTA (one K slice each)
-constexpr int kRows = 16;      // rows per tile (the m16 of the MMA)
-constexpr int kRing = 4;       // (tile, chunk) items in flight per warp
-constexpr int kOutPerLane = 8; // prefetched anchor values per lane and row
+constexpr int kCWarps = 8;                  // warps per CTA (each pipelines its own code stages)
+constexpr int kThreads = kCWarps * 32;
+constexpr int kCThreads = kCWarps * 32;
+constexpr int kRows = 16;                   // rows per tile (the m16 of the MMA)
+constexpr int kSlots = 6;                   // TMA stages in flight per warp
+constexpr int kMaxCluster = 8;              // K slices per cluster
+
+__device__ int g_otf_device_error;          // set when a bounded wait gives up
 
 struct LinearArgs {
   const uint16_t* x;
@@ -58,274 +68,359 @@ struct LinearArgs {
   int M, N, K, G;
   float c0, c1, c2, c3;
   int clamp;
+  int tiles_per_group;  // row tiles per cluster
 };
 
-__host__ __device__ inline int64_t gemv_smem_bytes(int W, int K, int n_out) {
-  const int SL = 32 * W + 8, SB = 2 * SL, nblk = K / (16 * W);
-  int64_t off = align_up((int64_t)nblk * SB, 16);
-  off += align_up((int64_t)K * 2, 16);     // staged activation x * mask (fp16)
-  off += 3 * (int64_t)nblk * 4;            // F, T, S per block
-  off += align_up(n_out, 4) * 4;           // anchor activations
-  off += 2 * kWarps * kRows * 4;           // double-buffered K partials
-  off = align_up(off, 16) + SL;            // zero block
-  return align_up(off, 16);
+// One CTA's shared memory: per-consumer-warp pipeline stages (codes via TMA) and their
+// mbarriers, the CTA's slice of the activation
+// table, the staged activation slice, per-block constants, the anchor activations,
+// the anchor weights of the rows this CTA finishes and the K-partials pushed to it.
+struct GemvSmem {
+  int64_t stages, bars, tbl, xs, meta, xo, afin, fin, zblk, total;
+  int stage_bytes;
+};
+
+__host__ __device__ inline GemvSmem gemv_smem_layout(int W, int K, int S, int n_out, int tiles_per_group) {
+  const int SL = 32 * W + 16, SB = 2 * SL, nblk = K / (16 * W), nch = (nblk + 3) / 4;
+  const int ch_slice = (nch + S - 1) / S, blk_slice = 4 * ch_slice;
+  const int grows = tiles_per_group * kRows;
+  const int frows = (grows + S - 1) / S;
+  GemvSmem L;
+  L.stage_bytes = kRows * 16 * W;  // one chunk of codes for the 16 rows of a tile
+  int64_t off = 0;
+  L.stages = off; off = align_up(off + (int64_t)kCWarps * kSlots * L.stage_bytes, 128);
+  L.bars = off;   off = align_up(off + kCWarps * kSlots * 8, 16);
+  L.tbl = off;    off = align_up(off + (int64_t)blk_slice * SB, 16);
+  L.xs = off;     off = align_up(off + (int64_t)blk_slice * 16 * W * 2, 16);
+  L.meta = off;   off = align_up(off + 3 * (int64_t)blk_slice * 4, 16);
+  L.xo = off;     off = align_up(off + (int64_t)n_out * 4, 16);
+  L.afin = off;   off = align_up(off + (int64_t)frows * 4, 16);  // anchor dot product per finished row
+  L.fin = off;    off = align_up(off + (int64_t)S * frows * 4, 16);
+  L.zblk = off;   off = align_up(off + SL, 16);
+  L.total = off;
+  return L;
 }
 
-template <int W>
-struct Item {
-  uint32_t wg[W], wg8[W];  // code words of rows g and g+8
-  uint32_t s;              // scales of rows g (lo) and g+8 (hi), fp16 bits
-  uint32_t z;              // zero points, same packing
-};
+// 2^e as a float for -126 <= e <= 127 (exact).
+__device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
+
+// Round-to-nearest-even of |v| < 2^22 via the 1.5*2^23 magic constant.
+__device__ __forceinline__ int rint_small(float v) { return __float_as_int(v + 12582912.0f) - 0x4B400000; }
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  const uint32_t p01 = __byte_perm((uint32_t)a, (uint32_t)b, 0x0040);
+  const uint32_t p23 = __byte_perm((uint32_t)c, (uint32_t)d, 0x0040);
+  return __byte_perm(p01, p23, 0x5410);
+}
 
 __device__ __forceinline__ uint16_t ldg_u16(const uint16_t* p) { return __ldg(p); }
 
+__device__ __forceinline__ void report_wait_failure() { atomicExch(&g_otf_device_error, 1); }
+
 template <int W, bool ZEROS>
-__global__ void __launch_bounds__(kWarps * 32, 2) k_gemv2b(const LinearArgs a) {
-  constexpr int BLK = 16 * W, SL = 32 * W + 8, SB = 2 * SL;
-  constexpr int LPB = 8 * W;          // table lanes per block
-  constexpr int BPP = 32 / LPB;       // blocks per warp pass
-  extern __shared__ __align__(16) uint8_t smem[];
+__global__ void __launch_bounds__(kThreads, 2) k_gemv2b(const LinearArgs a, const __grid_constant__ CUtensorMap tm) {
+  constexpr int BLK = 16 * W, SL = 32 * W + 16, SB = 2 * SL;
+  constexpr int CB = 16 * W;                       // code bytes per row per chunk
+  extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.K, N = a.N;
   const int nblk = K / BLK, nch = ceil_div(nblk, 4);
-  uint8_t* tbl = smem;
-  __half* xs = reinterpret_cast<__half*>(smem + align_up((int64_t)nblk * SB, 16));
-  float* sF = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + align_up((int64_t)K * 2, 16));
-  float* sT = sF + nblk;
-  float* sS = sT + nblk;
-  float* xo = sS + nblk;
-  float* red = xo + align_up(a.n_out, 4);
-  uint8_t* zblk = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(red + 2 * kWarps * kRows), 16));
+  uint32_t cs;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
+  const int S = (int)cs;
+  const int rank = (int)cluster_ctarank();
+  const int group = (int)blockIdx.x / S;
+  const int ch_slice = ceil_div(nch, S);
+  const int cbeg = min(rank * ch_slice, nch), cend = min(cbeg + ch_slice, nch);
+  const int blk0 = 4 * cbeg, blk1 = min(4 * cend, nblk);
+  const int kbeg = blk0 * BLK;
+  const int nbs = blk1 - blk0;
+  const int mych = cend - cbeg;
+  const int nbs_pad = 4 * mych;
+  const GemvSmem L = gemv_smem_layout(W, K, S, a.n_out, a.tiles_per_group);
+  const uint32_t stages_s = smem_u32(smem + L.stages);
+  const uint32_t bars_s = smem_u32(smem + L.bars);
+  uint8_t* tbl = smem + L.tbl;
+  __half* xs = reinterpret_cast<__half*>(smem + L.xs);
+  float* sF = reinterpret_cast<float*>(smem + L.meta);
+  float* sT = sF + 4 * ch_slice;
+  float* sS = sT + 4 * ch_slice;
+  float* xo = reinterpret_cast<float*>(smem + L.xo);
+  float* afin_sum = reinterpret_cast<float*>(smem + L.afin);
+  float* fin = reinterpret_cast<float*>(smem + L.fin);
+  uint8_t* zblk = smem + L.zblk;
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int cb = warp * nch / kWarps, ce = (warp + 1) * nch / kWarps;  // my chunks [cb, ce)
-  const int mych = ce - cb, ipt = mych > 0 ? mych : 1;                 // items per tile
-  const int ob = warp * a.n_out / kWarps, oe = (warp + 1) * a.n_out / kWarps;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ntiles = ceil_div(N, kRows);
-  const int my_tiles = (int)blockIdx.x < ntiles ? ceil_div(ntiles - (int)blockIdx.x, (int)gridDim.x) : 0;
-  const int nitems = my_tiles * ipt;
-  const int grp_div = a.G / BLK;
+  const int tile0 = group * a.tiles_per_group;
+  const int gtiles = max(0, min(a.tiles_per_group, ntiles - tile0));
+  const int grows = gtiles * kRows;
+  const int fin_rows = ceil_div(a.tiles_per_group * kRows, S);
+  const int gshift = __ffs(a.G / BLK) - 1;  // G / BLK is a power of two
+  auto full_bar = [&](int w, int slot) { return bars_s + (uint32_t)((w * kSlots + slot) * 8); };
+  auto stage_addr = [&](int w, int slot) { return stages_s + (uint32_t)((w * kSlots + slot) * L.stage_bytes); };
+  auto tiles_of = [&](int w) { return w < gtiles ? ceil_div(gtiles - w, kCWarps) : 0; };
 
-  auto load_item = [&](Item<W>& r, int it) {
-    bool ok = it < nitems;
-    int tile = 0, c = 0;
-    if (ok) {
-      const int ci = it % ipt;
-      tile = (int)blockIdx.x + (it / ipt) * (int)gridDim.x;
-      c = cb + ci;
-      ok = ci < mych;
-    }
-    const int blk = 4 * c + t;
-    ok = ok && blk < nblk;
-    const int rg = tile * kRows + g, rg8 = rg + 8;
-    const bool og = ok && rg < N, og8 = ok && rg8 < N;
-    const uint8_t* pg = a.packed + (int64_t)(og ? rg : 0) * a.ldp + (int64_t)blk * (BLK / 4);
-    const uint8_t* pg8 = a.packed + (int64_t)(og8 ? rg8 : 0) * a.ldp + (int64_t)blk * (BLK / 4);
-    if constexpr (W == 4) {
-      const uint4 v = og ? ld_stream16(pg) : make_uint4(0, 0, 0, 0);
-      const uint4 v8 = og8 ? ld_stream16(pg8) : make_uint4(0, 0, 0, 0);
-      r.wg[0] = v.x; r.wg[1] = v.y; r.wg[2] = v.z; r.wg[3] = v.w;
-      r.wg8[0] = v8.x; r.wg8[1] = v8.y; r.wg8[2] = v8.z; r.wg8[3] = v8.w;
-    } else {
-      const uint2 v = og ? ld_stream8(pg) : make_uint2(0, 0);
-      const uint2 v8 = og8 ? ld_stream8(pg8) : make_uint2(0, 0);
-      r.wg[0] = v.x; r.wg[1] = v.y;
-      r.wg8[0] = v8.x; r.wg8[1] = v8.y;
-    }
-    const int grp = blk / grp_div;
-    const uint32_t s0 = og ? ldg_u16(a.scales + (int64_t)rg * a.lds + grp) : 0u;
-    const uint32_t s1 = og8 ? ldg_u16(a.scales + (int64_t)rg8 * a.lds + grp) : 0u;
-    r.s = s0 | (s1 << 16);
-    if constexpr (ZEROS) {
-      const uint32_t z0 = og ? ldg_u16(a.zeros + (int64_t)rg * a.ldz + grp) : 0u;
-      const uint32_t z1 = og8 ? ldg_u16(a.zeros + (int64_t)rg8 * a.ldz + grp) : 0u;
-      r.z = z0 | (z1 << 16);
-    } else {
-      r.z = 0u;
+  if (tid == 0) {
+    for (int i = 0; i < kCWarps * kSlots; ++i) mbar_init(bars_s + i * 8, 1);  // expect_tx arrive (+ TMA bytes)
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  // Stage k of warp w = (tile w + 8*(k / mych), chunk k % mych of my slice).  Lane 0 of
+  // the warp issues its TMA into slot k % kSlots and refills the slot once consumed; the
+  // issue cursor (slot, chunk, tile row) advances without divisions.
+  const int my_tiles = tiles_of(warp);
+  const int nst = my_tiles * mych;
+  int is_slot = 0, is_cc = 0, is_row = (tile0 + warp) * kRows;
+  auto issue_next = [&]() {
+    const uint32_t fb = full_bar(warp, is_slot);
+    mbar_arrive_expect_tx(fb, kRows * CB);
+    tma_load_2d(stage_addr(warp, is_slot), &tm, (cbeg + is_cc) * CB, is_row, fb);
+    if (++is_slot == kSlots) is_slot = 0;
+    if (++is_cc == mych) {
+      is_cc = 0;
+      is_row += kCWarps * kRows;
     }
   };
-
-  // 1. Put the first kRing items of weights in flight before anything else.
-  Item<W> ring[kRing];
-#pragma unroll
-  for (int s = 0; s < kRing; ++s) load_item(ring[s], s);
-
-  // 2. Anchor activations (index load, then value load) go in flight next.
-  float xo_reg = 0.0f;
-  if ((int)threadIdx.x < a.n_out) xo_reg = h2f(ldg_u16(a.x + __ldg(a.oidx + threadIdx.x)));
-
-  // 3. Stage x * mask (fp16, as the reference multiplies) into shared memory: one
-  //    batch of independent 16-byte loads per thread, so the latency is paid once.
-  for (int v = threadIdx.x; v < K / 8; v += blockDim.x) {
-    uint4 xv = __ldg(reinterpret_cast<const uint4*>(a.x) + v);
-    if (a.mask) {
-      const uint4 mv = __ldg(reinterpret_cast<const uint4*>(a.mask) + v);
-      __half2* xh = reinterpret_cast<__half2*>(&xv);
-      const __half2* mh = reinterpret_cast<const __half2*>(&mv);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) xh[i] = __hmul2(xh[i], mh[i]);
-    }
-    reinterpret_cast<uint4*>(xs)[v] = xv;
-  }
-  __syncthreads();
-
-  // 4. Quantise this warp's slice of the activation table (blocks [4cb, 4ce)).
+  if (lane == 0)
+    for (int k = 0; k < min(kSlots, nst); ++k) issue_next();
   {
-    const float bl = a.c1 - a.c0, bh = 0.5f * (a.c2 - a.c0);
-    const float cmax = fmaxf(fabsf(bl), fabsf(bh));
-    const int sub = lane / LPB, l = lane % LPB;
-    const int limb = l / (4 * W), wq = (l % (4 * W)) / 4, j = l & 3;
-    const int b_end = min(4 * ce, nblk);
-    for (int b0 = 4 * cb; b0 < b_end; b0 += BPP) {
-      const int b = b0 + sub;
-      const bool on = b < b_end;
-      float xv[4];
-      float mx = 0.0f, sx = 0.0f;
+    // Epilogue inputs of the rows this CTA finishes (rank + S*i of the group).
+    const int fr = rank + S * tid;
+    const int frow = tile0 * kRows + fr;
+    const bool fin_ok = fr < grows && frow < N;
+    float ep = 0.0f;
+    if (fin_ok) {
+      if (a.bias) ep += h2f(ldg_u16(a.bias + frow));
+      if (a.res) ep += h2f(ldg_u16(a.res + frow));
+    }
+    for (int j = tid; j < a.n_out; j += kCThreads) xo[j] = h2f(ldg_u16(a.x + __ldg(a.oidx + j)));
+    // Stage my slice of x * mask (fp16, as the reference multiplies); padded tail = 0.
+    {
+      const uint4* xsrc = reinterpret_cast<const uint4*>(a.x + kbeg);
+      const uint4* msrc = a.mask ? reinterpret_cast<const uint4*>(a.mask + kbeg) : nullptr;
+      for (int v = tid; v < nbs_pad * BLK / 8; v += kCThreads) {
+        uint4 xv = make_uint4(0, 0, 0, 0);
+        if (v < nbs * BLK / 8) {
+          xv = __ldg(xsrc + v);
+          if (msrc) {
+            const uint4 mv = __ldg(msrc + v);
+            __half2* xh = reinterpret_cast<__half2*>(&xv);
+            const __half2* mh = reinterpret_cast<const __half2*>(&mv);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float v = on ? __half2float(xs[b * BLK + 16 * wq + 4 * i + j]) : 0.0f;
-        xv[i] = v;
-        mx = fmaxf(mx, fabsf(v));
-        sx += (limb == 0) ? v : 0.0f;
+            for (int i = 0; i < 4; ++i) xh[i] = __hmul2(xh[i], mh[i]);
+          }
+        }
+        reinterpret_cast<uint4*>(xs)[v] = xv;
       }
+    }
+    for (int i = tid; i < SL / 4; i += kCThreads) reinterpret_cast<uint32_t*>(zblk)[i] = 0u;
+    named_barrier_sync(1, kCThreads);
+    // Anchor dot products of the rows this CTA finishes: warp w takes finished-row slots
+    // i = w, w+8, ...; lanes stride over the anchors of the row (contiguous fp16), a
+    // shuffle reduction sums them, and the owning thread's epilogue term receives it.
+    {
+      const int nfin = ceil_div(grows - rank, S);  // finished rows of this CTA
+      for (int i = warp; i < nfin; i += kCWarps) {
+        const int row = tile0 * kRows + rank + S * i;
+        float d = 0.0f;
+        if (row < N) {
+          const uint16_t* ov = a.ovals + (int64_t)row * a.ldo;
+          for (int j = lane; j < a.n_out; j += 32) d = fmaf(xo[j], h2f(ldg_u16(ov + j)), d);
+        }
 #pragma unroll
-      for (int o = LPB / 2; o > 0; o >>= 1) {
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        sx += __shfl_xor_sync(0xffffffffu, sx, o);
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == 0) afin_sum[i] = d;
       }
-      const int E = fixed_point_exp(mx * cmax);
-      const float sc = ldexpf(1.0f, E);
-      uint32_t wl = 0, wh = 0;
+    }
+    // Quantise the table slice: 4W lanes per block, lane (w, j) owns codes 16w+4i+j.
+    {
+      constexpr int LPB = 4 * W;
+      constexpr int BPP = 32 / LPB;
+      const float bl = a.c1 - a.c0, bh = 0.5f * (a.c2 - a.c0);
+      const float cmax = fmaxf(fabsf(bl), fabsf(bh));
+      const int sub = lane / LPB, l = lane % LPB;
+      const int wq = l >> 2, j = l & 3;
+      for (int b0 = 0; b0 < nbs_pad; b0 += BPP * kCWarps) {
+        const int bi = b0 + warp * BPP + sub;
+        const bool on = bi < nbs_pad;
+        float xv[4];
+        float mx = 0.0f, sx = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        int hi, lo;
-        split_limbs(__float2int_rn(__fmul_rn(__fmul_rn(xv[i], bl), sc)), hi, lo);
-        wl |= (uint32_t)((limb == 0 ? hi : lo) & 0xff) << (8 * i);
-        split_limbs(__float2int_rn(__fmul_rn(__fmul_rn(xv[i], bh), sc)), hi, lo);
-        wh |= (uint32_t)((limb == 0 ? hi : lo) & 0xff) << (8 * i);
-      }
-      if (on) {
-        *reinterpret_cast<uint2*>(tbl + b * SB + limb * SL + (wq * 4 + j) * 8) = make_uint2(wl, wh);
-        if (l == 0) {
-          sF[b] = ldexpf(1.0f, -E) * (1.0f / 64.0f);
-          sT[b] = a.c0 * sx;
-          sS[b] = sx;
+        for (int i = 0; i < 4; ++i) {
+          const float v = on ? __half2float(xs[bi * BLK + 16 * wq + 4 * i + j]) : 0.0f;
+          xv[i] = v;
+          mx = fmaxf(mx, fabsf(v));
+          sx += v;
+        }
+#pragma unroll
+        for (int o = LPB / 2; o > 0; o >>= 1) {
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          sx += __shfl_xor_sync(0xffffffffu, sx, o);
+        }
+        const int E = fixed_point_exp(mx * cmax);
+        const float sc = exp2i(E);
+        const float kl = bl * sc, kh = bh * sc;
+        int hl[4], ll[4], hh[4], lh[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          split_limbs(rint_small(xv[i] * kl), hl[i], ll[i]);
+          split_limbs(rint_small(xv[i] * kh), hh[i], lh[i]);
+        }
+        if (on) {
+          uint8_t* e = tbl + bi * SB + (wq * 4 + j) * 8;
+          *reinterpret_cast<uint2*>(e) =
+              make_uint2(pack4(hl[0], hl[1], hl[2], hl[3]), pack4(hh[0], hh[1], hh[2], hh[3]));
+          *reinterpret_cast<uint2*>(e + SL) =
+              make_uint2(pack4(ll[0], ll[1], ll[2], ll[3]), pack4(lh[0], lh[1], lh[2], lh[3]));
+          if (l == 0) {
+            sF[bi] = exp2i(-E) * (1.0f / 64.0f);
+            sT[bi] = a.c0 * sx;
+            sS[bi] = sx;
+          }
         }
       }
     }
-  }
-  if ((int)threadIdx.x < a.n_out) xo[threadIdx.x] = xo_reg;
-  for (int i = (int)blockDim.x + threadIdx.x; i < a.n_out; i += blockDim.x) xo[i] = h2f(a.x[a.oidx[i]]);
-  for (int i = threadIdx.x; i < SL / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(zblk)[i] = 0u;
-  __syncthreads();
+    named_barrier_sync(1, kCThreads);
 
-  // 5. Stream items.  Per tile: chunks -> partials p0/p1 (rows g, g+8), anchors, flush.
-  float p0 = 0.0f, p1 = 0.0f;
-  float av0[kOutPerLane], av1[kOutPerLane];
-  float ep = 0.0f;  // bias + residual of this lane's epilogue row (warps 0-1, lanes 0-7)
+    // Main loop: my tiles tl = warp + 8*i, their chunks in order, one stage each.  The
+    // scales (and zero points) of stage k + kSlots are fetched into a register ring while
+    // stage k is consumed.
+    const int g = lane >> 2, t = lane & 3;
+    const bool breal = (g >> 1) == t;
+    const uint8_t* bbase = breal ? (tbl + (g >> 1) * SB + (g & 1) * SL) : zblk;
+    const int bstep = breal ? 4 * SB : 0;
+    // Parameter cursor: per-tile row pointers, per-stage group index.
+    int lt = 0, lc = 0;
+    const uint16_t* sp0 = nullptr;
+    const uint16_t* sp1 = nullptr;
+    const uint16_t* zp0 = nullptr;
+    const uint16_t* zp1 = nullptr;
+    bool pv0 = false, pv1 = false;
+    auto param_tile = [&]() {
+      const int rg = (tile0 + warp + kCWarps * lt) * kRows + g;
+      pv0 = lt < my_tiles && rg < N;
+      pv1 = lt < my_tiles && rg + 8 < N;
+      sp0 = a.scales + (pv0 ? (int64_t)rg * a.lds : 0);
+      sp1 = a.scales + (pv1 ? (int64_t)(rg + 8) * a.lds : 0);
+      if constexpr (ZEROS) {
+        zp0 = a.zeros + (pv0 ? (int64_t)rg * a.ldz : 0);
+        zp1 = a.zeros + (pv1 ? (int64_t)(rg + 8) * a.ldz : 0);
+      }
+    };
+    auto load_params = [&](uint32_t& s0, uint32_t& s1, uint32_t& z0, uint32_t& z1) {
+      const int blk = 4 * (cbeg + lc) + t;
+      const bool inb = blk < nblk;
+      const int grp = inb ? (blk >> gshift) : 0;
+      s0 = s1 = 0u;
+      ld_u16_pred(s0, sp0 + grp, pv0 && inb);
+      ld_u16_pred(s1, sp1 + grp, pv1 && inb);
+      z0 = z1 = 0u;
+      if constexpr (ZEROS) {
+        ld_u16_pred(z0, zp0 + grp, pv0 && inb);
+        ld_u16_pred(z1, zp1 + grp, pv1 && inb);
+      }
+      if (++lc == mych) {
+        lc = 0;
+        ++lt;
+        param_tile();
+      }
+    };
+    param_tile();
+    uint32_t rs0[kSlots], rs1[kSlots], rz0[kSlots], rz1[kSlots];
 #pragma unroll
-  for (int i = 0; i < kOutPerLane; ++i) av0[i] = av1[i] = 0.0f;
+    for (int s = 0; s < kSlots; ++s) load_params(rs0[s], rs1[s], rz0[s], rz1[s]);
+    float p0 = 0.0f, p1 = 0.0f;
+    int cc = 0, ct = 0;
+    for (int base = 0; base < nst; base += kSlots) {
+#pragma unroll
+      for (int s = 0; s < kSlots; ++s) {
+        const int k = base + s;
+        if (k < nst) {
+          if (!mbar_wait(full_bar(warp, s), (uint32_t)(base / kSlots) & 1u)) report_wait_failure();
+          const uint8_t* st = smem + L.stages + (warp * kSlots + s) * L.stage_bytes;
+          uint32_t cw[W], cw8[W];
+          if constexpr (W == 4) {
+            const uint4 v = *reinterpret_cast<const uint4*>(st + g * CB + t * 16);
+            const uint4 v8 = *reinterpret_cast<const uint4*>(st + (g + 8) * CB + t * 16);
+            cw[0] = v.x; cw[1] = v.y; cw[2] = v.z; cw[3] = v.w;
+            cw8[0] = v8.x; cw8[1] = v8.y; cw8[2] = v8.z; cw8[3] = v8.w;
+          } else {
+            const uint2 v = *reinterpret_cast<const uint2*>(st + g * CB + t * 8);
+            const uint2 v8 = *reinterpret_cast<const uint2*>(st + (g + 8) * CB + t * 8);
+            cw[0] = v.x; cw[1] = v.y;
+            cw8[0] = v8.x; cw8[1] = v8.y;
+          }
+          const float sg = h2f((uint16_t)rs0[s]), sg8 = h2f((uint16_t)rs1[s]);
+          const float zg = h2f((uint16_t)rz0[s]), zg8 = h2f((uint16_t)rz1[s]);
+          load_params(rs0[s], rs1[s], rz0[s], rz1[s]);
 
-  for (int base = 0; base < nitems; base += kRing) {
-#pragma unroll
-    for (int s = 0; s < kRing; ++s) {
-      const int it = base + s;
-      if (it < nitems) {
-        const int ci = it % ipt, tl = it / ipt;
-        const int tile = (int)blockIdx.x + tl * (int)gridDim.x;
-        const int rg = tile * kRows + g, rg8 = rg + 8;
-        if (ci == 0) {
-          // Anchor values of this tile for this warp's anchor columns, and the epilogue terms.
-#pragma unroll
-          for (int i = 0; i < kOutPerLane; ++i) {
-            const int jo = ob + t + 4 * i;
-            av0[i] = (jo < oe && rg < N) ? h2f(ldg_u16(a.ovals + (int64_t)rg * a.ldo + jo)) : 0.0f;
-            av1[i] = (jo < oe && rg8 < N) ? h2f(ldg_u16(a.ovals + (int64_t)rg8 * a.ldo + jo)) : 0.0f;
-          }
-          if (warp < 2 && lane < 8) {
-            const int r = tile * kRows + warp * 8 + lane;
-            ep = 0.0f;
-            if (r < N) {
-              if (a.bias) ep += h2f(ldg_u16(a.bias + r));
-              if (a.res) ep += h2f(ldg_u16(a.res + r));
-            }
-          }
-        }
-        if (ci < mych) {
-          const int c = cb + ci;
-          const int blk = 4 * c + t;
-          const int bblk = 4 * c + (g >> 1);
-          const uint8_t* bp = ((g >> 1) == t && bblk < nblk) ? (tbl + bblk * SB + (g & 1) * SL) : zblk;
+          const uint8_t* bp = bbase + cc * bstep;
           int C[4][4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int f = 0; f < 4; ++f) C[j][f] = 0;
 #pragma unroll
           for (int w = 0; w < W; ++w) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint2 bb = *reinterpret_cast<const uint2*>(bp + (w * 4 + j) * 8);
-              const uint32_t ml = 0x01010101u << (2 * j), mh = 0x02020202u << (2 * j);
-              mma_u8s8(C[j], ring[s].wg[w] & ml, ring[s].wg8[w] & ml, ring[s].wg[w] & mh, ring[s].wg8[w] & mh,
-                       bb.x, bb.y);
+            for (int jp = 0; jp < 4; jp += 2) {
+              const uint4 bq = *reinterpret_cast<const uint4*>(bp + (w * 4 + jp) * 8);
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int j = jp + h;
+                const uint32_t b0 = h ? bq.z : bq.x, b1 = h ? bq.w : bq.y;
+                const uint32_t ml = 0x01010101u << (2 * j), mh = 0x02020202u << (2 * j);
+                if (w == 0)
+                  mma_u8s8_z(C[j], cw[w] & ml, cw8[w] & ml, cw[w] & mh, cw8[w] & mh, b0, b1);
+                else
+                  mma_u8s8(C[j], cw[w] & ml, cw8[w] & ml, cw[w] & mh, cw8[w] & mh, b0, b1);
+              }
             }
           }
-          if (blk < nblk) {
+          {
+            const int lb = 4 * cc + t;
             int v[4];
 #pragma unroll
-            for (int f = 0; f < 4; ++f) v[f] = 64 * C[0][f] + 16 * C[1][f] + 4 * C[2][f] + C[3][f];
-            const float F = sF[blk], T = sT[blk];
-            const float sg = h2f((uint16_t)(ring[s].s & 0xffffu)), sg8 = h2f((uint16_t)(ring[s].s >> 16));
-            p0 = fmaf(sg, fmaf((float)(256 * v[0] + v[1]), F, T), p0);
-            p1 = fmaf(sg8, fmaf((float)(256 * v[2] + v[3]), F, T), p1);
+            for (int f = 0; f < 4; ++f) v[f] = ((C[0][f] * 4 + C[1][f]) * 4 + C[2][f]) * 4 + C[3][f];
+            const float F = sF[lb], T = sT[lb];
+            p0 = fmaf(sg, fmaf((float)(v[0] * 256 + v[1]), F, T), p0);
+            p1 = fmaf(sg8, fmaf((float)(v[2] * 256 + v[3]), F, T), p1);
             if constexpr (ZEROS) {
-              const float S = sS[blk];
-              p0 = fmaf(h2f((uint16_t)(ring[s].z & 0xffffu)), S, p0);
-              p1 = fmaf(h2f((uint16_t)(ring[s].z >> 16)), S, p1);
+              const float Sx = sS[lb];
+              p0 = fmaf(zg, Sx, p0);
+              p1 = fmaf(zg8, Sx, p1);
             }
           }
-        }
-        load_item(ring[s], it + kRing);
-        if (ci == ipt - 1) {
-          // Tile flush: anchors, quad reduction, cross-warp exchange, epilogue.
-#pragma unroll
-          for (int i = 0; i < kOutPerLane; ++i) {
-            const int jo = ob + t + 4 * i;
-            if (jo < oe) {
-              p0 = fmaf(xo[jo], av0[i], p0);
-              p1 = fmaf(xo[jo], av1[i], p1);
+          // The slot's codes have been consumed by every lane (the MMAs above used them):
+          // refill it with stage k + kSlots.
+          __syncwarp();
+          if (lane == 0 && k + kSlots < nst) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_next();
+          }
+          if (++cc == mych) {
+            const int lrow = (warp + kCWarps * ct) * kRows + g;
+            p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
+            p0 += __shfl_xor_sync(0xffffffffu, p0, 2);
+            p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
+            p1 += __shfl_xor_sync(0xffffffffu, p1, 2);
+            if (t == 0) {
+              const uint32_t f0 = smem_u32(fin + rank * fin_rows + lrow / S);
+              const uint32_t f1 = smem_u32(fin + rank * fin_rows + (lrow + 8) / S);
+              st_cluster_f32_plain(mapa_shared(f0, (uint32_t)(lrow % S)), p0);
+              st_cluster_f32_plain(mapa_shared(f1, (uint32_t)((lrow + 8) % S)), p1);
             }
-          }
-          for (int jo = ob + t + 4 * kOutPerLane; jo < oe; jo += 4) {  // beyond the prefetched span
-            if (rg < N) p0 = fmaf(xo[jo], h2f(ldg_u16(a.ovals + (int64_t)rg * a.ldo + jo)), p0);
-            if (rg8 < N) p1 = fmaf(xo[jo], h2f(ldg_u16(a.ovals + (int64_t)rg8 * a.ldo + jo)), p1);
-          }
-          p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
-          p0 += __shfl_xor_sync(0xffffffffu, p0, 2);
-          p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
-          p1 += __shfl_xor_sync(0xffffffffu, p1, 2);
-          float* rb = red + (tl & 1) * (kWarps * kRows);
-          if (t == 0) {
-            rb[warp * kRows + g] = p0;
-            rb[warp * kRows + g + 8] = p1;
-          }
-          p0 = p1 = 0.0f;
-          __syncthreads();
-          if (warp < 2 && lane < 8) {
-            const int rl = warp * 8 + lane;
-            const int r = tile * kRows + rl;
-            if (r < N) {
-              float yv = ep;
-#pragma unroll
-              for (int w = 0; w < kWarps; ++w) yv += rb[w * kRows + rl];
-              if (a.clamp) yv = fminf(fmaxf(yv, -65504.0f), 65504.0f);
-              a.y[r] = f2h(yv);
-            }
+            p0 = p1 = 0.0f;
+            cc = 0;
+            ++ct;
           }
         }
       }
+    }
+    // One cluster barrier below: every partial has landed in its finisher's shared memory.
+    cluster_sync_all();
+    if (fin_ok) {
+      float yv = ep + (a.n_out > 0 ? afin_sum[tid] : 0.0f);
+      for (int q = 0; q < S; ++q) yv += fin[q * fin_rows + tid];
+      if (a.clamp) yv = fminf(fmaxf(yv, -65504.0f), 65504.0f);
+      a.y[frow] = f2h(yv);
     }
   }
 }
@@ -421,9 +516,96 @@ static int num_sms() {
   return n;
 }
 
+// Largest number of co-resident clusters of S CTAs for a given dynamic shared memory
+// size (cached: the occupancy query is a host call we do not want per launch).
 template <int W, bool ZEROS>
-static int launch_gemv(const LinearArgs& a, cudaStream_t st) {
-  const int64_t smem = gemv_smem_bytes(W, a.K, a.n_out);
+static int max_active_clusters(int S, int64_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int64_t>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int64_t bucket = align_up(smem, 4096);
+  const auto key = std::make_tuple(dev, S, bucket);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)S, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)bucket;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int mc = 0;
+  if (cudaOccupancyMaxActiveClusters(&mc, k_gemv2b<W, ZEROS>, &cfg) != cudaSuccess || mc <= 0)
+    mc = std::max(1, num_sms() / S);
+  cudaGetLastError();
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = mc;
+  return mc;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// Tensor map of a packed code matrix: uint8 [rows, cols] with row stride ld bytes, box
+// [box_cols bytes, 16 rows], no swizzle (the 64/32-byte row pitch of a box is already
+// conflict-free for the consumers' 16/8-byte reads), zero fill out of bounds.
+static bool code_tensor_map(CUtensorMap* out, const uint8_t* base, int64_t rows, int64_t cols, int64_t ld,
+                            int box_cols) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int64_t, int64_t, int64_t, int>, CUtensorMap> cache;
+  const auto key = std::make_tuple((const void*)base, rows, cols, ld, box_cols);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return false;
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)kRows};
+  const cuuint32_t estr[2] = {1, 1};
+  if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() > 65536) cache.clear();
+  cache[key] = m;
+  *out = m;
+  return true;
+}
+
+template <int W, bool ZEROS>
+static int launch_gemv(LinearArgs a, cudaStream_t st) {
   static thread_local int configured_dev[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -432,11 +614,46 @@ static int launch_gemv(const LinearArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return set_cuda_error(e);
     configured_dev[dev] = 1;
   }
+  CUtensorMap tm;
+  if (!code_tensor_map(&tm, a.packed, a.N, a.K / 4, a.ldp, 16 * W)) return OTF_ERR_UNSUPPORTED;
+  const int nblk = a.K / (16 * W), nch = ceil_div(nblk, 4);
   const int ntiles = ceil_div(a.N, kRows);
-  const int per_sm = smem <= 100 * 1024 ? 2 : 1;
-  const int ctas = std::max(1, std::min(ntiles, per_sm * num_sms()));
-  k_gemv2b<W, ZEROS><<<ctas, kWarps * 32, smem, st>>>(a);
-  return set_cuda_error(cudaGetLastError());
+  // K slices: at least two chunks per slice, at most kMaxCluster slices, none empty.
+  int S = std::max(1, std::min(kMaxCluster, nch / 2));
+  while (S > 1 && ceil_div(nch, S) * (S - 1) >= nch) --S;
+  // Row groups: no more clusters than can be resident at once (a second wave of
+  // clusters would double the time), every consumer warp holding at least one tile, and
+  // each of the S*256 consumer threads of a cluster finishing at most one row.
+  const int min_groups = std::max(1, ceil_div(ntiles * kRows, S * kCThreads));
+  int groups = std::max(1, ceil_div(ntiles, kCWarps));
+  for (int pass = 0; pass < 3; ++pass) {
+    const int tpg = ceil_div(ntiles, std::max(groups, min_groups));
+    const int64_t smem = gemv_smem_layout(W, a.K, S, a.n_out, tpg).total;
+    if (smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
+    const int mc = max_active_clusters<W, ZEROS>(S, smem);
+    const int want = std::max(min_groups, std::min(mc, ceil_div(ntiles, kCWarps)));
+    if (want == groups) break;
+    groups = want;
+  }
+  groups = std::max(groups, min_groups);
+  a.tiles_per_group = ceil_div(ntiles, groups);
+  groups = ceil_div(ntiles, a.tiles_per_group);
+  if (a.tiles_per_group * kRows > S * kCThreads) return OTF_ERR_UNSUPPORTED;
+  const int64_t smem = gemv_smem_layout(W, a.K, S, a.n_out, a.tiles_per_group).total;
+  if (smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(groups * S), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return set_cuda_error(cudaLaunchKernelEx(&cfg, k_gemv2b<W, ZEROS>, a, tm));
 }
 
 static int launch_generic(const LinearArgs& a, cudaStream_t st) {
@@ -508,14 +725,16 @@ extern "C" OTF_API int otf2b_linear(const void* x, int64_t ldx, const uint8_t* p
   const float lhs = a.c3 - a.c2, rhs = a.c1 - a.c0;
   const bool affine = fabsf(lhs - rhs) <= 1e-6f * fmaxf(1.0f, fabsf(rhs));
   const uintptr_t pa = reinterpret_cast<uintptr_t>(packed);
-  const bool x_al = reinterpret_cast<uintptr_t>(x) % 16 == 0 && (!mask || reinterpret_cast<uintptr_t>(mask) % 16 == 0);
+  const bool x_al = reinterpret_cast<uintptr_t>(x) % 16 == 0 && (!mask || reinterpret_cast<uintptr_t>(mask) % 16 == 0) &&
+                    reinterpret_cast<uintptr_t>(scales) % 4 == 0 && (!zeros || reinterpret_cast<uintptr_t>(zeros) % 4 == 0);
   const bool fast_ok = !(flags & OTF_FLAG_FORCE_GENERIC) && affine && M == 1 && x_al && K % 8 == 0;
-  if (fast_ok && group_size % 64 == 0 && pa % 16 == 0 && ld_packed % 16 == 0 &&
-      gemv_smem_bytes(4, a.K, a.n_out) <= 227 * 1024)
-    return zeros ? launch_gemv<4, true>(a, s) : launch_gemv<4, false>(a, s);
-  if (fast_ok && group_size % 32 == 0 && pa % 8 == 0 && ld_packed % 8 == 0 &&
-      gemv_smem_bytes(2, a.K, a.n_out) <= 227 * 1024)
-    return zeros ? launch_gemv<2, true>(a, s) : launch_gemv<2, false>(a, s);
+  const auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
+  int rc = OTF_ERR_UNSUPPORTED;
+  if (fast_ok && group_size % 64 == 0 && pow2(group_size / 64) && pa % 16 == 0 && ld_packed % 16 == 0)
+    rc = zeros ? launch_gemv<4, true>(a, s) : launch_gemv<4, false>(a, s);
+  else if (fast_ok && group_size % 32 == 0 && pow2(group_size / 32) && pa % 8 == 0 && ld_packed % 8 == 0)
+    rc = zeros ? launch_gemv<2, true>(a, s) : launch_gemv<2, false>(a, s);
+  if (rc != OTF_ERR_UNSUPPORTED) return rc;
   return launch_generic(a, s);
 }
 
@@ -530,4 +749,14 @@ extern "C" OTF_API int otf2b_unpack_codes(const uint8_t* packed, int64_t ld_pack
   k_unpack_codes<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(packed, ld_packed, (int)N, (int)K, codes,
                                                                        ld_codes);
   return set_cuda_error(cudaGetLastError());
+}
+
+extern "C" OTF_API int otf_device_error(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, otf::g_otf_device_error, sizeof(int)) != cudaSuccess) { set_cuda_error(cudaGetLastError()); return -1; }
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(otf::g_otf_device_error, &z, sizeof(int));
+  }
+  return v;
 }

@@ -83,21 +83,21 @@ __global__ void __launch_bounds__(kHeadWarps * 32) k_i8_head_imma(const HeadArgs
     const int8_t* pg = a.w + (int64_t)(vg ? rg : 0) * a.ldw;
     const int8_t* pg8 = a.w + (int64_t)(vg8 ? rg8 : 0) * a.ldw;
     float acc0 = 0.0f, acc1 = 0.0f;
-    uint4 cw, cw8;
+    uint4 cw = make_uint4(0, 0, 0, 0), cw8 = make_uint4(0, 0, 0, 0);
     {
       const bool act = t < nb;
-      cw = (act && vg) ? ld_stream16(pg + 16 * t) : make_uint4(0, 0, 0, 0);
-      cw8 = (act && vg8) ? ld_stream16(pg8 + 16 * t) : make_uint4(0, 0, 0, 0);
+      ld_stream16_pred(cw, pg + 16 * t, act && vg);
+      ld_stream16_pred(cw8, pg8 + 16 * t, act && vg8);
     }
     for (int c = 0; c < nch; ++c) {
       const int blk = 4 * c + t;
       const bool act = blk < nb;
-      uint4 nw, nw8;
+      uint4 nw = make_uint4(0, 0, 0, 0), nw8 = make_uint4(0, 0, 0, 0);
       {
         const int blk2 = blk + 4;
         const bool act2 = blk2 < nb;
-        nw = (act2 && vg) ? ld_stream16(pg + 16 * (int64_t)blk2) : make_uint4(0, 0, 0, 0);
-        nw8 = (act2 && vg8) ? ld_stream16(pg8 + 16 * (int64_t)blk2) : make_uint4(0, 0, 0, 0);
+        ld_stream16_pred(nw, pg + 16 * (int64_t)blk2, act2 && vg);
+        ld_stream16_pred(nw8, pg8 + 16 * (int64_t)blk2, act2 && vg8);
       }
       const int bblk = 4 * c + (g >> 1);
       const uint8_t* bp = ((g >> 1) == t && bblk < nb) ? (tbl + bblk * kHeadSB + (g & 1) * kHeadSL) : zblk;

@@ -28,6 +28,17 @@ __device__ __forceinline__ void mma_s8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Same MMA with a zero accumulator input (starts a fresh sum without zeroing registers).
+__device__ __forceinline__ void mma_u8s8_z(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void st_cluster_f32_plain(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
 // Streaming 16/8-byte loads of weights: read once, do not keep them in L1.
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   uint4 v;
@@ -39,6 +50,88 @@ __device__ __forceinline__ uint2 ld_stream8(const void* p) {
   uint2 v;
   asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
   return v;
+}
+
+// Predicated streaming loads into registers the caller zero-initialised: when the
+// predicate is false the registers keep their zeros, and no instruction consumes the
+// loaded value before its first real use (a select on a pending load would stall).
+__device__ __forceinline__ void ld_stream16_pred(uint4& v, const void* p, bool pred) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+      "@q ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n\t}"
+      : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w) : "l"(p), "r"((int)pred));
+}
+__device__ __forceinline__ void ld_stream8_pred(uint2& v, const void* p, bool pred) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t"
+      "@q ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n\t}"
+      : "+r"(v.x), "+r"(v.y) : "l"(p), "r"((int)pred));
+}
+// 16-bit load (zero-extended into a 32-bit register), predicated the same way.
+__device__ __forceinline__ void ld_u16_pred(uint32_t& v, const void* p, bool pred) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t"
+      "@q ld.global.nc.u16 %0, [%1];\n\t}"
+      : "+r"(v) : "l"(p), "r"((int)pred));
+}
+
+// mbarrier + TMA (bulk tensor copy) helpers.  Every wait is bounded: after
+// kWaitLimit polls the waiter gives up, records the failure in g_otf_device_error
+// and carries on, so a broken pipeline can never hang the GPU.
+constexpr uint32_t kWaitLimit = 1u << 20;  // try_wait rounds of at most ~1 us each: about 1 s
+__device__ __forceinline__ void mbar_init(uint32_t addr, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(addr), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t addr) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t addr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(addr), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test_wait(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+  return ok != 0;
+}
+// try_wait with a 1 us suspend-time hint: the hardware parks the warp until the phase
+// completes or the hint expires.  Returns false (and the caller records an error) if the
+// phase has not completed after kWaitLimit rounds.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(addr), "r"(parity), "r"(1000u) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t addr, uint32_t parity) {
+  if (mbar_test_wait(addr, parity)) return true;
+  for (uint32_t i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait_hint(addr, parity)) return true;
+  return false;
+}
+// 2-D tiled bulk tensor load into this CTA's shared memory, completing on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int x, int y, uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(tmap), "r"(x), "r"(y), "r"(mbar) : "memory");
+}
+// 4-byte async copy global -> shared with zero fill: copies src_bytes (0..4) bytes,
+// zero-fills the rest (src_bytes == 0 reads nothing).
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+// Arrive on an mbarrier once all of this thread's prior cp.async copies have landed
+// (the arrival counts toward the barrier's expected count).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t mbar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(mbar) : "memory");
+}
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Thread-block-cluster helpers (distributed shared memory).

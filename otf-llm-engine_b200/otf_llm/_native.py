@@ -25,6 +25,7 @@ EXPORTS = (
     "otf_version",
     "otf_status_string",
     "otf_last_cuda_error",
+    "otf_device_error",
     "otf2b_linear",
     "otf2b_unpack_codes",
     "otf_i8_head",
@@ -53,6 +54,8 @@ def lib() -> ctypes.CDLL:
     L.otf_status_string.argtypes = [i32]
     L.otf_status_string.restype = ctypes.c_char_p
     L.otf_last_cuda_error.restype = i32
+    L.otf_device_error.argtypes = [i32]
+    L.otf_device_error.restype = i32
     L.otf2b_linear.argtypes = [vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, vp, i64, vp, vp, i64, vp, i64,
                                i64, i64, i64, i64, u32, vp]
     L.otf2b_linear.restype = i32
@@ -274,3 +277,8 @@ def silu_mul(g: torch.Tensor, u: torch.Tensor, out: Optional[torch.Tensor] = Non
         st = lib().otf_silu_mul(_ptr(g), _ptr(u), _ptr(out), g.numel(), _stream(g.device))
     _check(st, "otf_silu_mul")
     return out
+
+
+def device_error(clear: bool = True) -> int:
+    """1 if a pipelined kernel gave up on a bounded wait since the last clear (synchronous)."""
+    return int(lib().otf_device_error(1 if clear else 0))

@@ -121,6 +121,7 @@ def test_full_size_shapes(N, K, cuda_dev):
                              outlier_vals=ov.to(cuda_dev))
     assert rel_err(y1.cpu().numpy(), ref) < TOL
     assert torch.equal(y1, y2)  # deterministic
+    assert _native.device_error() == 0  # no pipeline wait gave up
 
 
 def test_unpack_codes_bit_exact(cuda_dev):
