@@ -39,6 +39,11 @@ extern "C" {
 #define OTF_ERR_CUDA 3         /* a CUDA runtime call failed (see otf_last_cuda_error) */
 #define OTF_ERR_DEVICE 4       /* current device is not sm_100 */
 
+/* Input transforms of otf2b_linear_group (applied to x while the kernel stages it). */
+#define OTF_XOP_NONE 0
+#define OTF_XOP_RMSNORM 1   /* x <- aux * fp16(x * rsqrt(mean(x^2) + eps)); aux may be NULL (ones) */
+#define OTF_XOP_SILU_MUL 2  /* x <- fp16(fp16(silu(x)) * aux) */
+
 /* Flags for otf2b_linear. */
 #define OTF_FLAG_CLAMP 1u          /* clamp output to [-65504, 65504] (SymmetricOTF2BitLinear) */
 #define OTF_FLAG_FORCE_GENERIC 2u  /* use the portable CUDA-core kernel (testing) */
@@ -94,6 +99,49 @@ OTF_API int otf2b_linear(const void* x, int64_t ldx,
                          void* y, int64_t ldy,
                          int64_t M, int64_t N, int64_t K, int64_t group_size,
                          uint32_t flags, void* stream);
+
+/*
+ * One layer of a grouped decode launch (batch 1).  Fields mean what the arguments of
+ * otf2b_linear mean; x_op transforms x while the kernel stages it (this package's fusion
+ * of the Llama decoder step around the reference's projections):
+ *   OTF_XOP_RMSNORM   x <- x_aux * fp16(x * rsqrt(mean(x^2) + eps))   (x_aux: fp16 [K] or NULL)
+ *   OTF_XOP_SILU_MUL  x <- fp16(fp16(silu(x)) * x_aux)               (x_aux: fp16 [K])
+ * The layer's mask applies after the transform; anchors use the transformed, unmasked x.
+ */
+typedef struct otf2b_layer {
+  const void* x;
+  int64_t ldx;
+  const uint8_t* packed;
+  int64_t ld_packed;
+  const void* scales;
+  int64_t ld_scales;
+  const void* zeros;
+  int64_t ld_zeros;
+  const float* codebook; /* host pointer to 4 floats */
+  const void* mask;
+  const int64_t* outlier_idx;
+  int64_t n_outliers;
+  const void* outlier_vals;
+  int64_t ld_outlier_vals;
+  const void* bias;
+  const void* residual;
+  int64_t ld_residual;
+  void* y;
+  int64_t ldy;
+  int64_t N, K, group_size;
+  uint32_t flags;
+  int32_t x_op;
+  const void* x_aux;
+  float eps;
+} otf2b_layer;
+
+/*
+ * Up to 4 layers in one launch (q/k/v, or gate/up, of a decoder step).  Layers with the
+ * same K, group size and zero-point use share one grid; otherwise they launch one after
+ * another.  The reference launched each projection separately
+ * (otf_llm/symmetric_2bit_engine.py:214-235 per module call).
+ */
+OTF_API int otf2b_linear_group(const otf2b_layer* layers, int n_layers, void* stream);
 
 /*
  * Unpack 2-bit codes to one byte per code: codes[n,k] = q[n,k] in {0..3}.

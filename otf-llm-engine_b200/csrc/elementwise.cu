@@ -11,6 +11,8 @@ int check_device();                 // capi.cu
 // One CTA per row: fp32 sum of squares, then out = w * fp16(x * rsqrt(mean + eps)).
 __global__ void __launch_bounds__(256) k_rmsnorm(const uint16_t* x, int64_t ldx, const uint16_t* w, float eps,
                                                  uint16_t* out, int64_t ldo, int K) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[8];
   const uint16_t* xr = x + blockIdx.x * ldx;
   uint16_t* orow = out + blockIdx.x * ldo;
@@ -35,6 +37,8 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const uint16_t* x, int64_t ldx,
 }
 
 __global__ void k_silu_mul(const uint16_t* g, const uint16_t* u, uint16_t* out, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float gv = h2f(g[i]);
     const __half s = __float2half_rn(gv / (1.0f + expf(-gv)));
@@ -52,10 +56,9 @@ extern "C" OTF_API int otf_rmsnorm(const void* x, int64_t ldx, const void* w, fl
   if (M > INT32_MAX || K > INT32_MAX) return OTF_ERR_UNSUPPORTED;
   int st = check_device();
   if (st != OTF_OK) return st;
-  k_rmsnorm<<<(unsigned)M, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(x), ldx, static_cast<const uint16_t*>(w), eps, static_cast<uint16_t*>(out), ldo,
-      (int)K);
-  return set_cuda_error(cudaGetLastError());
+  return set_cuda_error(launch_pdl(k_rmsnorm, dim3((unsigned)M), dim3(256), 0, static_cast<cudaStream_t>(stream), 1u,
+                                   static_cast<const uint16_t*>(x), ldx, static_cast<const uint16_t*>(w), eps,
+                                   static_cast<uint16_t*>(out), ldo, (int)K));
 }
 
 extern "C" OTF_API int otf_silu_mul(const void* g, const void* u, void* out, int64_t n, void* stream) {
@@ -64,7 +67,7 @@ extern "C" OTF_API int otf_silu_mul(const void* g, const void* u, void* out, int
   int st = check_device();
   if (st != OTF_OK) return st;
   const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 8);
-  k_silu_mul<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(g), static_cast<const uint16_t*>(u), static_cast<uint16_t*>(out), n);
-  return set_cuda_error(cudaGetLastError());
+  return set_cuda_error(launch_pdl(k_silu_mul, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream), 1u,
+                                   static_cast<const uint16_t*>(g), static_cast<const uint16_t*>(u),
+                                   static_cast<uint16_t*>(out), n));
 }

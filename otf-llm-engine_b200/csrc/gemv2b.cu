@@ -17,11 +17,16 @@
 //
 // Work split: a thread-block cluster of S CTAs covers one group of row tiles; CTA s of
 // the cluster owns K slice s, so it quantises only that slice of the activation table.
-// Each warp owns whole 16-row tiles inside its CTA's slice and streams its (tile, chunk)
-// items through a 4-deep register ring of code words and scales -- no CTA barrier in the
-// main loop.  The S K-partials of every row meet once, over distributed shared memory,
+// Each warp owns whole 16-row tiles inside its CTA's slice and pipelines its own code
+// stages: lane 0 issues a 2-D TMA box per (tile, chunk) into one of kSlots shared-memory
+// slots completing on an mbarrier, and refills the slot once the warp has consumed it;
+// scales and zero points follow through a kSlots-deep register ring.  No CTA barrier in
+// the main loop.  The S K-partials of every row meet once, over distributed shared memory,
 // where the fused epilogue adds the fp16 outlier anchors (dot products computed in the
 // prologue while the weights are in flight), bias and residual, clamps and stores fp16.
+//
+// Every wait is bounded; a wait that gives up sets g_otf_device_error (read through
+// otf_device_error) and the kernel runs to completion with wrong data instead of hanging.
 //
 // Reference behaviour replaced: otf_llm/otf_triton_2bit_kernel.py:164-194 (dispatch,
 // mask multiply, LUT path), :23-113 (warp GEMV), otf_llm/symmetric_2bit_engine.py:
@@ -69,6 +74,19 @@ struct LinearArgs {
   float c0, c1, c2, c3;
   int clamp;
   int tiles_per_group;  // row tiles per cluster
+  int xop;              // OTF_XOP_*: transform applied to x while staging it
+  const uint16_t* xaux; // RMSNorm weight or the SiLU gate's second operand
+  float eps;            // RMSNorm epsilon
+};
+
+// A group of layers launched together (decode-step fusion: q/k/v or gate/up share an
+// input and one launch).  Cluster c serves layer m with prefix[m] <= c < prefix[m+1].
+constexpr int kMaxGroup = 4;
+struct GroupParams {
+  LinearArgs L[kMaxGroup];
+  CUtensorMap tm[kMaxGroup];
+  int n;
+  int prefix[kMaxGroup + 1];
 };
 
 // One CTA's shared memory: per-consumer-warp pipeline stages (codes via TMA) and their
@@ -76,7 +94,7 @@ struct LinearArgs {
 // table, the staged activation slice, per-block constants, the anchor activations,
 // the anchor weights of the rows this CTA finishes and the K-partials pushed to it.
 struct GemvSmem {
-  int64_t stages, bars, tbl, xs, meta, xo, afin, fin, zblk, total;
+  int64_t stages, bars, tbl, xs, meta, xo, afin, fin, zblk, nrm, total;
   int stage_bytes;
 };
 
@@ -97,6 +115,7 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int W, int K, int S, int n_
   L.afin = off;   off = align_up(off + (int64_t)frows * 4, 16);  // anchor dot product per finished row
   L.fin = off;    off = align_up(off + (int64_t)S * frows * 4, 16);
   L.zblk = off;   off = align_up(off + SL, 16);
+  L.nrm = off;    off = align_up(off + kMaxCluster * 4 + kCWarps * 4, 16);  // RMSNorm partial sums
   L.total = off;
   return L;
 }
@@ -117,8 +136,22 @@ __device__ __forceinline__ uint16_t ldg_u16(const uint16_t* p) { return __ldg(p)
 
 __device__ __forceinline__ void report_wait_failure() { atomicExch(&g_otf_device_error, 1); }
 
+// x transform while staging: x <- w * fp16(x * rsqrt(mean(x^2) + eps)) (Llama RMSNorm) or
+// x <- fp16(fp16(silu(x)) * aux) (Llama SiLU gate), then the layer's mask multiply.
+__device__ __forceinline__ __half xform(__half x, int xop, const uint16_t* aux, int k, float r) {
+  if (xop == OTF_XOP_RMSNORM) {
+    const __half v = __float2half_rn(__half2float(x) * r);
+    return aux ? __hmul(__ushort_as_half(aux[k]), v) : v;
+  }
+  if (xop == OTF_XOP_SILU_MUL) {
+    const float gv = __half2float(x);
+    return __hmul(__float2half_rn(gv / (1.0f + expf(-gv))), __ushort_as_half(aux[k]));
+  }
+  return x;
+}
+
 template <int W, bool ZEROS>
-__global__ void __launch_bounds__(kThreads, 2) k_gemv2b(const LinearArgs a, const __grid_constant__ CUtensorMap tm) {
+__device__ __forceinline__ void gemv_body(const LinearArgs& a, const CUtensorMap* tmp, const int group) {
   constexpr int BLK = 16 * W, SL = 32 * W + 16, SB = 2 * SL;
   constexpr int CB = 16 * W;                       // code bytes per row per chunk
   extern __shared__ __align__(128) uint8_t smem[];
@@ -128,7 +161,6 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv2b(const LinearArgs a, cons
   asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
   const int S = (int)cs;
   const int rank = (int)cluster_ctarank();
-  const int group = (int)blockIdx.x / S;
   const int ch_slice = ceil_div(nch, S);
   const int cbeg = min(rank * ch_slice, nch), cend = min(cbeg + ch_slice, nch);
   const int blk0 = 4 * cbeg, blk1 = min(4 * cend, nblk);
@@ -160,11 +192,16 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv2b(const LinearArgs a, cons
   auto stage_addr = [&](int w, int slot) { return stages_s + (uint32_t)((w * kSlots + slot) * L.stage_bytes); };
   auto tiles_of = [&](int w) { return w < gtiles ? ceil_div(gtiles - w, kCWarps) : 0; };
 
+  // Programmatic dependent launch: let the next kernel in the stream start launching now
+  // (no-op without the launch attribute).  Everything this kernel reads from its
+  // predecessor's output comes after griddepcontrol.wait below.
+  pdl_trigger();
   if (tid == 0) {
     for (int i = 0; i < kCWarps * kSlots; ++i) mbar_init(bars_s + i * 8, 1);  // expect_tx arrive (+ TMA bytes)
     mbar_fence_init();
   }
   __syncthreads();
+  cluster_arrive_relaxed();  // paired with cluster_wait() before the first DSMEM store
 
   // Stage k of warp w = (tile w + 8*(k / mych), chunk k % mych of my slice).  Lane 0 of
   // the warp issues its TMA into slot k % kSlots and refills the slot once consumed; the
@@ -175,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv2b(const LinearArgs a, cons
   auto issue_next = [&]() {
     const uint32_t fb = full_bar(warp, is_slot);
     mbar_arrive_expect_tx(fb, kRows * CB);
-    tma_load_2d(stage_addr(warp, is_slot), &tm, (cbeg + is_cc) * CB, is_row, fb);
+    tma_load_2d(stage_addr(warp, is_slot), tmp, (cbeg + is_cc) * CB, is_row, fb);
     if (++is_slot == kSlots) is_slot = 0;
     if (++is_cc == mych) {
       is_cc = 0;
@@ -184,35 +221,136 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv2b(const LinearArgs a, cons
   };
   if (lane == 0)
     for (int k = 0; k < min(kSlots, nst); ++k) issue_next();
+  const int g = lane >> 2, t = lane & 3;
+  // Parameter cursor: per-tile row pointers, per-stage group index.
+  int lt = 0, lc = 0;
+  const uint16_t* sp0 = nullptr;
+  const uint16_t* sp1 = nullptr;
+  const uint16_t* zp0 = nullptr;
+  const uint16_t* zp1 = nullptr;
+  bool pv0 = false, pv1 = false;
+  auto param_tile = [&]() {
+    const int rg = (tile0 + warp + kCWarps * lt) * kRows + g;
+    pv0 = lt < my_tiles && rg < N;
+    pv1 = lt < my_tiles && rg + 8 < N;
+    sp0 = a.scales + (pv0 ? (int64_t)rg * a.lds : 0);
+    sp1 = a.scales + (pv1 ? (int64_t)(rg + 8) * a.lds : 0);
+    if constexpr (ZEROS) {
+      zp0 = a.zeros + (pv0 ? (int64_t)rg * a.ldz : 0);
+      zp1 = a.zeros + (pv1 ? (int64_t)(rg + 8) * a.ldz : 0);
+    }
+  };
+  auto load_params = [&](uint32_t& s0, uint32_t& s1, uint32_t& z0, uint32_t& z1) {
+    const int blk = 4 * (cbeg + lc) + t;
+    const bool inb = blk < nblk;
+    const int grp = inb ? (blk >> gshift) : 0;
+    s0 = s1 = 0u;
+    ld_u16_pred(s0, sp0 + grp, pv0 && inb);
+    ld_u16_pred(s1, sp1 + grp, pv1 && inb);
+    z0 = z1 = 0u;
+    if constexpr (ZEROS) {
+      ld_u16_pred(z0, zp0 + grp, pv0 && inb);
+      ld_u16_pred(z1, zp1 + grp, pv1 && inb);
+    }
+    if (++lc == mych) {
+      lc = 0;
+      ++lt;
+      param_tile();
+    }
+  };
+  param_tile();
+  uint32_t rs0[kSlots], rs1[kSlots], rz0[kSlots], rz1[kSlots];
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s) load_params(rs0[s], rs1[s], rz0[s], rz1[s]);
   {
     // Epilogue inputs of the rows this CTA finishes (rank + S*i of the group).
     const int fr = rank + S * tid;
     const int frow = tile0 * kRows + fr;
     const bool fin_ok = fr < grows && frow < N;
     float ep = 0.0f;
-    if (fin_ok) {
-      if (a.bias) ep += h2f(ldg_u16(a.bias + frow));
-      if (a.res) ep += h2f(ldg_u16(a.res + frow));
-    }
-    for (int j = tid; j < a.n_out; j += kCThreads) xo[j] = h2f(ldg_u16(a.x + __ldg(a.oidx + j)));
-    // Stage my slice of x * mask (fp16, as the reference multiplies); padded tail = 0.
+    if (fin_ok && a.bias) ep += h2f(ldg_u16(a.bias + frow));
+    // Weights, scales and bias are in flight; from here on we read the predecessor's output.
+    pdl_wait();
+    if (fin_ok && a.res) ep += h2f(ldg_u16(a.res + frow));
+    // Stage my slice of x (fp16); padded tail = 0.  The SiLU gate and the mask apply on the
+    // way in; RMSNorm first needs the sum of squares of all K, combined across the cluster
+    // (the K slices partition K) over distributed shared memory, then a second pass.
+    float* nrm = reinterpret_cast<float*>(smem + L.nrm);
+    const bool norm = a.xop == OTF_XOP_RMSNORM;
+    float ssq = 0.0f;
     {
       const uint4* xsrc = reinterpret_cast<const uint4*>(a.x + kbeg);
-      const uint4* msrc = a.mask ? reinterpret_cast<const uint4*>(a.mask + kbeg) : nullptr;
       for (int v = tid; v < nbs_pad * BLK / 8; v += kCThreads) {
         uint4 xv = make_uint4(0, 0, 0, 0);
         if (v < nbs * BLK / 8) {
           xv = __ldg(xsrc + v);
-          if (msrc) {
-            const uint4 mv = __ldg(msrc + v);
-            __half2* xh = reinterpret_cast<__half2*>(&xv);
-            const __half2* mh = reinterpret_cast<const __half2*>(&mv);
+          __half2* xh = reinterpret_cast<__half2*>(&xv);
+          if (norm) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) xh[i] = __hmul2(xh[i], mh[i]);
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = __half22float2(xh[i]);
+              ssq = fmaf(f.x, f.x, fmaf(f.y, f.y, ssq));
+            }
+          } else {
+            if (a.xop == OTF_XOP_SILU_MUL) {
+              const uint4 uv = __ldg(reinterpret_cast<const uint4*>(a.xaux + kbeg) + v);
+              const __half* uh = reinterpret_cast<const __half*>(&uv);
+              __half* e = reinterpret_cast<__half*>(&xv);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float gv = __half2float(e[i]);
+                e[i] = __hmul(__float2half_rn(gv / (1.0f + expf(-gv))), uh[i]);
+              }
+            }
+            if (a.mask) {
+              const uint4 mv = __ldg(reinterpret_cast<const uint4*>(a.mask + kbeg) + v);
+              const __half2* mh = reinterpret_cast<const __half2*>(&mv);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) xh[i] = __hmul2(xh[i], mh[i]);
+            }
           }
         }
         reinterpret_cast<uint4*>(xs)[v] = xv;
       }
+    }
+    cluster_wait();  // every CTA of the cluster is running: peers' shared memory is live
+    float rnorm = 1.0f;
+    if (norm) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
+      if (lane == 0) nrm[kMaxCluster + warp] = ssq;
+      named_barrier_sync(1, kCThreads);
+      if (tid == 0) {
+        float part = 0.0f;
+        for (int w = 0; w < kCWarps; ++w) part += nrm[kMaxCluster + w];
+        for (int q = 0; q < S; ++q) st_cluster_f32_plain(mapa_shared(smem_u32(nrm + rank), (uint32_t)q), part);
+      }
+      cluster_sync_all();
+      float tot = 0.0f;
+      for (int q = 0; q < S; ++q) tot += nrm[q];
+      rnorm = rsqrtf(tot / (float)K + a.eps);
+      for (int v = tid; v < nbs * BLK / 8; v += kCThreads) {
+        uint4 xv = reinterpret_cast<uint4*>(xs)[v];
+        __half* e = reinterpret_cast<__half*>(&xv);
+        uint4 wv = make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);  // ones
+        if (a.xaux) wv = __ldg(reinterpret_cast<const uint4*>(a.xaux + kbeg) + v);
+        const __half* wh = reinterpret_cast<const __half*>(&wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) e[i] = __hmul(wh[i], __float2half_rn(__half2float(e[i]) * rnorm));
+        if (a.mask) {
+          const uint4 mv = __ldg(reinterpret_cast<const uint4*>(a.mask + kbeg) + v);
+          __half2* xh = reinterpret_cast<__half2*>(&xv);
+          const __half2* mh = reinterpret_cast<const __half2*>(&mv);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) xh[i] = __hmul2(xh[i], mh[i]);
+        }
+        reinterpret_cast<uint4*>(xs)[v] = xv;
+      }
+    }
+    // Anchor activations: the transformed, unmasked x at the anchor columns.
+    for (int j = tid; j < a.n_out; j += kCThreads) {
+      const int k = (int)__ldg(a.oidx + j);
+      xo[j] = __half2float(xform(__ushort_as_half(ldg_u16(a.x + k)), a.xop, a.xaux, k, rnorm));
     }
     for (int i = tid; i < SL / 4; i += kCThreads) reinterpret_cast<uint32_t*>(zblk)[i] = 0u;
     named_barrier_sync(1, kCThreads);
@@ -286,50 +424,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv2b(const LinearArgs a, cons
     // Main loop: my tiles tl = warp + 8*i, their chunks in order, one stage each.  The
     // scales (and zero points) of stage k + kSlots are fetched into a register ring while
     // stage k is consumed.
-    const int g = lane >> 2, t = lane & 3;
     const bool breal = (g >> 1) == t;
     const uint8_t* bbase = breal ? (tbl + (g >> 1) * SB + (g & 1) * SL) : zblk;
     const int bstep = breal ? 4 * SB : 0;
-    // Parameter cursor: per-tile row pointers, per-stage group index.
-    int lt = 0, lc = 0;
-    const uint16_t* sp0 = nullptr;
-    const uint16_t* sp1 = nullptr;
-    const uint16_t* zp0 = nullptr;
-    const uint16_t* zp1 = nullptr;
-    bool pv0 = false, pv1 = false;
-    auto param_tile = [&]() {
-      const int rg = (tile0 + warp + kCWarps * lt) * kRows + g;
-      pv0 = lt < my_tiles && rg < N;
-      pv1 = lt < my_tiles && rg + 8 < N;
-      sp0 = a.scales + (pv0 ? (int64_t)rg * a.lds : 0);
-      sp1 = a.scales + (pv1 ? (int64_t)(rg + 8) * a.lds : 0);
-      if constexpr (ZEROS) {
-        zp0 = a.zeros + (pv0 ? (int64_t)rg * a.ldz : 0);
-        zp1 = a.zeros + (pv1 ? (int64_t)(rg + 8) * a.ldz : 0);
-      }
-    };
-    auto load_params = [&](uint32_t& s0, uint32_t& s1, uint32_t& z0, uint32_t& z1) {
-      const int blk = 4 * (cbeg + lc) + t;
-      const bool inb = blk < nblk;
-      const int grp = inb ? (blk >> gshift) : 0;
-      s0 = s1 = 0u;
-      ld_u16_pred(s0, sp0 + grp, pv0 && inb);
-      ld_u16_pred(s1, sp1 + grp, pv1 && inb);
-      z0 = z1 = 0u;
-      if constexpr (ZEROS) {
-        ld_u16_pred(z0, zp0 + grp, pv0 && inb);
-        ld_u16_pred(z1, zp1 + grp, pv1 && inb);
-      }
-      if (++lc == mych) {
-        lc = 0;
-        ++lt;
-        param_tile();
-      }
-    };
-    param_tile();
-    uint32_t rs0[kSlots], rs1[kSlots], rz0[kSlots], rz1[kSlots];
-#pragma unroll
-    for (int s = 0; s < kSlots; ++s) load_params(rs0[s], rs1[s], rz0[s], rz1[s]);
     float p0 = 0.0f, p1 = 0.0f;
     int cc = 0, ct = 0;
     for (int base = 0; base < nst; base += kSlots) {
@@ -425,10 +522,30 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv2b(const LinearArgs a, cons
   }
 }
 
+template <int W, bool ZEROS>
+__global__ void __launch_bounds__(kThreads, 2)
+k_gemv2b(const __grid_constant__ LinearArgs a, const __grid_constant__ CUtensorMap tm) {
+  uint32_t cs;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
+  gemv_body<W, ZEROS>(a, &tm, (int)(blockIdx.x / cs));
+}
+
+template <int W, bool ZEROS>
+__global__ void __launch_bounds__(kThreads, 2) k_gemv2b_group(const __grid_constant__ GroupParams gp) {
+  uint32_t cs;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
+  const int cid = (int)(blockIdx.x / cs);
+  int m = 0;
+  while (m + 1 < gp.n && cid >= gp.prefix[m + 1]) ++m;
+  gemv_body<W, ZEROS>(gp.L[m], &gp.tm[m], cid - gp.prefix[m]);
+}
+
 // Portable CUDA-core kernel: any M, any G dividing K with G % 4 == 0, any codebook.
 // One warp per output row, lanes stride over packed bytes; MT activation rows per launch.
 template <int MT>
 __global__ void __launch_bounds__(256) k_linear_generic(const LinearArgs a, int m0) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= a.N) return;
@@ -486,6 +603,8 @@ __global__ void __launch_bounds__(256) k_linear_generic(const LinearArgs a, int 
 
 // 2-bit code unpack: one thread per packed byte, four code bytes out.
 __global__ void k_unpack_codes(const uint8_t* packed, int64_t ldp, int N, int K, uint8_t* codes, int64_t ldc) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t kb4 = K / 4;
   const int64_t total = (int64_t)N * kb4;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -514,6 +633,35 @@ static int num_sms() {
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   if (dev >= 0 && dev < 64) cached[dev] = n;
   return n;
+}
+
+// Launch geometry of one layer: K slices per cluster (S) and row tiles per cluster.
+struct GemvPlan {
+  int S, groups, tpg;
+  int64_t smem;
+};
+
+template <int W>
+static int gemv_S(int K) {
+  const int nblk = K / (16 * W), nch = ceil_div(nblk, 4);
+  int S = std::max(1, std::min(kMaxCluster, nch / 2));
+  while (S > 1 && ceil_div(nch, S) * (S - 1) >= nch) --S;  // every slice non-empty
+  return S;
+}
+
+// Row groups for a layer given a budget of clusters: every consumer warp holds at least
+// one tile, and each of the S*256 threads of a cluster finishes at most one row.
+template <int W>
+static GemvPlan gemv_plan(const LinearArgs& a, int S, int budget) {
+  GemvPlan p;
+  p.S = S;
+  const int ntiles = ceil_div(a.N, kRows);
+  const int min_groups = std::max(1, ceil_div(ntiles * kRows, S * kCThreads));
+  int groups = std::max(min_groups, std::min(std::max(budget, 1), ceil_div(ntiles, kCWarps)));
+  p.tpg = ceil_div(ntiles, groups);
+  p.groups = ceil_div(ntiles, p.tpg);
+  p.smem = gemv_smem_layout(W, a.K, S, a.n_out, p.tpg).total;
+  return p;
 }
 
 // Largest number of co-resident clusters of S CTAs for a given dynamic shared memory
@@ -605,62 +753,90 @@ static bool code_tensor_map(CUtensorMap* out, const uint8_t* base, int64_t rows,
 }
 
 template <int W, bool ZEROS>
-static int launch_gemv(LinearArgs a, cudaStream_t st) {
+static int configure_kernels() {
   static thread_local int configured_dev[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured_dev[dev]) {
     cudaError_t e = cudaFuncSetAttribute(k_gemv2b<W, ZEROS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k_gemv2b_group<W, ZEROS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return set_cuda_error(e);
     configured_dev[dev] = 1;
   }
+  return OTF_OK;
+}
+
+template <int W, bool ZEROS>
+static int launch_gemv(LinearArgs a, cudaStream_t st) {
+  int rc = configure_kernels<W, ZEROS>();
+  if (rc != OTF_OK) return rc;
   CUtensorMap tm;
   if (!code_tensor_map(&tm, a.packed, a.N, a.K / 4, a.ldp, 16 * W)) return OTF_ERR_UNSUPPORTED;
-  const int nblk = a.K / (16 * W), nch = ceil_div(nblk, 4);
-  const int ntiles = ceil_div(a.N, kRows);
-  // K slices: at least two chunks per slice, at most kMaxCluster slices, none empty.
-  int S = std::max(1, std::min(kMaxCluster, nch / 2));
-  while (S > 1 && ceil_div(nch, S) * (S - 1) >= nch) --S;
-  // Row groups: no more clusters than can be resident at once (a second wave of
-  // clusters would double the time), every consumer warp holding at least one tile, and
-  // each of the S*256 consumer threads of a cluster finishing at most one row.
-  const int min_groups = std::max(1, ceil_div(ntiles * kRows, S * kCThreads));
-  int groups = std::max(1, ceil_div(ntiles, kCWarps));
+  const int S = gemv_S<W>(a.K);
+  // No more clusters than can be resident at once: a second wave would double the time.
+  GemvPlan p = gemv_plan<W>(a, S, 1 << 20);
   for (int pass = 0; pass < 3; ++pass) {
-    const int tpg = ceil_div(ntiles, std::max(groups, min_groups));
-    const int64_t smem = gemv_smem_layout(W, a.K, S, a.n_out, tpg).total;
+    if (p.smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
+    const GemvPlan q = gemv_plan<W>(a, S, max_active_clusters<W, ZEROS>(S, p.smem));
+    if (q.groups == p.groups) break;
+    p = q;
+  }
+  if (p.smem > 227 * 1024 || p.tpg * kRows > S * kCThreads) return OTF_ERR_UNSUPPORTED;
+  a.tiles_per_group = p.tpg;
+  return set_cuda_error(launch_pdl(k_gemv2b<W, ZEROS>, dim3((unsigned)(p.groups * S)), dim3(kThreads),
+                                   (size_t)p.smem, st, (unsigned)S, a, tm));
+}
+
+// Layers with the same K, G and zero-point use launched as one grid: cluster budgets are
+// split in proportion to each layer's row tiles so that the whole group is co-resident.
+template <int W, bool ZEROS>
+static int launch_gemv_group(LinearArgs* L, int n, cudaStream_t st) {
+  int rc = configure_kernels<W, ZEROS>();
+  if (rc != OTF_OK) return rc;
+  static thread_local GroupParams gp;  // large: keep it off the host stack
+  gp.n = n;
+  const int S = gemv_S<W>(L[0].K);
+  int64_t smem_hi = 0;
+  int tiles_total = 0;
+  for (int m = 0; m < n; ++m) {
+    if (!code_tensor_map(&gp.tm[m], L[m].packed, L[m].N, L[m].K / 4, L[m].ldp, 16 * W)) return OTF_ERR_UNSUPPORTED;
+    tiles_total += ceil_div(L[m].N, kRows);
+    smem_hi = std::max(smem_hi, gemv_plan<W>(L[m], S, 1 << 20).smem);
+  }
+  GemvPlan plans[kMaxGroup];
+  int64_t smem = smem_hi;
+  for (int pass = 0; pass < 3; ++pass) {
     if (smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
     const int mc = max_active_clusters<W, ZEROS>(S, smem);
-    const int want = std::max(min_groups, std::min(mc, ceil_div(ntiles, kCWarps)));
-    if (want == groups) break;
-    groups = want;
+    int64_t s2 = 0;
+    for (int m = 0; m < n; ++m) {
+      const int tiles = ceil_div(L[m].N, kRows);
+      const int budget = std::max(1, (int)((int64_t)mc * tiles / std::max(tiles_total, 1)));
+      plans[m] = gemv_plan<W>(L[m], S, budget);
+      s2 = std::max(s2, plans[m].smem);
+    }
+    if (s2 == smem) break;
+    smem = s2;
   }
-  groups = std::max(groups, min_groups);
-  a.tiles_per_group = ceil_div(ntiles, groups);
-  groups = ceil_div(ntiles, a.tiles_per_group);
-  if (a.tiles_per_group * kRows > S * kCThreads) return OTF_ERR_UNSUPPORTED;
-  const int64_t smem = gemv_smem_layout(W, a.K, S, a.n_out, a.tiles_per_group).total;
+  int clusters = 0;
+  for (int m = 0; m < n; ++m) {
+    if (plans[m].tpg * kRows > S * kCThreads) return OTF_ERR_UNSUPPORTED;
+    gp.L[m] = L[m];
+    gp.L[m].tiles_per_group = plans[m].tpg;
+    gp.prefix[m] = clusters;
+    clusters += plans[m].groups;
+  }
+  gp.prefix[n] = clusters;
   if (smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(groups * S), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = (size_t)smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)S;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return set_cuda_error(cudaLaunchKernelEx(&cfg, k_gemv2b<W, ZEROS>, a, tm));
+  return set_cuda_error(launch_pdl(k_gemv2b_group<W, ZEROS>, dim3((unsigned)(clusters * S)), dim3(kThreads),
+                                   (size_t)smem, st, (unsigned)S, gp));
 }
 
 static int launch_generic(const LinearArgs& a, cudaStream_t st) {
   const int ctas = ceil_div(a.N, 8);
   for (int m0 = 0; m0 < a.M; m0 += 4) {
-    k_linear_generic<4><<<ctas, 256, 0, st>>>(a, m0);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(k_linear_generic<4>, dim3(ctas), dim3(256), 0, st, 1u, a, m0);
     if (e != cudaSuccess) return set_cuda_error(e);
   }
   return OTF_OK;
@@ -670,13 +846,12 @@ static int launch_generic(const LinearArgs& a, cudaStream_t st) {
 
 using namespace otf;
 
-extern "C" OTF_API int otf2b_linear(const void* x, int64_t ldx, const uint8_t* packed, int64_t ld_packed,
-                                    const void* scales, int64_t ld_scales, const void* zeros, int64_t ld_zeros,
-                                    const float* codebook, const void* mask, const int64_t* outlier_idx,
-                                    int64_t n_outliers, const void* outlier_vals, int64_t ld_outlier_vals,
-                                    const void* bias, const void* residual, int64_t ld_residual, void* y,
-                                    int64_t ldy, int64_t M, int64_t N, int64_t K,
-                                    int64_t group_size, uint32_t flags, void* stream) {
+// Validate one layer's arguments and fill LinearArgs; returns OTF_OK or an error code.
+static int build_args(LinearArgs& a, const void* x, int64_t ldx, const uint8_t* packed, int64_t ld_packed,
+                      const void* scales, int64_t ld_scales, const void* zeros, int64_t ld_zeros, const float* codebook,
+                      const void* mask, const int64_t* outlier_idx, int64_t n_outliers, const void* outlier_vals,
+                      int64_t ld_outlier_vals, const void* bias, const void* residual, int64_t ld_residual, void* y,
+                      int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size, uint32_t flags) {
   if (!x || !packed || !scales || !codebook || !y) return OTF_ERR_INVALID;
   if (M <= 0 || N <= 0 || K <= 0 || group_size <= 0) return OTF_ERR_INVALID;
   if (K % 4 || group_size % 4 || K % group_size) return OTF_ERR_INVALID;
@@ -687,10 +862,7 @@ extern "C" OTF_API int otf2b_linear(const void* x, int64_t ldx, const uint8_t* p
   if (n_outliers < 0 || (n_outliers > 0 && (!outlier_idx || !outlier_vals || ld_outlier_vals < n_outliers)))
     return OTF_ERR_INVALID;
   if (n_outliers > 65536) return OTF_ERR_UNSUPPORTED;
-  int st = check_device();
-  if (st != OTF_OK) return st;
-
-  LinearArgs a;
+  a = LinearArgs{};
   a.x = static_cast<const uint16_t*>(x);
   a.ldx = ldx;
   a.packed = packed;
@@ -718,24 +890,91 @@ extern "C" OTF_API int otf2b_linear(const void* x, int64_t ldx, const uint8_t* p
   a.c2 = codebook[2];
   a.c3 = codebook[3];
   a.clamp = (flags & OTF_FLAG_CLAMP) ? 1 : 0;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  a.xop = OTF_XOP_NONE;
+  a.xaux = nullptr;
+  a.eps = 0.0f;
+  return OTF_OK;
+}
 
-  // The tensor-pipe path needs c3 - c2 == c1 - c0 (affine in the two code bits),
-  // a block of 16W codes inside one scale group and aligned packed rows.
+// Which tensor-pipe variant serves these arguments: 4 (G % 64), 2 (G % 32) or 0 (none).
+// It needs c3 - c2 == c1 - c0 (affine in the two code bits), batch 1, a block of 16W codes
+// inside one scale group, and aligned rows and vectors.
+static int fast_variant(const LinearArgs& a, uint32_t flags) {
+  const auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
   const float lhs = a.c3 - a.c2, rhs = a.c1 - a.c0;
   const bool affine = fabsf(lhs - rhs) <= 1e-6f * fmaxf(1.0f, fabsf(rhs));
-  const uintptr_t pa = reinterpret_cast<uintptr_t>(packed);
-  const bool x_al = reinterpret_cast<uintptr_t>(x) % 16 == 0 && (!mask || reinterpret_cast<uintptr_t>(mask) % 16 == 0) &&
-                    reinterpret_cast<uintptr_t>(scales) % 4 == 0 && (!zeros || reinterpret_cast<uintptr_t>(zeros) % 4 == 0);
-  const bool fast_ok = !(flags & OTF_FLAG_FORCE_GENERIC) && affine && M == 1 && x_al && K % 8 == 0;
-  const auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
+  const auto al = [](const void* p, int n) { return reinterpret_cast<uintptr_t>(p) % n == 0; };
+  const bool vec_ok = al(a.x, 16) && (!a.mask || al(a.mask, 16)) && (!a.xaux || al(a.xaux, 16)) && al(a.scales, 4) &&
+                      (!a.zeros || al(a.zeros, 4));
+  if ((flags & OTF_FLAG_FORCE_GENERIC) || !affine || a.M != 1 || !vec_ok || a.K % 8) return 0;
+  if (a.G % 64 == 0 && pow2(a.G / 64) && al(a.packed, 16) && a.ldp % 16 == 0) return 4;
+  if (a.G % 32 == 0 && pow2(a.G / 32) && al(a.packed, 8) && a.ldp % 8 == 0) return 2;
+  return 0;
+}
+
+extern "C" OTF_API int otf2b_linear(const void* x, int64_t ldx, const uint8_t* packed, int64_t ld_packed,
+                                    const void* scales, int64_t ld_scales, const void* zeros, int64_t ld_zeros,
+                                    const float* codebook, const void* mask, const int64_t* outlier_idx,
+                                    int64_t n_outliers, const void* outlier_vals, int64_t ld_outlier_vals,
+                                    const void* bias, const void* residual, int64_t ld_residual, void* y,
+                                    int64_t ldy, int64_t M, int64_t N, int64_t K,
+                                    int64_t group_size, uint32_t flags, void* stream) {
+  LinearArgs a;
+  int st = build_args(a, x, ldx, packed, ld_packed, scales, ld_scales, zeros, ld_zeros, codebook, mask, outlier_idx,
+                      n_outliers, outlier_vals, ld_outlier_vals, bias, residual, ld_residual, y, ldy, M, N, K,
+                      group_size, flags);
+  if (st != OTF_OK) return st;
+  st = check_device();
+  if (st != OTF_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = OTF_ERR_UNSUPPORTED;
-  if (fast_ok && group_size % 64 == 0 && pow2(group_size / 64) && pa % 16 == 0 && ld_packed % 16 == 0)
-    rc = zeros ? launch_gemv<4, true>(a, s) : launch_gemv<4, false>(a, s);
-  else if (fast_ok && group_size % 32 == 0 && pow2(group_size / 32) && pa % 8 == 0 && ld_packed % 8 == 0)
-    rc = zeros ? launch_gemv<2, true>(a, s) : launch_gemv<2, false>(a, s);
+  switch (fast_variant(a, flags)) {
+    case 4: rc = zeros ? launch_gemv<4, true>(a, s) : launch_gemv<4, false>(a, s); break;
+    case 2: rc = zeros ? launch_gemv<2, true>(a, s) : launch_gemv<2, false>(a, s); break;
+    default: break;
+  }
   if (rc != OTF_ERR_UNSUPPORTED) return rc;
   return launch_generic(a, s);
+}
+
+extern "C" OTF_API int otf2b_linear_group(const otf2b_layer* layers, int n_layers, void* stream) {
+  if (!layers || n_layers <= 0 || n_layers > kMaxGroup) return OTF_ERR_INVALID;
+  LinearArgs L[kMaxGroup];
+  for (int m = 0; m < n_layers; ++m) {
+    const otf2b_layer& d = layers[m];
+    int st = build_args(L[m], d.x, d.ldx, d.packed, d.ld_packed, d.scales, d.ld_scales, d.zeros, d.ld_zeros,
+                        d.codebook, d.mask, d.outlier_idx, d.n_outliers, d.outlier_vals, d.ld_outlier_vals, d.bias,
+                        d.residual, d.ld_residual, d.y, d.ldy, 1, d.N, d.K, d.group_size, d.flags);
+    if (st != OTF_OK) return st;
+    if (d.x_op < OTF_XOP_NONE || d.x_op > OTF_XOP_SILU_MUL) return OTF_ERR_INVALID;
+    if (d.x_op == OTF_XOP_SILU_MUL && !d.x_aux) return OTF_ERR_INVALID;
+    L[m].xop = d.x_op;
+    L[m].xaux = static_cast<const uint16_t*>(d.x_aux);
+    L[m].eps = d.eps;
+  }
+  int st = check_device();
+  if (st != OTF_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // One grid needs one kernel variant and one cluster shape: same K, G and zero-point use.
+  bool same = true;
+  const int v0 = fast_variant(L[0], layers[0].flags);
+  for (int m = 1; m < n_layers; ++m)
+    same = same && L[m].K == L[0].K && L[m].G == L[0].G && (L[m].zeros != nullptr) == (L[0].zeros != nullptr) &&
+           fast_variant(L[m], layers[m].flags) == v0;
+  if (same && v0 == 4)
+    return L[0].zeros ? launch_gemv_group<4, true>(L, n_layers, s) : launch_gemv_group<4, false>(L, n_layers, s);
+  if (same && v0 == 2)
+    return L[0].zeros ? launch_gemv_group<2, true>(L, n_layers, s) : launch_gemv_group<2, false>(L, n_layers, s);
+  // Otherwise one launch per layer; transforms need the tensor-pipe kernel.
+  for (int m = 0; m < n_layers; ++m) {
+    const int v = fast_variant(L[m], layers[m].flags);
+    int rc = OTF_ERR_UNSUPPORTED;
+    if (v == 4) rc = L[m].zeros ? launch_gemv<4, true>(L[m], s) : launch_gemv<4, false>(L[m], s);
+    else if (v == 2) rc = L[m].zeros ? launch_gemv<2, true>(L[m], s) : launch_gemv<2, false>(L[m], s);
+    else if (L[m].xop == OTF_XOP_NONE) rc = launch_generic(L[m], s);
+    if (rc != OTF_OK) return rc;
+  }
+  return OTF_OK;
 }
 
 extern "C" OTF_API int otf2b_unpack_codes(const uint8_t* packed, int64_t ld_packed, int64_t N, int64_t K,
@@ -746,9 +985,8 @@ extern "C" OTF_API int otf2b_unpack_codes(const uint8_t* packed, int64_t ld_pack
   if (st != OTF_OK) return st;
   const int64_t total = N * (K / 4);
   const int blocks = (int)std::min<int64_t>(ceil_div((int)std::min<int64_t>(total, INT32_MAX), 256), 148 * 16);
-  k_unpack_codes<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(packed, ld_packed, (int)N, (int)K, codes,
-                                                                       ld_codes);
-  return set_cuda_error(cudaGetLastError());
+  return set_cuda_error(launch_pdl(k_unpack_codes, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream), 1u,
+                                   packed, ld_packed, (int)N, (int)K, codes, ld_codes));
 }
 
 extern "C" OTF_API int otf_device_error(int clear) {

@@ -40,6 +40,8 @@ __device__ __forceinline__ float head_finish(float v, float s) {
 }
 
 __global__ void __launch_bounds__(kHeadWarps * 32) k_i8_head_imma(const HeadArgs a) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) uint8_t smem[];
   const int nb = a.D / 16;
   const int nch = ceil_div(nb, 4);
@@ -127,6 +129,8 @@ __global__ void __launch_bounds__(kHeadWarps * 32) k_i8_head_imma(const HeadArgs
 
 // Portable head for any D / stride: one warp per vocabulary row.
 __global__ void __launch_bounds__(256) k_i8_head_generic(const HeadArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= a.V) return;
@@ -139,6 +143,8 @@ __global__ void __launch_bounds__(256) k_i8_head_generic(const HeadArgs a) {
 
 __global__ void k_i8_embed(const int64_t* ids, int n, const int8_t* w, int64_t ldw, const uint16_t* scales,
                            uint16_t* out, int64_t ldo, int64_t V, int D, int32_t* bad) {
+  pdl_trigger();
+  pdl_wait();
   const int tok = blockIdx.x;
   if (tok >= n) return;
   const int64_t id = ids[tok];
@@ -188,14 +194,11 @@ extern "C" OTF_API int otf_i8_head(const void* x, int64_t ldx, const int8_t* w, 
     a.out = logits + m * ldl;
     a.V = (int)V;
     a.D = (int)D;
-    if (fast) {
-      const int tiles = ceil_div((int)V, 16);
-      const int ctas = std::max(1, std::min(ceil_div(tiles, kHeadWarps), sms * 2));
-      k_i8_head_imma<<<ctas, kHeadWarps * 32, head_smem_bytes((int)D), s>>>(a);
-    } else {
-      k_i8_head_generic<<<ceil_div((int)V, 8), 256, 0, s>>>(a);
-    }
-    cudaError_t e = cudaGetLastError();
+
+    cudaError_t e = fast ? launch_pdl(k_i8_head_imma, dim3(std::max(1, std::min(ceil_div(ceil_div((int)V, 16), kHeadWarps),
+                                                                               sms * 2))),
+                                      dim3(kHeadWarps * 32), (size_t)head_smem_bytes((int)D), s, 1u, a)
+                         : launch_pdl(k_i8_head_generic, dim3(ceil_div((int)V, 8)), dim3(256), 0, s, 1u, a);
     if (e != cudaSuccess) return set_cuda_error(e);
   }
   return OTF_OK;
@@ -208,7 +211,7 @@ extern "C" OTF_API int otf_i8_embed(const int64_t* ids, int64_t n, const int8_t*
   if (n > INT32_MAX || D > INT32_MAX) return OTF_ERR_UNSUPPORTED;
   int st = check_device();
   if (st != OTF_OK) return st;
-  k_i8_embed<<<(int)n, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      ids, (int)n, w, ldw, static_cast<const uint16_t*>(scales), static_cast<uint16_t*>(out), ldo, V, (int)D, bad_ids);
-  return set_cuda_error(cudaGetLastError());
+  return set_cuda_error(launch_pdl(k_i8_embed, dim3((unsigned)n), dim3(128), 0, static_cast<cudaStream_t>(stream), 1u,
+                                   ids, (int)n, w, ldw, static_cast<const uint16_t*>(scales),
+                                   static_cast<uint16_t*>(out), ldo, V, (int)D, bad_ids));
 }

@@ -4,6 +4,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <utility>
 
 #include "otf_b200.h"
 
@@ -155,6 +156,15 @@ __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Split cluster barrier: arrive on entry, wait before the first distributed-shared-memory
+// access, so that every CTA of the cluster is known to be running when a peer's shared
+// memory is touched (the arrive costs nothing; by the wait the peers have long started).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
 
 // Choose the power-of-two exponent E for 16-bit fixed point so that
 // maxabs * 2^E lies in [8192, 16384): |X| <= 16384 keeps both s8 limbs of X
@@ -173,6 +183,42 @@ __device__ __forceinline__ void split_limbs(int X, int& hi, int& lo) {
 }
 
 __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// Programmatic dependent launch inside a kernel: pdl_trigger lets the next kernel in the
+// stream begin launching; pdl_wait blocks until the previous kernel has completed and its
+// memory is visible.  Both are no-ops when the launch carried no PDL attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+#ifndef __CUDACC_RTC__
+// Launch with the programmatic-stream-serialization attribute (and optional cluster size),
+// so a kernel may start while its predecessor drains; every kernel of this library reads
+// predecessor outputs only after pdl_wait().
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              unsigned cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+#endif
 __host__ __device__ constexpr int64_t align_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 
 }  // namespace otf

@@ -19,6 +19,31 @@ _lib: Optional[ctypes.CDLL] = None
 
 OTF_FLAG_CLAMP = 1
 OTF_FLAG_FORCE_GENERIC = 2
+OTF_XOP_NONE = 0
+OTF_XOP_RMSNORM = 1
+OTF_XOP_SILU_MUL = 2
+
+
+class Layer(ctypes.Structure):
+    """Mirror of `otf2b_layer` (include/otf_b200.h)."""
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("ldx", ctypes.c_int64),
+        ("packed", ctypes.c_void_p), ("ld_packed", ctypes.c_int64),
+        ("scales", ctypes.c_void_p), ("ld_scales", ctypes.c_int64),
+        ("zeros", ctypes.c_void_p), ("ld_zeros", ctypes.c_int64),
+        ("codebook", ctypes.POINTER(ctypes.c_float)),
+        ("mask", ctypes.c_void_p),
+        ("outlier_idx", ctypes.c_void_p), ("n_outliers", ctypes.c_int64),
+        ("outlier_vals", ctypes.c_void_p), ("ld_outlier_vals", ctypes.c_int64),
+        ("bias", ctypes.c_void_p),
+        ("residual", ctypes.c_void_p), ("ld_residual", ctypes.c_int64),
+        ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
+        ("N", ctypes.c_int64), ("K", ctypes.c_int64), ("group_size", ctypes.c_int64),
+        ("flags", ctypes.c_uint32),
+        ("x_op", ctypes.c_int32),
+        ("x_aux", ctypes.c_void_p),
+        ("eps", ctypes.c_float),
+    ]
 
 # Names exported by the library; kept in step with include/otf_b200.h.
 EXPORTS = (
@@ -27,6 +52,7 @@ EXPORTS = (
     "otf_last_cuda_error",
     "otf_device_error",
     "otf2b_linear",
+    "otf2b_linear_group",
     "otf2b_unpack_codes",
     "otf_i8_head",
     "otf_i8_embed",
@@ -59,6 +85,8 @@ def lib() -> ctypes.CDLL:
     L.otf2b_linear.argtypes = [vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, vp, i64, vp, vp, i64, vp, i64,
                                i64, i64, i64, i64, u32, vp]
     L.otf2b_linear.restype = i32
+    L.otf2b_linear_group.argtypes = [ctypes.POINTER(Layer), ctypes.c_int, vp]
+    L.otf2b_linear_group.restype = i32
     L.otf2b_unpack_codes.argtypes = [vp, i64, i64, i64, vp, i64, vp]
     L.otf2b_unpack_codes.restype = i32
     L.otf_i8_head.argtypes = [vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, vp]
@@ -282,3 +310,66 @@ def silu_mul(g: torch.Tensor, u: torch.Tensor, out: Optional[torch.Tensor] = Non
 def device_error(clear: bool = True) -> int:
     """1 if a pipelined kernel gave up on a bounded wait since the last clear (synchronous)."""
     return int(lib().otf_device_error(1 if clear else 0))
+
+
+class GroupItem:
+    """One layer of `linear_group`: a SymmetricOTF2BitLinear-like module plus its input,
+    output, optional residual and input transform (x_op with its aux vector and eps)."""
+
+    def __init__(self, module, x: torch.Tensor, out: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                 x_op: int = OTF_XOP_NONE, x_aux: Optional[torch.Tensor] = None, eps: float = 0.0,
+                 clamp: bool = True):
+        self.m, self.x, self.out, self.residual = module, x, out, residual
+        self.x_op, self.x_aux, self.eps, self.clamp = x_op, x_aux, eps, clamp
+
+
+def _layer_struct(it: GroupItem, keep: list) -> Layer:
+    m = it.m
+    K, N, G = m.d_in, m.out_features, m.group_size
+    for name, t, dt, cols in (("x", it.x, torch.float16, K), ("out", it.out, torch.float16, N)):
+        _need_cuda(t, name)
+        _rows(t, name, dt, cols)
+    if it.x.shape[0] != 1:
+        raise ValueError("linear_group runs batch-1 decode steps")
+    cb = (ctypes.c_float * 4)(*codebook_floats(m.codebook))
+    keep.append(cb)
+    has_o = getattr(m, "has_outliers", False)
+    zeros = getattr(m, "zeros", None)
+    L = Layer()
+    L.x, L.ldx = it.x.data_ptr(), _rows(it.x, "x", torch.float16, K)
+    L.packed, L.ld_packed = m.packed_uint8.data_ptr(), _rows(m.packed_uint8, "packed", torch.uint8, K // 4)
+    L.scales, L.ld_scales = m.scales.data_ptr(), _rows(m.scales, "scales", torch.float16, K // G)
+    if zeros is not None:
+        L.zeros, L.ld_zeros = zeros.data_ptr(), _rows(zeros, "zeros", torch.float16, K // G)
+    L.codebook = ctypes.cast(cb, ctypes.POINTER(ctypes.c_float))
+    if has_o:
+        L.mask = m.outlier_mask_vector.data_ptr()
+        L.outlier_idx, L.n_outliers = m.outlier_indices.data_ptr(), m.outlier_indices.numel()
+        L.outlier_vals = m.outliers_fp16.data_ptr()
+        L.ld_outlier_vals = _rows(m.outliers_fp16, "outlier_vals", torch.float16, L.n_outliers)
+    if getattr(m, "has_bias", False):
+        L.bias = m.bias.data_ptr()
+    if it.residual is not None:
+        L.residual, L.ld_residual = it.residual.data_ptr(), _rows(it.residual, "residual", torch.float16, N)
+    L.y, L.ldy = it.out.data_ptr(), _rows(it.out, "out", torch.float16, N)
+    L.N, L.K, L.group_size = N, K, G
+    L.flags = OTF_FLAG_CLAMP if it.clamp else 0
+    L.x_op = it.x_op
+    if it.x_aux is not None:
+        if it.x_aux.dtype != torch.float16 or it.x_aux.numel() != K or not it.x_aux.is_contiguous():
+            raise ValueError("x_aux must be a contiguous fp16 vector of length K")
+        L.x_aux = it.x_aux.data_ptr()
+    L.eps = float(it.eps)
+    return L
+
+
+def linear_group(items: Sequence[GroupItem]) -> None:
+    """Run up to 4 decode-step layers in one launch (see otf2b_linear_group)."""
+    if not 1 <= len(items) <= 4:
+        raise ValueError("linear_group takes 1 to 4 layers")
+    dev = items[0].x.device
+    keep: list = []
+    arr = (Layer * len(items))(*[_layer_struct(it, keep) for it in items])
+    with torch.cuda.device(dev):
+        st = lib().otf2b_linear_group(arr, len(items), _stream(dev))
+    _check(st, "otf2b_linear_group")

@@ -108,9 +108,10 @@ class Llama2BitLinearStack(nn.Module):
     """Random-init, 2-bit quantized decoder linear stack (batch-1 decode step)."""
 
     def __init__(self, cfg: StackConfig = LLAMA2_7B, device="cuda", seed: int = 0, rank: int = 0, world: int = 1,
-                 process_group=None):
+                 process_group=None, fused: bool = True):
         super().__init__()
         self.cfg = cfg
+        self.fused = fused
         self.rank, self.world, self.pg = rank, world, process_group
         dev = torch.device(device)
         shapes = cfg.shapes()
@@ -157,7 +158,7 @@ class Llama2BitLinearStack(nn.Module):
                 for layer in self.layers for m in layer.values()]
 
     def launches_per_token(self) -> int:
-        return 10 * len(self.layers)
+        return (4 if self.fused else 10) * len(self.layers)
 
     # -- forward ----------------------------------------------------------------------
     def _lin(self, m: SymmetricOTF2BitLinear, x: torch.Tensor, out: torch.Tensor,
@@ -178,8 +179,34 @@ class Llama2BitLinearStack(nn.Module):
         out.view(-1, rep, hd).copy_(v.view(-1, 1, hd).expand(-1, rep, hd))
         return out
 
+    def _forward_fused(self, h: torch.Tensor) -> torch.Tensor:
+        """Four launches per layer: [rmsnorm + q/k/v], [o + residual], [rmsnorm + gate/up],
+        [silu gate + down + residual] (the norms and the gate run inside the GEMV prologue)."""
+        b = self._buf
+        cfg = self.cfg
+        tp = self.world > 1
+        G = _native.GroupItem
+        cur = h
+        for layer in self.layers:
+            _native.linear_group([G(layer[n], cur, b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.norm_w,
+                                    eps=cfg.rms_eps) for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"))])
+            attn = self._attn_passthrough(b["v"], b["attn"])
+            _native.linear_group([G(layer["o_proj"], attn, b["h1"], residual=None if (tp and self.rank) else cur)])
+            if tp:
+                torch.distributed.all_reduce(b["h1"], group=self.pg)
+            _native.linear_group([G(layer[n], b["h1"], b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.norm_w,
+                                    eps=cfg.rms_eps) for n, o in (("gate_proj", "g"), ("up_proj", "u"))])
+            _native.linear_group([G(layer["down_proj"], b["g"], b["h2"], residual=None if (tp and self.rank) else b["h1"],
+                                    x_op=_native.OTF_XOP_SILU_MUL, x_aux=b["u"])])
+            if tp:
+                torch.distributed.all_reduce(b["h2"], group=self.pg)
+            cur = b["h2"]
+        return cur
+
     def forward(self, h: torch.Tensor, linears_only: bool = False) -> torch.Tensor:
         """One decode step for h [1, hidden] fp16; returns the new residual stream."""
+        if self.fused and not linears_only:
+            return self._forward_fused(h)
         b = self._buf
         cur = h
         for li, layer in enumerate(self.layers):

@@ -1,0 +1,97 @@
+"""Tensor-parallel sharding on CPU ranks (gloo, world size 2).
+
+Each rank shards a quantized layer the way the decode stack does (column shards for
+q/k/v/gate/up, row shards cut at group boundaries with anchors re-based for o/down),
+evaluates its shard with the oracle, and the ranks all-reduce / all-gather.  The result
+must equal the unsharded layer: the exchange step and the anchor re-basing are exact
+up to fp32 summation order.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import load_golden, rel_err
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _oracle_layer(lay, x):
+    from oracle import oracle
+    p = lambda t: None if t is None else t.numpy()
+    return oracle.linear_f32(x, p(lay.packed_uint8), p(lay.scales), lay.group_size,
+                             mask=p(lay.outlier_mask_vector) if lay.has_outliers else None,
+                             outlier_idx=p(lay.outlier_indices) if lay.has_outliers else None,
+                             outlier_vals=p(lay.outliers_fp16) if lay.has_outliers else None)
+
+
+def _worker(rank, world, port, name, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from otf_llm.decoder_stack import shard_linear
+        from otf_llm.symmetric_2bit_engine import SymmetricOTF2BitLinear
+        gd = load_golden(name)
+        K = gd["packed"].shape[1] * 4
+        full = SymmetricOTF2BitLinear(torch.from_numpy(gd["packed"]), torch.from_numpy(gd["scales"]), K,
+                                      int(gd["G"]), torch.from_numpy(gd["outliers"]),
+                                      torch.from_numpy(gd["outlier_idx"]))
+        x = gd["x_m1"]
+        # row-parallel (o/down): shard K, all-reduce partial sums
+        rs = shard_linear(full, rank, world, "in")
+        k0 = rank * K // world
+        part = torch.from_numpy(_oracle_layer(rs, x[:, k0:k0 + rs.d_in]).astype(np.float32))
+        dist.all_reduce(part)
+        # column-parallel (q/k/v/gate/up): shard N, all-gather
+        cs = shard_linear(full, rank, world, "out")
+        mine = torch.from_numpy(_oracle_layer(cs, x).astype(np.float32))
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine)
+        if rank == 0:
+            q.put((part.numpy(), torch.cat(gathered, dim=1).numpy(), _oracle_layer(full, x)))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # surface the failure to the parent
+        q.put(e)
+        raise
+
+
+@pytest.mark.parametrize("name", ["sym_g64_k4096", "sym_g128"])
+def test_tp_shards_reproduce_full_layer(name):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, name, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=180)
+    for p in procs:
+        p.join(timeout=60)
+    assert not isinstance(res, Exception), res
+    row_par, col_par, full = res
+    assert rel_err(row_par, full) < 1e-5
+    assert rel_err(col_par, full) < 1e-6
+
+
+def test_row_shard_rebases_anchors():
+    from otf_llm.decoder_stack import shard_linear
+    from otf_llm.symmetric_2bit_engine import SymmetricOTF2BitLinear
+    gd = load_golden("sym_g64_k4096")
+    full = SymmetricOTF2BitLinear(torch.from_numpy(gd["packed"]), torch.from_numpy(gd["scales"]), 4096, 64,
+                                  torch.from_numpy(gd["outliers"]), torch.from_numpy(gd["outlier_idx"]))
+    seen = []
+    for r in range(4):
+        s = shard_linear(full, r, 4, "in")
+        if s.has_outliers:
+            assert int(s.outlier_indices.min()) >= 0 and int(s.outlier_indices.max()) < 1024
+            seen.extend((s.outlier_indices + r * 1024).tolist())
+    assert sorted(seen) == sorted(gd["outlier_idx"].tolist())
