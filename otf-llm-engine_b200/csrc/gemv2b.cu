@@ -17,13 +17,17 @@
 //
 // Work split: a thread-block cluster of S CTAs covers one group of row tiles; CTA s of
 // the cluster owns K slice s, so it quantises only that slice of the activation table.
-// Each warp owns whole 16-row tiles inside its CTA's slice and pipelines its own code
-// stages: lane 0 issues a 2-D TMA box per (tile, chunk) into one of kSlots shared-memory
-// slots completing on an mbarrier, and refills the slot once the warp has consumed it;
-// scales and zero points follow through a kSlots-deep register ring.  No CTA barrier in
-// the main loop.  The S K-partials of every row meet once, over distributed shared memory,
-// where the fused epilogue adds the fp16 outlier anchors (dot products computed in the
-// prologue while the weights are in flight), bias and residual, clamps and stores fp16.
+// Each warp owns whole 16-row tiles inside its CTA's slice and pipelines its own stages
+// of 16 rows x 128 code bytes (512 codes) plus their scales: every lane issues 16-byte
+// cp.async copies into one of kSlots shared-memory slots (row pitch 144 bytes, so the
+// consumers' 16-byte reads are bank-conflict-free), one commit group per stage, and the
+// warp refills a slot as soon as it has consumed it.  No CTA barrier in the main loop.
+// A stage is consumed as 8/W "sets": lane quad t takes blocks t*8/W + s, so each set is
+// one block-diagonal MMA group over four blocks.  The S K-partials of every row meet
+// once, over distributed shared memory, in the CTA that finishes the row (contiguous
+// blocks of rows per CTA); its fused epilogue adds the fp16 outlier anchors (their
+// weights arrive by one bulk copy issued at kernel entry), bias and residual, clamps and
+// stores fp16.
 //
 // Every wait is bounded; a wait that gives up sets g_otf_device_error (read through
 // otf_device_error) and the kernel runs to completion with wrong data instead of hanging.
@@ -31,8 +35,6 @@
 // Reference behaviour replaced: otf_llm/otf_triton_2bit_kernel.py:164-194 (dispatch,
 // mask multiply, LUT path), :23-113 (warp GEMV), otf_llm/symmetric_2bit_engine.py:
 // 214-235 (bias, outlier anchors, clamp), otf_llm/otf_2bit_quantizer.py:193-221.
-#include <cuda.h>
-
 #include <algorithm>
 #include <map>
 #include <mutex>
@@ -42,12 +44,16 @@
 
 namespace otf {
 
-constexpr int kCWarps = 8;                  // warps per CTA (each pipelines its own code stages)
+constexpr int kCWarps = 8;                  // warps per CTA (each pipelines its own stages)
 constexpr int kThreads = kCWarps * 32;
 constexpr int kCThreads = kCWarps * 32;
 constexpr int kRows = 16;                   // rows per tile (the m16 of the MMA)
-constexpr int kSlots = 6;                   // TMA stages in flight per warp
+constexpr int kSlots = 3;                   // stages in flight per warp
+constexpr int kChunk = 128;                 // code bytes per row per stage (512 codes)
+constexpr int kChunkCodes = 4 * kChunk;
+constexpr int kPitch = kChunk + 16;         // shared-memory row pitch of a stage
 constexpr int kMaxCluster = 8;              // K slices per cluster
+constexpr int kOvMax = 32 * 1024;           // largest anchor-weight block staged in shared memory
 
 __device__ int g_otf_device_error;          // set when a bounded wait gives up
 
@@ -84,38 +90,58 @@ struct LinearArgs {
 constexpr int kMaxGroup = 4;
 struct GroupParams {
   LinearArgs L[kMaxGroup];
-  CUtensorMap tm[kMaxGroup];
   int n;
   int prefix[kMaxGroup + 1];
 };
 
-// One CTA's shared memory: per-consumer-warp pipeline stages (codes via TMA) and their
-// mbarriers, the CTA's slice of the activation
-// table, the staged activation slice, per-block constants, the anchor activations,
-// the anchor weights of the rows this CTA finishes and the K-partials pushed to it.
+// Table geometry for W words per block: limb row SL = 32W+16 bytes (hi row, then lo row),
+// block stride SB a multiple of 128 so that every block's two real reads fall on the same
+// two 16-byte bank groups, and the all-zero block read by the other lanes sits 64 bytes off
+// them (no bank conflict between the real and the zero reads of one instruction).
+__host__ __device__ constexpr int tbl_sl(int W) { return 32 * W + 16; }
+__host__ __device__ constexpr int tbl_sb(int W) { return (2 * tbl_sl(W) + 127) / 128 * 128; }
+
+// Rows a CTA of the cluster finishes: tiles are dealt out in contiguous blocks of tpf.
+__host__ __device__ inline int tiles_per_finisher(int tiles_per_group, int S) { return ceil_div(tiles_per_group, S); }
+
+// One CTA's shared memory: per-warp pipeline stages (codes, scales, zero points), the
+// CTA's slice of the activation table, the staged activation slice, per-block constants,
+// the anchor activations, the anchor weights and per-row anchor sums of the rows this CTA
+// finishes, the K-partials pushed to it and a few scalars.
 struct GemvSmem {
-  int64_t stages, bars, tbl, xs, meta, xo, afin, fin, zblk, nrm, total;
-  int stage_bytes;
+  int64_t stages, tbl, xs, meta, xo, ov, afin, fin, zblk, nrm, bars, total;
+  int stage_bytes, stage_scales, stage_zeros, ov_bytes;
 };
 
-__host__ __device__ inline GemvSmem gemv_smem_layout(int W, int K, int S, int n_out, int tiles_per_group) {
-  const int SL = 32 * W + 16, SB = 2 * SL, nblk = K / (16 * W), nch = (nblk + 3) / 4;
-  const int ch_slice = (nch + S - 1) / S, blk_slice = 4 * ch_slice;
-  const int grows = tiles_per_group * kRows;
-  const int frows = (grows + S - 1) / S;
+// Bytes of scales per row of a stage: the stage's 512/G groups plus 4 bytes of padding
+// (rows of a stage then start on distinct banks).
+__host__ __device__ inline int scale_pitch(int G) { return 2 * (kChunkCodes / G) + 4; }
+
+__host__ __device__ inline GemvSmem gemv_smem_layout(int W, bool zeros, int K, int G, int S, int n_out, int64_t ldo,
+                                                      int tiles_per_group) {
+  const int BLK = 16 * W, SB = tbl_sb(W);
+  const int nch = ceil_div(K, kChunkCodes);
+  const int ch_slice = ceil_div(nch, S), blk_slice = ch_slice * (kChunkCodes / BLK);
+  const int frows = tiles_per_finisher(tiles_per_group, S) * kRows;
   GemvSmem L;
-  L.stage_bytes = kRows * 16 * W;  // one chunk of codes for the 16 rows of a tile
+  L.stage_scales = kRows * kPitch;
+  L.stage_zeros = L.stage_scales + kRows * scale_pitch(G);
+  L.stage_bytes = L.stage_zeros + (zeros ? kRows * scale_pitch(G) : 0);
+  const int64_t ovb = n_out > 0 ? ((int64_t)(frows - 1) * ldo + n_out) * 2 + 32 : 0;
+  L.ov_bytes = ovb <= kOvMax ? (int)align_up(ovb, 16) : 0;  // 0: anchors read from global memory
   int64_t off = 0;
   L.stages = off; off = align_up(off + (int64_t)kCWarps * kSlots * L.stage_bytes, 128);
-  L.bars = off;   off = align_up(off + kCWarps * kSlots * 8, 16);
-  L.tbl = off;    off = align_up(off + (int64_t)blk_slice * SB, 16);
-  L.xs = off;     off = align_up(off + (int64_t)blk_slice * 16 * W * 2, 16);
+  L.tbl = off;    off = align_up(off + (int64_t)blk_slice * SB, 128);
+  L.zblk = off;   off = off + 64 + 128;  // zero block at offset 64 mod 128, 128 bytes long
+  off = align_up(off, 16);
+  L.xs = off;     off = align_up(off + (int64_t)blk_slice * BLK * 2, 16);
   L.meta = off;   off = align_up(off + 3 * (int64_t)blk_slice * 4, 16);
   L.xo = off;     off = align_up(off + (int64_t)n_out * 4, 16);
-  L.afin = off;   off = align_up(off + (int64_t)frows * 4, 16);  // anchor dot product per finished row
+  L.ov = off;     off = align_up(off + L.ov_bytes, 16);
+  L.afin = off;   off = align_up(off + (int64_t)frows * 4, 16);
   L.fin = off;    off = align_up(off + (int64_t)S * frows * 4, 16);
-  L.zblk = off;   off = align_up(off + SL, 16);
   L.nrm = off;    off = align_up(off + kMaxCluster * 4 + kCWarps * 4, 16);  // RMSNorm partial sums
+  L.bars = off;   off = align_up(off + 8, 16);
   L.total = off;
   return L;
 }
@@ -138,140 +164,162 @@ __device__ __forceinline__ void report_wait_failure() { atomicExch(&g_otf_device
 
 // x transform while staging: x <- w * fp16(x * rsqrt(mean(x^2) + eps)) (Llama RMSNorm) or
 // x <- fp16(fp16(silu(x)) * aux) (Llama SiLU gate), then the layer's mask multiply.
-__device__ __forceinline__ __half xform(__half x, int xop, const uint16_t* aux, int k, float r) {
+// aux_v is the auxiliary operand at this column (has_aux: whether the layer has one).
+__device__ __forceinline__ __half xform_v(__half x, int xop, uint16_t aux_v, bool has_aux, float r) {
   if (xop == OTF_XOP_RMSNORM) {
     const __half v = __float2half_rn(__half2float(x) * r);
-    return aux ? __hmul(__ushort_as_half(aux[k]), v) : v;
+    return has_aux ? __hmul(__ushort_as_half(aux_v), v) : v;
   }
   if (xop == OTF_XOP_SILU_MUL) {
     const float gv = __half2float(x);
-    return __hmul(__float2half_rn(gv / (1.0f + expf(-gv))), __ushort_as_half(aux[k]));
+    return __hmul(__float2half_rn(gv / (1.0f + expf(-gv))), __ushort_as_half(aux_v));
   }
   return x;
 }
 
 template <int W, bool ZEROS>
-__device__ __forceinline__ void gemv_body(const LinearArgs& a, const CUtensorMap* tmp, const int group) {
-  constexpr int BLK = 16 * W, SL = 32 * W + 16, SB = 2 * SL;
-  constexpr int CB = 16 * W;                       // code bytes per row per chunk
+__device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) {
+  constexpr int BLK = 16 * W, SL = tbl_sl(W), SB = tbl_sb(W);
+  constexpr int NBC = kChunkCodes / BLK;           // blocks per stage row (8 or 16)
+  constexpr int NBT = NBC / 4;                     // blocks per lane quad = MMA sets per stage
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.K, N = a.N;
-  const int nblk = K / BLK, nch = ceil_div(nblk, 4);
+  const int nblk = K / BLK, nch = ceil_div(K, kChunkCodes);
   uint32_t cs;
   asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
   const int S = (int)cs;
   const int rank = (int)cluster_ctarank();
   const int ch_slice = ceil_div(nch, S);
   const int cbeg = min(rank * ch_slice, nch), cend = min(cbeg + ch_slice, nch);
-  const int blk0 = 4 * cbeg, blk1 = min(4 * cend, nblk);
+  const int mych = cend - cbeg;                    // stages per tile in my slice
+  const int blk0 = cbeg * NBC, blk1 = min(cend * NBC, nblk);
   const int kbeg = blk0 * BLK;
-  const int nbs = blk1 - blk0;
-  const int mych = cend - cbeg;
-  const int nbs_pad = 4 * mych;
-  const GemvSmem L = gemv_smem_layout(W, K, S, a.n_out, a.tiles_per_group);
-  const uint32_t stages_s = smem_u32(smem + L.stages);
-  const uint32_t bars_s = smem_u32(smem + L.bars);
+  const int nbs = blk1 - blk0;                     // real blocks in my slice
+  const int nbs_pad = mych * NBC;
+  const GemvSmem L = gemv_smem_layout(W, ZEROS, K, a.G, S, a.n_out, a.ldo, a.tiles_per_group);
+  const int spitch = scale_pitch(a.G);
   uint8_t* tbl = smem + L.tbl;
   __half* xs = reinterpret_cast<__half*>(smem + L.xs);
-  float* sF = reinterpret_cast<float*>(smem + L.meta);
-  float* sT = sF + 4 * ch_slice;
-  float* sS = sT + 4 * ch_slice;
+  float2* sFT = reinterpret_cast<float2*>(smem + L.meta);  // (2^-E/64, c0*sum x) per block
+  float* sS = reinterpret_cast<float*>(smem + L.meta) + 2 * nbs_pad;
   float* xo = reinterpret_cast<float*>(smem + L.xo);
   float* afin_sum = reinterpret_cast<float*>(smem + L.afin);
   float* fin = reinterpret_cast<float*>(smem + L.fin);
-  uint8_t* zblk = smem + L.zblk;
+  uint8_t* zblk = smem + L.zblk + 64;
+  const uint32_t ov_bar = smem_u32(smem + L.bars);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ntiles = ceil_div(N, kRows);
   const int tile0 = group * a.tiles_per_group;
   const int gtiles = max(0, min(a.tiles_per_group, ntiles - tile0));
-  const int grows = gtiles * kRows;
-  const int fin_rows = ceil_div(a.tiles_per_group * kRows, S);
-  const int gshift = __ffs(a.G / BLK) - 1;  // G / BLK is a power of two
-  auto full_bar = [&](int w, int slot) { return bars_s + (uint32_t)((w * kSlots + slot) * 8); };
-  auto stage_addr = [&](int w, int slot) { return stages_s + (uint32_t)((w * kSlots + slot) * L.stage_bytes); };
-  auto tiles_of = [&](int w) { return w < gtiles ? ceil_div(gtiles - w, kCWarps) : 0; };
+  const int tpf = tiles_per_finisher(a.tiles_per_group, S);
+  const int fin_rows = tpf * kRows;
+  const int gshift = __ffs(a.G / BLK) - 1;         // G / BLK is a power of two
+  const int ngrp = K / a.G;                        // scale groups per row
 
   // Programmatic dependent launch: let the next kernel in the stream start launching now
   // (no-op without the launch attribute).  Everything this kernel reads from its
   // predecessor's output comes after griddepcontrol.wait below.
   pdl_trigger();
-  if (tid == 0) {
-    for (int i = 0; i < kCWarps * kSlots; ++i) mbar_init(bars_s + i * 8, 1);  // expect_tx arrive (+ TMA bytes)
-    mbar_fence_init();
+
+  // Rows this CTA finishes: local rows [rank*fin_rows, +nfin) of the group.
+  const int frow0 = tile0 * kRows + rank * fin_rows;
+  const int nfin = max(0, min(min(fin_rows, gtiles * kRows - rank * fin_rows), N - frow0));
+  // Anchor weights of those rows: one bulk copy of the contiguous byte range, widened to
+  // 16-byte boundaries (the widening stays inside the 16-byte segments that hold the first
+  // and last bytes, so it never leaves mapped memory).
+  const bool ov_smem = a.n_out > 0 && L.ov_bytes > 0 && nfin > 0;
+  uint32_t ov_skew = 0;
+  if (ov_smem) {
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(a.ovals + (int64_t)frow0 * a.ldo);
+    const uintptr_t hi = reinterpret_cast<uintptr_t>(a.ovals + (int64_t)(frow0 + nfin - 1) * a.ldo + a.n_out);
+    const uintptr_t lo16 = lo & ~(uintptr_t)15, hi16 = (hi + 15) & ~(uintptr_t)15;
+    ov_skew = (uint32_t)(lo - lo16);
+    if (tid == 0) {
+      mbar_init(ov_bar, 1);
+      mbar_fence_init();
+      mbar_arrive_expect_tx(ov_bar, (uint32_t)(hi16 - lo16));
+      bulk_load(smem_u32(smem + L.ov), reinterpret_cast<const void*>(lo16), (uint32_t)(hi16 - lo16), ov_bar);
+    }
   }
-  __syncthreads();
   cluster_arrive_relaxed();  // paired with cluster_wait() before the first DSMEM store
 
-  // Stage k of warp w = (tile w + 8*(k / mych), chunk k % mych of my slice).  Lane 0 of
-  // the warp issues its TMA into slot k % kSlots and refills the slot once consumed; the
-  // issue cursor (slot, chunk, tile row) advances without divisions.
-  const int my_tiles = tiles_of(warp);
+  // Stage k of warp w = (tile w + 8*(k / mych), chunk cbeg + k % mych).  Each lane copies
+  // four 16-byte pieces of codes (rows lane/8 + 4i, bytes 16*(lane%8)) and its share of
+  // the stage's scales (and zero points) as 4-byte pieces; one commit group per stage.
+  const int my_tiles = warp < gtiles ? ceil_div(gtiles - warp, kCWarps) : 0;
   const int nst = my_tiles * mych;
-  int is_slot = 0, is_cc = 0, is_row = (tile0 + warp) * kRows;
-  auto issue_next = [&]() {
-    const uint32_t fb = full_bar(warp, is_slot);
-    mbar_arrive_expect_tx(fb, kRows * CB);
-    tma_load_2d(stage_addr(warp, is_slot), tmp, (cbeg + is_cc) * CB, is_row, fb);
-    if (++is_slot == kSlots) is_slot = 0;
+  uint8_t* const wstages = smem + L.stages + (int64_t)warp * kSlots * L.stage_bytes;
+  const int sgr = kChunkCodes / a.G;               // scale groups per stage row (2..16)
+  const int lspr = __ffs(sgr) - 2;                 // log2 of the 4-byte scale pieces per row
+  const int kbytes = K / 4;
+  // Issue cursor: chunk within the slice, tile, and per-tile row state.
+  int is_cc = 0, is_tile = 0, irow0 = 0;
+  const uint8_t* ip = a.packed;                    // row irow0 + lane/8, byte 16*(lane%8)
+  uint32_t ivalid = 0;                             // bit i: row irow0 + lane/8 + 4i exists
+  const int64_t ldp4 = 4 * a.ldp;
+  auto issue_tile = [&]() {
+    irow0 = (tile0 + warp + kCWarps * is_tile) * kRows;
+    const int r0 = irow0 + (lane >> 3);
+    ip = a.packed + (int64_t)min(r0, N - 1) * a.ldp + 16 * (lane & 7);
+    ivalid = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ivalid |= (r0 + 4 * i < N ? 1u : 0u) << i;
+  };
+  auto issue = [&](int slot) {
+    uint8_t* d = wstages + slot * L.stage_bytes;
+    const int cb = (cbeg + is_cc) * kChunk;        // byte offset of the chunk in a row
+    const int rem = kbytes - cb - 16 * (lane & 7);
+    const uint32_t kb = (uint32_t)max(0, min(16, rem));
+    const uint8_t* src = ip + cb;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = (lane >> 3) + 4 * i;
+      const bool on = ((ivalid >> i) & 1u) && kb > 0;
+      cp_async16(smem_u32(d + r * kPitch + 16 * (lane & 7)), on ? src + i * ldp4 : a.packed, on ? kb : 0u);
+    }
+    const int g0 = (cbeg + is_cc) * sgr;           // first scale group of the chunk
+    for (int p = lane; p < (kRows << lspr); p += 32) {
+      const int r = p >> lspr, q = p & ((1 << lspr) - 1);
+      const int grp = g0 + 2 * q;
+      const bool on = irow0 + r < N && grp < ngrp;
+      const uint32_t nb = on ? (uint32_t)min(2 * (ngrp - grp), 4) : 0u;
+      const int64_t ro = on ? (int64_t)(irow0 + r) : 0;
+      cp_async4(smem_u32(d + L.stage_scales + r * spitch + 4 * q), a.scales + (on ? ro * a.lds + grp : 0), nb);
+      if constexpr (ZEROS)
+        cp_async4(smem_u32(d + L.stage_zeros + r * spitch + 4 * q), a.zeros + (on ? ro * a.ldz + grp : 0), nb);
+    }
     if (++is_cc == mych) {
       is_cc = 0;
-      is_row += kCWarps * kRows;
+      ++is_tile;
+      issue_tile();
     }
   };
-  if (lane == 0)
-    for (int k = 0; k < min(kSlots, nst); ++k) issue_next();
-  const int g = lane >> 2, t = lane & 3;
-  // Parameter cursor: per-tile row pointers, per-stage group index.
-  int lt = 0, lc = 0;
-  const uint16_t* sp0 = nullptr;
-  const uint16_t* sp1 = nullptr;
-  const uint16_t* zp0 = nullptr;
-  const uint16_t* zp1 = nullptr;
-  bool pv0 = false, pv1 = false;
-  auto param_tile = [&]() {
-    const int rg = (tile0 + warp + kCWarps * lt) * kRows + g;
-    pv0 = lt < my_tiles && rg < N;
-    pv1 = lt < my_tiles && rg + 8 < N;
-    sp0 = a.scales + (pv0 ? (int64_t)rg * a.lds : 0);
-    sp1 = a.scales + (pv1 ? (int64_t)(rg + 8) * a.lds : 0);
-    if constexpr (ZEROS) {
-      zp0 = a.zeros + (pv0 ? (int64_t)rg * a.ldz : 0);
-      zp1 = a.zeros + (pv1 ? (int64_t)(rg + 8) * a.ldz : 0);
-    }
-  };
-  auto load_params = [&](uint32_t& s0, uint32_t& s1, uint32_t& z0, uint32_t& z1) {
-    const int blk = 4 * (cbeg + lc) + t;
-    const bool inb = blk < nblk;
-    const int grp = inb ? (blk >> gshift) : 0;
-    s0 = s1 = 0u;
-    ld_u16_pred(s0, sp0 + grp, pv0 && inb);
-    ld_u16_pred(s1, sp1 + grp, pv1 && inb);
-    z0 = z1 = 0u;
-    if constexpr (ZEROS) {
-      ld_u16_pred(z0, zp0 + grp, pv0 && inb);
-      ld_u16_pred(z1, zp1 + grp, pv1 && inb);
-    }
-    if (++lc == mych) {
-      lc = 0;
-      ++lt;
-      param_tile();
-    }
-  };
-  param_tile();
-  uint32_t rs0[kSlots], rs1[kSlots], rz0[kSlots], rz1[kSlots];
+  issue_tile();
 #pragma unroll
-  for (int s = 0; s < kSlots; ++s) load_params(rs0[s], rs1[s], rz0[s], rz1[s]);
+  for (int k = 0; k < kSlots; ++k) {
+    if (k < nst) issue(k);
+    cp_async_commit();
+  }
+
+  const int g = lane >> 2, t = lane & 3;
   {
-    // Epilogue inputs of the rows this CTA finishes (rank + S*i of the group).
-    const int fr = rank + S * tid;
-    const int frow = tile0 * kRows + fr;
-    const bool fin_ok = fr < grows && frow < N;
+    // Epilogue inputs of the rows this CTA finishes: thread i takes row frow0 + i.
+    const bool fin_ok = tid < nfin;
+    const int frow = frow0 + tid;
     float ep = 0.0f;
     if (fin_ok && a.bias) ep += h2f(ldg_u16(a.bias + frow));
+    // Anchor columns (independent of the predecessor): thread j < n_out holds column j.
+    int kcol = 0;
+    if (tid < a.n_out) kcol = (int)__ldg(a.oidx + tid);
     // Weights, scales and bias are in flight; from here on we read the predecessor's output.
     pdl_wait();
     if (fin_ok && a.res) ep += h2f(ldg_u16(a.res + frow));
+    // x at this thread's anchor column (and the transform's second operand there), issued
+    // together with the staging loads below.
+    uint32_t x_k = 0u, xaux_k = 0u;
+    ld_u16_pred(x_k, a.x + kcol, tid < a.n_out);
+    ld_u16_pred(xaux_k, a.xaux + kcol, tid < a.n_out && a.xaux != nullptr && a.xop != OTF_XOP_NONE);
     // Stage my slice of x (fp16); padded tail = 0.  The SiLU gate and the mask apply on the
     // way in; RMSNorm first needs the sum of squares of all K, combined across the cluster
     // (the K slices partition K) over distributed shared memory, then a second pass.
@@ -348,29 +396,15 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const CUtensorMap
       }
     }
     // Anchor activations: the transformed, unmasked x at the anchor columns.
-    for (int j = tid; j < a.n_out; j += kCThreads) {
+    if (tid < a.n_out)
+      xo[tid] = __half2float(xform_v(__ushort_as_half((uint16_t)x_k), a.xop, (uint16_t)xaux_k, a.xaux != nullptr, rnorm));
+    for (int j = tid + kCThreads; j < a.n_out; j += kCThreads) {
       const int k = (int)__ldg(a.oidx + j);
-      xo[j] = __half2float(xform(__ushort_as_half(ldg_u16(a.x + k)), a.xop, a.xaux, k, rnorm));
+      const uint16_t av = (a.xaux && a.xop != OTF_XOP_NONE) ? ldg_u16(a.xaux + k) : (uint16_t)0;
+      xo[j] = __half2float(xform_v(__ushort_as_half(ldg_u16(a.x + k)), a.xop, av, a.xaux != nullptr, rnorm));
     }
-    for (int i = tid; i < SL / 4; i += kCThreads) reinterpret_cast<uint32_t*>(zblk)[i] = 0u;
-    named_barrier_sync(1, kCThreads);
-    // Anchor dot products of the rows this CTA finishes: warp w takes finished-row slots
-    // i = w, w+8, ...; lanes stride over the anchors of the row (contiguous fp16), a
-    // shuffle reduction sums them, and the owning thread's epilogue term receives it.
-    {
-      const int nfin = ceil_div(grows - rank, S);  // finished rows of this CTA
-      for (int i = warp; i < nfin; i += kCWarps) {
-        const int row = tile0 * kRows + rank + S * i;
-        float d = 0.0f;
-        if (row < N) {
-          const uint16_t* ov = a.ovals + (int64_t)row * a.ldo;
-          for (int j = lane; j < a.n_out; j += 32) d = fmaf(xo[j], h2f(ldg_u16(ov + j)), d);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        if (lane == 0) afin_sum[i] = d;
-      }
-    }
+    for (int i = tid; i < 32; i += kCThreads) reinterpret_cast<uint32_t*>(zblk)[i] = 0u;
+    named_barrier_sync(1, kCThreads);  // the staged slice of x is complete
     // Quantise the table slice: 4W lanes per block, lane (w, j) owns codes 16w+4i+j.
     {
       constexpr int LPB = 4 * W;
@@ -412,21 +446,33 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const CUtensorMap
           *reinterpret_cast<uint2*>(e + SL) =
               make_uint2(pack4(ll[0], ll[1], ll[2], ll[3]), pack4(lh[0], lh[1], lh[2], lh[3]));
           if (l == 0) {
-            sF[bi] = exp2i(-E) * (1.0f / 64.0f);
-            sT[bi] = a.c0 * sx;
+            sFT[bi] = make_float2(exp2i(-E) * (1.0f / 64.0f), a.c0 * sx);
             sS[bi] = sx;
           }
         }
       }
     }
     named_barrier_sync(1, kCThreads);
+    // Anchor dot products of the rows this CTA finishes, one row per thread, from the
+    // weights the bulk copy brought in (or from global memory when they did not fit).
+    if (a.n_out > 0 && tid < nfin) {
+      float d = 0.0f;
+      if (ov_smem) {
+        if (!mbar_wait(ov_bar, 0u)) report_wait_failure();
+        const uint16_t* ovr = reinterpret_cast<const uint16_t*>(smem + L.ov + ov_skew) + (int64_t)tid * a.ldo;
+        for (int j = 0; j < a.n_out; ++j) d = fmaf(xo[j], h2f(ovr[j]), d);
+      } else {
+        const uint16_t* ovr = a.ovals + (int64_t)(frow0 + tid) * a.ldo;
+        for (int j = 0; j < a.n_out; ++j) d = fmaf(xo[j], h2f(ldg_u16(ovr + j)), d);
+      }
+      afin_sum[tid] = d;
+    }
 
-    // Main loop: my tiles tl = warp + 8*i, their chunks in order, one stage each.  The
-    // scales (and zero points) of stage k + kSlots are fetched into a register ring while
-    // stage k is consumed.
+    // Main loop: my tiles tl = warp + 8*i, their chunks in order, one stage each.
     const bool breal = (g >> 1) == t;
-    const uint8_t* bbase = breal ? (tbl + (g >> 1) * SB + (g & 1) * SL) : zblk;
-    const int bstep = breal ? 4 * SB : 0;
+    const uint8_t* bbase = breal ? (tbl + t * NBT * SB + (g & 1) * SL) : zblk;
+    const int bstep = breal ? NBC * SB : 0;         // next chunk
+    const int sstep = breal ? SB : 0;               // next set
     float p0 = 0.0f, p1 = 0.0f;
     int cc = 0, ct = 0;
     for (int base = 0; base < nst; base += kSlots) {
@@ -434,83 +480,82 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const CUtensorMap
       for (int s = 0; s < kSlots; ++s) {
         const int k = base + s;
         if (k < nst) {
-          if (!mbar_wait(full_bar(warp, s), (uint32_t)(base / kSlots) & 1u)) report_wait_failure();
-          const uint8_t* st = smem + L.stages + (warp * kSlots + s) * L.stage_bytes;
-          uint32_t cw[W], cw8[W];
-          if constexpr (W == 4) {
-            const uint4 v = *reinterpret_cast<const uint4*>(st + g * CB + t * 16);
-            const uint4 v8 = *reinterpret_cast<const uint4*>(st + (g + 8) * CB + t * 16);
-            cw[0] = v.x; cw[1] = v.y; cw[2] = v.z; cw[3] = v.w;
-            cw8[0] = v8.x; cw8[1] = v8.y; cw8[2] = v8.z; cw8[3] = v8.w;
-          } else {
-            const uint2 v = *reinterpret_cast<const uint2*>(st + g * CB + t * 8);
-            const uint2 v8 = *reinterpret_cast<const uint2*>(st + (g + 8) * CB + t * 8);
-            cw[0] = v.x; cw[1] = v.y;
-            cw8[0] = v8.x; cw8[1] = v8.y;
-          }
-          const float sg = h2f((uint16_t)rs0[s]), sg8 = h2f((uint16_t)rs1[s]);
-          const float zg = h2f((uint16_t)rz0[s]), zg8 = h2f((uint16_t)rz1[s]);
-          load_params(rs0[s], rs1[s], rz0[s], rz1[s]);
-
+          cp_async_wait<kSlots - 1>();
+          __syncwarp();
+          const uint8_t* st = wstages + s * L.stage_bytes;
+          // Codes of rows g and g+8, bytes [32t, 32t+32): words of blocks t*NBT .. +NBT.
+          const uint4 va = *reinterpret_cast<const uint4*>(st + g * kPitch + 32 * t);
+          const uint4 vb = *reinterpret_cast<const uint4*>(st + g * kPitch + 32 * t + 16);
+          const uint4 vc = *reinterpret_cast<const uint4*>(st + (g + 8) * kPitch + 32 * t);
+          const uint4 vd = *reinterpret_cast<const uint4*>(st + (g + 8) * kPitch + 32 * t + 16);
+          const uint32_t cw[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+          const uint32_t cw8[8] = {vc.x, vc.y, vc.z, vc.w, vd.x, vd.y, vd.z, vd.w};
+          const uint16_t* ssc = reinterpret_cast<const uint16_t*>(st + L.stage_scales);
+          const uint16_t* szr = reinterpret_cast<const uint16_t*>(st + L.stage_zeros);
           const uint8_t* bp = bbase + cc * bstep;
-          int C[4][4];
 #pragma unroll
-          for (int w = 0; w < W; ++w) {
+          for (int set = 0; set < NBT; ++set) {
+            int C[4][4];
 #pragma unroll
-            for (int jp = 0; jp < 4; jp += 2) {
-              const uint4 bq = *reinterpret_cast<const uint4*>(bp + (w * 4 + jp) * 8);
+            for (int w = 0; w < W; ++w) {
+              const uint32_t aw = cw[set * W + w], aw8 = cw8[set * W + w];
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int j = jp + h;
-                const uint32_t b0 = h ? bq.z : bq.x, b1 = h ? bq.w : bq.y;
-                const uint32_t ml = 0x01010101u << (2 * j), mh = 0x02020202u << (2 * j);
-                if (w == 0)
-                  mma_u8s8_z(C[j], cw[w] & ml, cw8[w] & ml, cw[w] & mh, cw8[w] & mh, b0, b1);
-                else
-                  mma_u8s8(C[j], cw[w] & ml, cw8[w] & ml, cw[w] & mh, cw8[w] & mh, b0, b1);
+              for (int jp = 0; jp < 4; jp += 2) {
+                const uint4 bq = *reinterpret_cast<const uint4*>(bp + set * sstep + (w * 4 + jp) * 8);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const int j = jp + h;
+                  const uint32_t b0 = h ? bq.z : bq.x, b1 = h ? bq.w : bq.y;
+                  const uint32_t ml = 0x01010101u << (2 * j), mh = 0x02020202u << (2 * j);
+                  if (w == 0)
+                    mma_u8s8_z(C[j], aw & ml, aw8 & ml, aw & mh, aw8 & mh, b0, b1);
+                  else
+                    mma_u8s8(C[j], aw & ml, aw8 & ml, aw & mh, aw8 & mh, b0, b1);
+                }
               }
             }
-          }
-          {
-            const int lb = 4 * cc + t;
+            const int lb = cc * NBC + t * NBT + set;     // my block within the slice
+            const int gi = (t * NBT + set) >> gshift;     // its scale group within the stage
+            const float sg = h2f(ssc[g * (spitch / 2) + gi]), sg8 = h2f(ssc[(g + 8) * (spitch / 2) + gi]);
             int v[4];
 #pragma unroll
             for (int f = 0; f < 4; ++f) v[f] = ((C[0][f] * 4 + C[1][f]) * 4 + C[2][f]) * 4 + C[3][f];
-            const float F = sF[lb], T = sT[lb];
-            p0 = fmaf(sg, fmaf((float)(v[0] * 256 + v[1]), F, T), p0);
-            p1 = fmaf(sg8, fmaf((float)(v[2] * 256 + v[3]), F, T), p1);
+            const float2 FT = sFT[lb];
+            p0 = fmaf(sg, fmaf((float)(v[0] * 256 + v[1]), FT.x, FT.y), p0);
+            p1 = fmaf(sg8, fmaf((float)(v[2] * 256 + v[3]), FT.x, FT.y), p1);
             if constexpr (ZEROS) {
               const float Sx = sS[lb];
-              p0 = fmaf(zg, Sx, p0);
-              p1 = fmaf(zg8, Sx, p1);
+              p0 = fmaf(h2f(szr[g * (spitch / 2) + gi]), Sx, p0);
+              p1 = fmaf(h2f(szr[(g + 8) * (spitch / 2) + gi]), Sx, p1);
             }
           }
-          // The slot's codes have been consumed by every lane (the MMAs above used them):
-          // refill it with stage k + kSlots.
+          // Every lane has read the slot (its values fed the MMAs above): refill it.
           __syncwarp();
-          if (lane == 0 && k + kSlots < nst) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue_next();
-          }
+          if (k + kSlots < nst) issue(s);
           if (++cc == mych) {
-            const int lrow = (warp + kCWarps * ct) * kRows + g;
+            // Tile done: reduce over the lane quad and push the K-partials of rows g, g+8
+            // to the CTA that finishes this tile.
+            const int tl = warp + kCWarps * ct;
+            const int q = tl / tpf;
+            const int slot = (tl - q * tpf) * kRows + g;
             p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
             p0 += __shfl_xor_sync(0xffffffffu, p0, 2);
             p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
             p1 += __shfl_xor_sync(0xffffffffu, p1, 2);
             if (t == 0) {
-              const uint32_t f0 = smem_u32(fin + rank * fin_rows + lrow / S);
-              const uint32_t f1 = smem_u32(fin + rank * fin_rows + (lrow + 8) / S);
-              st_cluster_f32_plain(mapa_shared(f0, (uint32_t)(lrow % S)), p0);
-              st_cluster_f32_plain(mapa_shared(f1, (uint32_t)((lrow + 8) % S)), p1);
+              const uint32_t f0 = smem_u32(fin + rank * fin_rows + slot);
+              st_cluster_f32_plain(mapa_shared(f0, (uint32_t)q), p0);
+              st_cluster_f32_plain(mapa_shared(f0 + 8 * 4, (uint32_t)q), p1);
             }
             p0 = p1 = 0.0f;
             cc = 0;
             ++ct;
           }
         }
+        cp_async_commit();
       }
     }
+    cp_async_wait<0>();
     // One cluster barrier below: every partial has landed in its finisher's shared memory.
     cluster_sync_all();
     if (fin_ok) {
@@ -523,11 +568,10 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const CUtensorMap
 }
 
 template <int W, bool ZEROS>
-__global__ void __launch_bounds__(kThreads, 2)
-k_gemv2b(const __grid_constant__ LinearArgs a, const __grid_constant__ CUtensorMap tm) {
+__global__ void __launch_bounds__(kThreads, 2) k_gemv2b(const __grid_constant__ LinearArgs a) {
   uint32_t cs;
   asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
-  gemv_body<W, ZEROS>(a, &tm, (int)(blockIdx.x / cs));
+  gemv_body<W, ZEROS>(a, (int)(blockIdx.x / cs));
 }
 
 template <int W, bool ZEROS>
@@ -537,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv2b_group(const __grid_const
   const int cid = (int)(blockIdx.x / cs);
   int m = 0;
   while (m + 1 < gp.n && cid >= gp.prefix[m + 1]) ++m;
-  gemv_body<W, ZEROS>(gp.L[m], &gp.tm[m], cid - gp.prefix[m]);
+  gemv_body<W, ZEROS>(gp.L[m], cid - gp.prefix[m]);
 }
 
 // Portable CUDA-core kernel: any M, any G dividing K with G % 4 == 0, any codebook.
@@ -641,26 +685,26 @@ struct GemvPlan {
   int64_t smem;
 };
 
-template <int W>
 static int gemv_S(int K) {
-  const int nblk = K / (16 * W), nch = ceil_div(nblk, 4);
-  int S = std::max(1, std::min(kMaxCluster, nch / 2));
+  const int nch = ceil_div(K, kChunkCodes);
+  int S = std::max(1, std::min(kMaxCluster, nch));
   while (S > 1 && ceil_div(nch, S) * (S - 1) >= nch) --S;  // every slice non-empty
   return S;
 }
 
-// Row groups for a layer given a budget of clusters: every consumer warp holds at least
-// one tile, and each of the S*256 threads of a cluster finishes at most one row.
+// Row groups for a layer given a budget of clusters: every warp holds at least one tile,
+// and each CTA finishes at most one row per thread.
 template <int W>
 static GemvPlan gemv_plan(const LinearArgs& a, int S, int budget) {
   GemvPlan p;
   p.S = S;
   const int ntiles = ceil_div(a.N, kRows);
-  const int min_groups = std::max(1, ceil_div(ntiles * kRows, S * kCThreads));
+  const int max_tpg = S * (kCThreads / kRows);
+  const int min_groups = std::max(1, ceil_div(ntiles, max_tpg));
   int groups = std::max(min_groups, std::min(std::max(budget, 1), ceil_div(ntiles, kCWarps)));
   p.tpg = ceil_div(ntiles, groups);
   p.groups = ceil_div(ntiles, p.tpg);
-  p.smem = gemv_smem_layout(W, a.K, S, a.n_out, p.tpg).total;
+  p.smem = gemv_smem_layout(W, a.zeros != nullptr, a.K, a.G, S, a.n_out, a.ldo, p.tpg).total;
   return p;
 }
 
@@ -699,59 +743,6 @@ static int max_active_clusters(int S, int64_t smem) {
   return mc;
 }
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_tiled_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, []() {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-    cudaGetLastError();
-  });
-  return fn;
-}
-
-// Tensor map of a packed code matrix: uint8 [rows, cols] with row stride ld bytes, box
-// [box_cols bytes, 16 rows], no swizzle (the 64/32-byte row pitch of a box is already
-// conflict-free for the consumers' 16/8-byte reads), zero fill out of bounds.
-static bool code_tensor_map(CUtensorMap* out, const uint8_t* base, int64_t rows, int64_t cols, int64_t ld,
-                            int box_cols) {
-  static std::mutex mu;
-  static std::map<std::tuple<const void*, int64_t, int64_t, int64_t, int>, CUtensorMap> cache;
-  const auto key = std::make_tuple((const void*)base, rows, cols, ld, box_cols);
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    auto it = cache.find(key);
-    if (it != cache.end()) {
-      *out = it->second;
-      return true;
-    }
-  }
-  EncodeTiledFn fn = encode_tiled_fn();
-  if (!fn) return false;
-  CUtensorMap m;
-  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)ld};
-  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)kRows};
-  const cuuint32_t estr[2] = {1, 1};
-  if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
-         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return false;
-  std::lock_guard<std::mutex> lk(mu);
-  if (cache.size() > 65536) cache.clear();
-  cache[key] = m;
-  *out = m;
-  return true;
-}
-
 template <int W, bool ZEROS>
 static int configure_kernels() {
   static thread_local int configured_dev[64] = {};
@@ -771,9 +762,7 @@ template <int W, bool ZEROS>
 static int launch_gemv(LinearArgs a, cudaStream_t st) {
   int rc = configure_kernels<W, ZEROS>();
   if (rc != OTF_OK) return rc;
-  CUtensorMap tm;
-  if (!code_tensor_map(&tm, a.packed, a.N, a.K / 4, a.ldp, 16 * W)) return OTF_ERR_UNSUPPORTED;
-  const int S = gemv_S<W>(a.K);
+  const int S = gemv_S(a.K);
   // No more clusters than can be resident at once: a second wave would double the time.
   GemvPlan p = gemv_plan<W>(a, S, 1 << 20);
   for (int pass = 0; pass < 3; ++pass) {
@@ -782,10 +771,10 @@ static int launch_gemv(LinearArgs a, cudaStream_t st) {
     if (q.groups == p.groups) break;
     p = q;
   }
-  if (p.smem > 227 * 1024 || p.tpg * kRows > S * kCThreads) return OTF_ERR_UNSUPPORTED;
+  if (p.smem > 227 * 1024 || tiles_per_finisher(p.tpg, S) * kRows > kCThreads) return OTF_ERR_UNSUPPORTED;
   a.tiles_per_group = p.tpg;
   return set_cuda_error(launch_pdl(k_gemv2b<W, ZEROS>, dim3((unsigned)(p.groups * S)), dim3(kThreads),
-                                   (size_t)p.smem, st, (unsigned)S, a, tm));
+                                   (size_t)p.smem, st, (unsigned)S, a));
 }
 
 // Layers with the same K, G and zero-point use launched as one grid: cluster budgets are
@@ -796,11 +785,10 @@ static int launch_gemv_group(LinearArgs* L, int n, cudaStream_t st) {
   if (rc != OTF_OK) return rc;
   static thread_local GroupParams gp;  // large: keep it off the host stack
   gp.n = n;
-  const int S = gemv_S<W>(L[0].K);
+  const int S = gemv_S(L[0].K);
   int64_t smem_hi = 0;
   int tiles_total = 0;
   for (int m = 0; m < n; ++m) {
-    if (!code_tensor_map(&gp.tm[m], L[m].packed, L[m].N, L[m].K / 4, L[m].ldp, 16 * W)) return OTF_ERR_UNSUPPORTED;
     tiles_total += ceil_div(L[m].N, kRows);
     smem_hi = std::max(smem_hi, gemv_plan<W>(L[m], S, 1 << 20).smem);
   }
@@ -821,7 +809,7 @@ static int launch_gemv_group(LinearArgs* L, int n, cudaStream_t st) {
   }
   int clusters = 0;
   for (int m = 0; m < n; ++m) {
-    if (plans[m].tpg * kRows > S * kCThreads) return OTF_ERR_UNSUPPORTED;
+    if (tiles_per_finisher(plans[m].tpg, S) * kRows > kCThreads) return OTF_ERR_UNSUPPORTED;
     gp.L[m] = L[m];
     gp.L[m].tiles_per_group = plans[m].tpg;
     gp.prefix[m] = clusters;
@@ -896,19 +884,21 @@ static int build_args(LinearArgs& a, const void* x, int64_t ldx, const uint8_t* 
   return OTF_OK;
 }
 
-// Which tensor-pipe variant serves these arguments: 4 (G % 64), 2 (G % 32) or 0 (none).
-// It needs c3 - c2 == c1 - c0 (affine in the two code bits), batch 1, a block of 16W codes
-// inside one scale group, and aligned rows and vectors.
+// Which tensor-pipe variant serves these arguments: 4 (G % 64), 2 (G == 32) or 0 (none).
+// It needs c3 - c2 == c1 - c0 (affine in the two code bits), batch 1, G a power-of-two
+// multiple of the 16W-code block with at least two groups per 512-code stage, 16-byte
+// aligned code rows, 4-byte aligned scale rows and 16-byte aligned activation vectors.
 static int fast_variant(const LinearArgs& a, uint32_t flags) {
   const auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
   const float lhs = a.c3 - a.c2, rhs = a.c1 - a.c0;
   const bool affine = fabsf(lhs - rhs) <= 1e-6f * fmaxf(1.0f, fabsf(rhs));
   const auto al = [](const void* p, int n) { return reinterpret_cast<uintptr_t>(p) % n == 0; };
   const bool vec_ok = al(a.x, 16) && (!a.mask || al(a.mask, 16)) && (!a.xaux || al(a.xaux, 16)) && al(a.scales, 4) &&
-                      (!a.zeros || al(a.zeros, 4));
-  if ((flags & OTF_FLAG_FORCE_GENERIC) || !affine || a.M != 1 || !vec_ok || a.K % 8) return 0;
-  if (a.G % 64 == 0 && pow2(a.G / 64) && al(a.packed, 16) && a.ldp % 16 == 0) return 4;
-  if (a.G % 32 == 0 && pow2(a.G / 32) && al(a.packed, 8) && a.ldp % 8 == 0) return 2;
+                      a.lds % 2 == 0 && (!a.zeros || (al(a.zeros, 4) && a.ldz % 2 == 0)) && al(a.packed, 16) &&
+                      a.ldp % 16 == 0 && a.K % 8 == 0;
+  if ((flags & OTF_FLAG_FORCE_GENERIC) || !affine || a.M != 1 || !vec_ok || !pow2(a.G) || a.G > 256) return 0;
+  if (a.G >= 64) return 4;
+  if (a.G == 32) return 2;
   return 0;
 }
 
