@@ -53,6 +53,10 @@ constexpr int kChunk = 128;                 // code bytes per row per stage (512
 constexpr int kChunkCodes = 4 * kChunk;
 constexpr int kPitch = kChunk + 16;         // shared-memory row pitch of a stage
 constexpr int kMaxCluster = 8;              // K slices per cluster
+#ifndef OTF_GEMV_MIN_CTAS
+#define OTF_GEMV_MIN_CTAS 2
+#endif
+constexpr int kMinCtas = OTF_GEMV_MIN_CTAS;  // resident CTAs per SM the register budget targets
 constexpr int kOvMax = 32 * 1024;           // largest anchor-weight block staged in shared memory
 
 __device__ int g_otf_device_error;          // set when a bounded wait gives up
@@ -177,11 +181,22 @@ __device__ __forceinline__ __half xform_v(__half x, int xop, uint16_t aux_v, boo
   return x;
 }
 
-template <int W, bool ZEROS>
+// Words per 16W-code block for group size G (the block never straddles a group).
+__host__ __device__ constexpr int words_for(int G) { return G >= 64 ? 4 : 2; }
+
+template <int G, bool ZEROS>
 __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) {
+  constexpr int W = words_for(G);
   constexpr int BLK = 16 * W, SL = tbl_sl(W), SB = tbl_sb(W);
   constexpr int NBC = kChunkCodes / BLK;           // blocks per stage row (8 or 16)
   constexpr int NBT = NBC / 4;                     // blocks per lane quad = MMA sets per stage
+  constexpr int GSHIFT = G == 32 ? 0 : (G == 64 ? 0 : (G == 128 ? 1 : 2));  // log2(G / BLK)
+  constexpr int SGR = kChunkCodes / G;             // scale groups per stage row (2..16)
+  constexpr int SPITCH = 2 * SGR + 4;              // bytes of scales per stage row (padded)
+  static_assert(G == 32 || G == 64 || G == 128 || G == 256, "group size");
+  constexpr int kStageScales = kRows * kPitch;     // stage layout: codes, scales, zero points
+  constexpr int kStageZeros = kStageScales + kRows * SPITCH;
+  constexpr int kStageBytes = kStageZeros + (ZEROS ? kRows * SPITCH : 0);
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.K, N = a.N;
   const int nblk = K / BLK, nch = ceil_div(K, kChunkCodes);
@@ -196,8 +211,7 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
   const int kbeg = blk0 * BLK;
   const int nbs = blk1 - blk0;                     // real blocks in my slice
   const int nbs_pad = mych * NBC;
-  const GemvSmem L = gemv_smem_layout(W, ZEROS, K, a.G, S, a.n_out, a.ldo, a.tiles_per_group);
-  const int spitch = scale_pitch(a.G);
+  const GemvSmem L = gemv_smem_layout(W, ZEROS, K, G, S, a.n_out, a.ldo, a.tiles_per_group);
   uint8_t* tbl = smem + L.tbl;
   __half* xs = reinterpret_cast<__half*>(smem + L.xs);
   float2* sFT = reinterpret_cast<float2*>(smem + L.meta);  // (2^-E/64, c0*sum x) per block
@@ -214,8 +228,7 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
   const int gtiles = max(0, min(a.tiles_per_group, ntiles - tile0));
   const int tpf = tiles_per_finisher(a.tiles_per_group, S);
   const int fin_rows = tpf * kRows;
-  const int gshift = __ffs(a.G / BLK) - 1;         // G / BLK is a power of two
-  const int ngrp = K / a.G;                        // scale groups per row
+  const int ngrp = K / G;                          // scale groups per row
 
   // Programmatic dependent launch: let the next kernel in the stream start launching now
   // (no-op without the launch attribute).  Everything this kernel reads from its
@@ -244,50 +257,63 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
   }
   cluster_arrive_relaxed();  // paired with cluster_wait() before the first DSMEM store
 
-  // Stage k of warp w = (tile w + 8*(k / mych), chunk cbeg + k % mych).  Each lane copies
-  // four 16-byte pieces of codes (rows lane/8 + 4i, bytes 16*(lane%8)) and its share of
-  // the stage's scales (and zero points) as 4-byte pieces; one commit group per stage.
+  // Stage k of warp w = (tile w + 8*(k / mych), chunk cbeg + k % mych).  Lane pair
+  // (2r, 2r+1) copies row r of the stage: lane half h takes code bytes [64h, 64h+64) as four
+  // 16-byte pieces and scale groups [h*SGR/2, (h+1)*SGR/2) as 4-byte pieces; one commit
+  // group per stage.
   const int my_tiles = warp < gtiles ? ceil_div(gtiles - warp, kCWarps) : 0;
   const int nst = my_tiles * mych;
-  uint8_t* const wstages = smem + L.stages + (int64_t)warp * kSlots * L.stage_bytes;
-  const int sgr = kChunkCodes / a.G;               // scale groups per stage row (2..16)
-  const int lspr = __ffs(sgr) - 2;                 // log2 of the 4-byte scale pieces per row
+  uint8_t* const wstages = smem + L.stages + warp * kSlots * kStageBytes;
   const int kbytes = K / 4;
-  // Issue cursor: chunk within the slice, tile, and per-tile row state.
-  int is_cc = 0, is_tile = 0, irow0 = 0;
-  const uint8_t* ip = a.packed;                    // row irow0 + lane/8, byte 16*(lane%8)
-  uint32_t ivalid = 0;                             // bit i: row irow0 + lane/8 + 4i exists
-  const int64_t ldp4 = 4 * a.ldp;
+  const int lr = lane >> 1, lh = lane & 1;
+  const uint32_t cdst0 = smem_u32(wstages) + lr * kPitch + 64 * lh;
+  const uint32_t sdst0 = smem_u32(wstages + kStageScales) + lr * SPITCH + lh * SGR;
+  const uint32_t zdst0 = smem_u32(wstages + kStageZeros) + lr * SPITCH + lh * SGR;
+  // Issue cursor: chunk within the slice and tile, with the tile's row pointers.
+  int is_cc = 0, is_tile = 0;
+  const uint8_t* crow = a.packed;
+  const uint16_t* srow = a.scales;
+  const uint16_t* zrow = a.zeros;
+  bool row_ok = false;
   auto issue_tile = [&]() {
-    irow0 = (tile0 + warp + kCWarps * is_tile) * kRows;
-    const int r0 = irow0 + (lane >> 3);
-    ip = a.packed + (int64_t)min(r0, N - 1) * a.ldp + 16 * (lane & 7);
-    ivalid = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) ivalid |= (r0 + 4 * i < N ? 1u : 0u) << i;
+    const int r = (tile0 + warp + kCWarps * is_tile) * kRows + lr;
+    row_ok = r < N;
+    const int64_t rr = row_ok ? r : 0;
+    crow = a.packed + rr * a.ldp + 64 * lh;
+    srow = a.scales + rr * a.lds + lh * (SGR / 2);
+    if constexpr (ZEROS) zrow = a.zeros + rr * a.ldz + lh * (SGR / 2);
   };
   auto issue = [&](int slot) {
-    uint8_t* d = wstages + slot * L.stage_bytes;
-    const int cb = (cbeg + is_cc) * kChunk;        // byte offset of the chunk in a row
-    const int rem = kbytes - cb - 16 * (lane & 7);
-    const uint32_t kb = (uint32_t)max(0, min(16, rem));
-    const uint8_t* src = ip + cb;
+    const uint32_t so = (uint32_t)(slot * kStageBytes);
+    const int ch = cbeg + is_cc;
+    const int cb = ch * kChunk;                    // byte offset of the chunk in a row
+    const int g0 = ch * SGR;                       // its first scale group
+    if (row_ok && cb + kChunk <= kbytes) {         // whole chunk inside the row: no tail
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = (lane >> 3) + 4 * i;
-      const bool on = ((ivalid >> i) & 1u) && kb > 0;
-      cp_async16(smem_u32(d + r * kPitch + 16 * (lane & 7)), on ? src + i * ldp4 : a.packed, on ? kb : 0u);
-    }
-    const int g0 = (cbeg + is_cc) * sgr;           // first scale group of the chunk
-    for (int p = lane; p < (kRows << lspr); p += 32) {
-      const int r = p >> lspr, q = p & ((1 << lspr) - 1);
-      const int grp = g0 + 2 * q;
-      const bool on = irow0 + r < N && grp < ngrp;
-      const uint32_t nb = on ? (uint32_t)min(2 * (ngrp - grp), 4) : 0u;
-      const int64_t ro = on ? (int64_t)(irow0 + r) : 0;
-      cp_async4(smem_u32(d + L.stage_scales + r * spitch + 4 * q), a.scales + (on ? ro * a.lds + grp : 0), nb);
-      if constexpr (ZEROS)
-        cp_async4(smem_u32(d + L.stage_zeros + r * spitch + 4 * q), a.zeros + (on ? ro * a.ldz + grp : 0), nb);
+      for (int i = 0; i < 4; ++i) cp_async16(cdst0 + so + 16 * i, crow + cb + 16 * i, 16u);
+      if (G != 256 || lh == 0) {
+#pragma unroll
+        for (int i = 0; i < (SGR >= 4 ? SGR / 4 : 1); ++i) {
+          cp_async4(sdst0 + so + 4 * i, srow + g0 + 2 * i, 4u);
+          if constexpr (ZEROS) cp_async4(zdst0 + so + 4 * i, zrow + g0 + 2 * i, 4u);
+        }
+      }
+    } else {                                       // ragged tail or a row past N: zero fill
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int rem = row_ok ? kbytes - cb - 64 * lh - 16 * i : 0;
+        const uint32_t nb = (uint32_t)max(0, min(16, rem));
+        cp_async16(cdst0 + so + 16 * i, nb ? crow + cb + 16 * i : a.packed, nb);
+      }
+      if (G != 256 || lh == 0) {
+#pragma unroll
+        for (int i = 0; i < (SGR >= 4 ? SGR / 4 : 1); ++i) {
+          const int grp = g0 + lh * (SGR / 2) + 2 * i;
+          const uint32_t nb = row_ok ? (uint32_t)max(0, min(2 * (ngrp - grp), 4)) : 0u;
+          cp_async4(sdst0 + so + 4 * i, nb ? srow + g0 + 2 * i : a.scales, nb);
+          if constexpr (ZEROS) cp_async4(zdst0 + so + 4 * i, nb ? zrow + g0 + 2 * i : a.zeros, nb);
+        }
+      }
     }
     if (++is_cc == mych) {
       is_cc = 0;
@@ -468,91 +494,125 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
       afin_sum[tid] = d;
     }
 
-    // Main loop: my tiles tl = warp + 8*i, their chunks in order, one stage each.
+    // Main loop: my tiles tl = warp + 8*i, their chunks in order, one stage each.  The MMA
+    // accumulators run across a tile's stages; each set's contribution is the difference of
+    // the folded sums before and after it (uint32 arithmetic), so no MMA starts from zero.
     const bool breal = (g >> 1) == t;
     const uint8_t* bbase = breal ? (tbl + t * NBT * SB + (g & 1) * SL) : zblk;
     const int bstep = breal ? NBC * SB : 0;         // next chunk
     const int sstep = breal ? SB : 0;               // next set
+    const float inv_tpf = 1.0f / (float)tpf;
+    // Per-thread offsets inside a stage: codes of row g (row g+8 is 8 pitches further) and
+    // the scale of row g for the first set (later sets add 2*(set >> GSHIFT) bytes).
+    const int a_off = g * kPitch + 32 * t;
+    const int s_off = kStageScales + g * SPITCH + 2 * ((t * NBT) >> GSHIFT);
+    const float2* ft0 = sFT + t * NBT;
+    const float* sx0 = sS + t * NBT;
+    int C[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int f = 0; f < 4; ++f) C[j][f] = 0;
+    uint32_t vprev[4] = {0u, 0u, 0u, 0u};
     float p0 = 0.0f, p1 = 0.0f;
     int cc = 0, ct = 0;
-    for (int base = 0; base < nst; base += kSlots) {
+    int s = 0;                                      // slot of stage k
+    const uint8_t* st = wstages;                    // that slot's base
+    for (int k = 0; k < nst; ++k) {
+      cp_async_wait<kSlots - 1>();
+      __syncwarp();
+      const uint8_t* pa = st + a_off;
+      const uint8_t* ps = st + s_off;
+      const uint8_t* bp = bbase + cc * bstep;
+      const float2* ft = ft0 + cc * NBC;
 #pragma unroll
-      for (int s = 0; s < kSlots; ++s) {
-        const int k = base + s;
-        if (k < nst) {
-          cp_async_wait<kSlots - 1>();
-          __syncwarp();
-          const uint8_t* st = wstages + s * L.stage_bytes;
-          // Codes of rows g and g+8, bytes [32t, 32t+32): words of blocks t*NBT .. +NBT.
-          const uint4 va = *reinterpret_cast<const uint4*>(st + g * kPitch + 32 * t);
-          const uint4 vb = *reinterpret_cast<const uint4*>(st + g * kPitch + 32 * t + 16);
-          const uint4 vc = *reinterpret_cast<const uint4*>(st + (g + 8) * kPitch + 32 * t);
-          const uint4 vd = *reinterpret_cast<const uint4*>(st + (g + 8) * kPitch + 32 * t + 16);
-          const uint32_t cw[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
-          const uint32_t cw8[8] = {vc.x, vc.y, vc.z, vc.w, vd.x, vd.y, vd.z, vd.w};
-          const uint16_t* ssc = reinterpret_cast<const uint16_t*>(st + L.stage_scales);
-          const uint16_t* szr = reinterpret_cast<const uint16_t*>(st + L.stage_zeros);
-          const uint8_t* bp = bbase + cc * bstep;
+      for (int set = 0; set < NBT; ++set) {
+        // Codes of rows g and g+8 in block t*NBT + set: W words each.
+        uint32_t cw[W], cw8[W];
+        if constexpr (W == 4) {
+          const uint4 va = *reinterpret_cast<const uint4*>(pa + 16 * set);
+          const uint4 vc = *reinterpret_cast<const uint4*>(pa + 8 * kPitch + 16 * set);
+          cw[0] = va.x; cw[1] = va.y; cw[2] = va.z; cw[3] = va.w;
+          cw8[0] = vc.x; cw8[1] = vc.y; cw8[2] = vc.z; cw8[3] = vc.w;
+        } else {
+          const uint2 va = *reinterpret_cast<const uint2*>(pa + 8 * set);
+          const uint2 vc = *reinterpret_cast<const uint2*>(pa + 8 * kPitch + 8 * set);
+          cw[0] = va.x; cw[1] = va.y;
+          cw8[0] = vc.x; cw8[1] = vc.y;
+        }
+        const uint8_t* bs = bp + set * sstep;
 #pragma unroll
-          for (int set = 0; set < NBT; ++set) {
-            int C[4][4];
+        for (int w = 0; w < W; ++w) {
 #pragma unroll
-            for (int w = 0; w < W; ++w) {
-              const uint32_t aw = cw[set * W + w], aw8 = cw8[set * W + w];
+          for (int jp = 0; jp < 4; jp += 2) {
+            const uint4 bq = *reinterpret_cast<const uint4*>(bs + (w * 4 + jp) * 8);
 #pragma unroll
-              for (int jp = 0; jp < 4; jp += 2) {
-                const uint4 bq = *reinterpret_cast<const uint4*>(bp + set * sstep + (w * 4 + jp) * 8);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const int j = jp + h;
-                  const uint32_t b0 = h ? bq.z : bq.x, b1 = h ? bq.w : bq.y;
-                  const uint32_t ml = 0x01010101u << (2 * j), mh = 0x02020202u << (2 * j);
-                  if (w == 0)
-                    mma_u8s8_z(C[j], aw & ml, aw8 & ml, aw & mh, aw8 & mh, b0, b1);
-                  else
-                    mma_u8s8(C[j], aw & ml, aw8 & ml, aw & mh, aw8 & mh, b0, b1);
-                }
-              }
+            for (int h = 0; h < 2; ++h) {
+              const int j = jp + h;
+              const uint32_t b0 = h ? bq.z : bq.x, b1 = h ? bq.w : bq.y;
+              const uint32_t ml = 0x01010101u << (2 * j), mh = 0x02020202u << (2 * j);
+              mma_u8s8(C[j], cw[w] & ml, cw8[w] & ml, cw[w] & mh, cw8[w] & mh, b0, b1);
             }
-            const int lb = cc * NBC + t * NBT + set;     // my block within the slice
-            const int gi = (t * NBT + set) >> gshift;     // its scale group within the stage
-            const float sg = h2f(ssc[g * (spitch / 2) + gi]), sg8 = h2f(ssc[(g + 8) * (spitch / 2) + gi]);
-            int v[4];
-#pragma unroll
-            for (int f = 0; f < 4; ++f) v[f] = ((C[0][f] * 4 + C[1][f]) * 4 + C[2][f]) * 4 + C[3][f];
-            const float2 FT = sFT[lb];
-            p0 = fmaf(sg, fmaf((float)(v[0] * 256 + v[1]), FT.x, FT.y), p0);
-            p1 = fmaf(sg8, fmaf((float)(v[2] * 256 + v[3]), FT.x, FT.y), p1);
-            if constexpr (ZEROS) {
-              const float Sx = sS[lb];
-              p0 = fmaf(h2f(szr[g * (spitch / 2) + gi]), Sx, p0);
-              p1 = fmaf(h2f(szr[(g + 8) * (spitch / 2) + gi]), Sx, p1);
-            }
-          }
-          // Every lane has read the slot (its values fed the MMAs above): refill it.
-          __syncwarp();
-          if (k + kSlots < nst) issue(s);
-          if (++cc == mych) {
-            // Tile done: reduce over the lane quad and push the K-partials of rows g, g+8
-            // to the CTA that finishes this tile.
-            const int tl = warp + kCWarps * ct;
-            const int q = tl / tpf;
-            const int slot = (tl - q * tpf) * kRows + g;
-            p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
-            p0 += __shfl_xor_sync(0xffffffffu, p0, 2);
-            p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
-            p1 += __shfl_xor_sync(0xffffffffu, p1, 2);
-            if (t == 0) {
-              const uint32_t f0 = smem_u32(fin + rank * fin_rows + slot);
-              st_cluster_f32_plain(mapa_shared(f0, (uint32_t)q), p0);
-              st_cluster_f32_plain(mapa_shared(f0 + 8 * 4, (uint32_t)q), p1);
-            }
-            p0 = p1 = 0.0f;
-            cc = 0;
-            ++ct;
           }
         }
-        cp_async_commit();
+        // Flush the set: fold the classes, take the difference, scale.
+        uint32_t v[4];
+#pragma unroll
+        for (int f = 0; f < 4; ++f) {
+          const uint32_t vn =
+              4u * (4u * (4u * (uint32_t)C[0][f] + (uint32_t)C[1][f]) + (uint32_t)C[2][f]) + (uint32_t)C[3][f];
+          v[f] = vn - vprev[f];
+          vprev[f] = vn;
+        }
+        const int so = 2 * (set >> GSHIFT);
+        const float sg = h2f(*reinterpret_cast<const uint16_t*>(ps + so));
+        const float sg8 = h2f(*reinterpret_cast<const uint16_t*>(ps + 8 * SPITCH + so));
+        const float2 FT = ft[set];
+        p0 = fmaf(sg, fmaf((float)(int)(v[0] * 256u + v[1]), FT.x, FT.y), p0);
+        p1 = fmaf(sg8, fmaf((float)(int)(v[2] * 256u + v[3]), FT.x, FT.y), p1);
+        if constexpr (ZEROS) {
+          const float Sx = sx0[cc * NBC + set];
+          const uint8_t* pz = ps + (kStageZeros - kStageScales);
+          p0 = fmaf(h2f(*reinterpret_cast<const uint16_t*>(pz + so)), Sx, p0);
+          p1 = fmaf(h2f(*reinterpret_cast<const uint16_t*>(pz + 8 * SPITCH + so)), Sx, p1);
+        }
+      }
+      // Every lane has read the slot (its values fed the MMAs above): refill it.
+      __syncwarp();
+      if (k + kSlots < nst) issue(s);
+      cp_async_commit();
+      if (++s == kSlots) {
+        s = 0;
+        st = wstages;
+      } else {
+        st += kStageBytes;
+      }
+      if (++cc == mych) {
+        // Tile done: reduce over the lane quad and push the K-partials of rows g, g+8 to the
+        // CTA that finishes this tile (q = tl / tpf; exact in float for these sizes).
+        const int tl = warp + kCWarps * ct;
+        const int q = (int)(((float)tl + 0.5f) * inv_tpf);
+        const int slot = (tl - q * tpf) * kRows + g;
+        p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
+        p0 += __shfl_xor_sync(0xffffffffu, p0, 2);
+        p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
+        p1 += __shfl_xor_sync(0xffffffffu, p1, 2);
+        if (t == 0) {
+          const uint32_t f0 = smem_u32(fin + rank * fin_rows + slot);
+          st_cluster_f32_plain(mapa_shared(f0, (uint32_t)q), p0);
+          st_cluster_f32_plain(mapa_shared(f0 + 8 * 4, (uint32_t)q), p1);
+        }
+        p0 = p1 = 0.0f;
+        cc = 0;
+        ++ct;
+        // Restart the running sums per tile: a tile's sums stay far inside int32 (at most
+        // 2^19 per MMA output times 8 MMAs per stage times K/4096 stages).
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int f = 0; f < 4; ++f) C[j][f] = 0;
+#pragma unroll
+        for (int f = 0; f < 4; ++f) vprev[f] = 0u;
       }
     }
     cp_async_wait<0>();
@@ -567,21 +627,21 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
   }
 }
 
-template <int W, bool ZEROS>
-__global__ void __launch_bounds__(kThreads, 2) k_gemv2b(const __grid_constant__ LinearArgs a) {
+template <int G, bool ZEROS>
+__global__ void __launch_bounds__(kThreads, kMinCtas) k_gemv2b(const __grid_constant__ LinearArgs a) {
   uint32_t cs;
   asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
-  gemv_body<W, ZEROS>(a, (int)(blockIdx.x / cs));
+  gemv_body<G, ZEROS>(a, (int)(blockIdx.x / cs));
 }
 
-template <int W, bool ZEROS>
-__global__ void __launch_bounds__(kThreads, 2) k_gemv2b_group(const __grid_constant__ GroupParams gp) {
+template <int G, bool ZEROS>
+__global__ void __launch_bounds__(kThreads, kMinCtas) k_gemv2b_group(const __grid_constant__ GroupParams gp) {
   uint32_t cs;
   asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
   const int cid = (int)(blockIdx.x / cs);
   int m = 0;
   while (m + 1 < gp.n && cid >= gp.prefix[m + 1]) ++m;
-  gemv_body<W, ZEROS>(gp.L[m], cid - gp.prefix[m]);
+  gemv_body<G, ZEROS>(gp.L[m], cid - gp.prefix[m]);
 }
 
 // Portable CUDA-core kernel: any M, any G dividing K with G % 4 == 0, any codebook.
@@ -694,8 +754,9 @@ static int gemv_S(int K) {
 
 // Row groups for a layer given a budget of clusters: every warp holds at least one tile,
 // and each CTA finishes at most one row per thread.
-template <int W>
+template <int G>
 static GemvPlan gemv_plan(const LinearArgs& a, int S, int budget) {
+  constexpr int W = words_for(G);
   GemvPlan p;
   p.S = S;
   const int ntiles = ceil_div(a.N, kRows);
@@ -704,13 +765,13 @@ static GemvPlan gemv_plan(const LinearArgs& a, int S, int budget) {
   int groups = std::max(min_groups, std::min(std::max(budget, 1), ceil_div(ntiles, kCWarps)));
   p.tpg = ceil_div(ntiles, groups);
   p.groups = ceil_div(ntiles, p.tpg);
-  p.smem = gemv_smem_layout(W, a.zeros != nullptr, a.K, a.G, S, a.n_out, a.ldo, p.tpg).total;
+  p.smem = gemv_smem_layout(W, a.zeros != nullptr, a.K, G, S, a.n_out, a.ldo, p.tpg).total;
   return p;
 }
 
 // Largest number of co-resident clusters of S CTAs for a given dynamic shared memory
 // size (cached: the occupancy query is a host call we do not want per launch).
-template <int W, bool ZEROS>
+template <int G, bool ZEROS>
 static int max_active_clusters(int S, int64_t smem) {
   static std::mutex mu;
   static std::map<std::tuple<int, int, int64_t>, int> cache;
@@ -735,7 +796,7 @@ static int max_active_clusters(int S, int64_t smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int mc = 0;
-  if (cudaOccupancyMaxActiveClusters(&mc, k_gemv2b<W, ZEROS>, &cfg) != cudaSuccess || mc <= 0)
+  if (cudaOccupancyMaxActiveClusters(&mc, k_gemv2b<G, ZEROS>, &cfg) != cudaSuccess || mc <= 0)
     mc = std::max(1, num_sms() / S);
   cudaGetLastError();
   std::lock_guard<std::mutex> lk(mu);
@@ -743,45 +804,45 @@ static int max_active_clusters(int S, int64_t smem) {
   return mc;
 }
 
-template <int W, bool ZEROS>
+template <int G, bool ZEROS>
 static int configure_kernels() {
   static thread_local int configured_dev[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured_dev[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemv2b<W, ZEROS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(k_gemv2b<G, ZEROS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(k_gemv2b_group<W, ZEROS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      e = cudaFuncSetAttribute(k_gemv2b_group<G, ZEROS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return set_cuda_error(e);
     configured_dev[dev] = 1;
   }
   return OTF_OK;
 }
 
-template <int W, bool ZEROS>
+template <int G, bool ZEROS>
 static int launch_gemv(LinearArgs a, cudaStream_t st) {
-  int rc = configure_kernels<W, ZEROS>();
+  int rc = configure_kernels<G, ZEROS>();
   if (rc != OTF_OK) return rc;
   const int S = gemv_S(a.K);
   // No more clusters than can be resident at once: a second wave would double the time.
-  GemvPlan p = gemv_plan<W>(a, S, 1 << 20);
+  GemvPlan p = gemv_plan<G>(a, S, 1 << 20);
   for (int pass = 0; pass < 3; ++pass) {
     if (p.smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
-    const GemvPlan q = gemv_plan<W>(a, S, max_active_clusters<W, ZEROS>(S, p.smem));
+    const GemvPlan q = gemv_plan<G>(a, S, max_active_clusters<G, ZEROS>(S, p.smem));
     if (q.groups == p.groups) break;
     p = q;
   }
   if (p.smem > 227 * 1024 || tiles_per_finisher(p.tpg, S) * kRows > kCThreads) return OTF_ERR_UNSUPPORTED;
   a.tiles_per_group = p.tpg;
-  return set_cuda_error(launch_pdl(k_gemv2b<W, ZEROS>, dim3((unsigned)(p.groups * S)), dim3(kThreads),
+  return set_cuda_error(launch_pdl(k_gemv2b<G, ZEROS>, dim3((unsigned)(p.groups * S)), dim3(kThreads),
                                    (size_t)p.smem, st, (unsigned)S, a));
 }
 
 // Layers with the same K, G and zero-point use launched as one grid: cluster budgets are
 // split in proportion to each layer's row tiles so that the whole group is co-resident.
-template <int W, bool ZEROS>
+template <int G, bool ZEROS>
 static int launch_gemv_group(LinearArgs* L, int n, cudaStream_t st) {
-  int rc = configure_kernels<W, ZEROS>();
+  int rc = configure_kernels<G, ZEROS>();
   if (rc != OTF_OK) return rc;
   static thread_local GroupParams gp;  // large: keep it off the host stack
   gp.n = n;
@@ -790,18 +851,18 @@ static int launch_gemv_group(LinearArgs* L, int n, cudaStream_t st) {
   int tiles_total = 0;
   for (int m = 0; m < n; ++m) {
     tiles_total += ceil_div(L[m].N, kRows);
-    smem_hi = std::max(smem_hi, gemv_plan<W>(L[m], S, 1 << 20).smem);
+    smem_hi = std::max(smem_hi, gemv_plan<G>(L[m], S, 1 << 20).smem);
   }
   GemvPlan plans[kMaxGroup];
   int64_t smem = smem_hi;
   for (int pass = 0; pass < 3; ++pass) {
     if (smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
-    const int mc = max_active_clusters<W, ZEROS>(S, smem);
+    const int mc = max_active_clusters<G, ZEROS>(S, smem);
     int64_t s2 = 0;
     for (int m = 0; m < n; ++m) {
       const int tiles = ceil_div(L[m].N, kRows);
       const int budget = std::max(1, (int)((int64_t)mc * tiles / std::max(tiles_total, 1)));
-      plans[m] = gemv_plan<W>(L[m], S, budget);
+      plans[m] = gemv_plan<G>(L[m], S, budget);
       s2 = std::max(s2, plans[m].smem);
     }
     if (s2 == smem) break;
@@ -817,7 +878,7 @@ static int launch_gemv_group(LinearArgs* L, int n, cudaStream_t st) {
   }
   gp.prefix[n] = clusters;
   if (smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
-  return set_cuda_error(launch_pdl(k_gemv2b_group<W, ZEROS>, dim3((unsigned)(clusters * S)), dim3(kThreads),
+  return set_cuda_error(launch_pdl(k_gemv2b_group<G, ZEROS>, dim3((unsigned)(clusters * S)), dim3(kThreads),
                                    (size_t)smem, st, (unsigned)S, gp));
 }
 
@@ -884,7 +945,7 @@ static int build_args(LinearArgs& a, const void* x, int64_t ldx, const uint8_t* 
   return OTF_OK;
 }
 
-// Which tensor-pipe variant serves these arguments: 4 (G % 64), 2 (G == 32) or 0 (none).
+// Which tensor-pipe variant serves these arguments: the group size (32, 64, 128, 256) or 0.
 // It needs c3 - c2 == c1 - c0 (affine in the two code bits), batch 1, G a power-of-two
 // multiple of the 16W-code block with at least two groups per 512-code stage, 16-byte
 // aligned code rows, 4-byte aligned scale rows and 16-byte aligned activation vectors.
@@ -896,10 +957,21 @@ static int fast_variant(const LinearArgs& a, uint32_t flags) {
   const bool vec_ok = al(a.x, 16) && (!a.mask || al(a.mask, 16)) && (!a.xaux || al(a.xaux, 16)) && al(a.scales, 4) &&
                       a.lds % 2 == 0 && (!a.zeros || (al(a.zeros, 4) && a.ldz % 2 == 0)) && al(a.packed, 16) &&
                       a.ldp % 16 == 0 && a.K % 8 == 0;
-  if ((flags & OTF_FLAG_FORCE_GENERIC) || !affine || a.M != 1 || !vec_ok || !pow2(a.G) || a.G > 256) return 0;
-  if (a.G >= 64) return 4;
-  if (a.G == 32) return 2;
-  return 0;
+  if ((flags & OTF_FLAG_FORCE_GENERIC) || !affine || a.M != 1 || !vec_ok || !pow2(a.G) || a.G > 256 || a.G < 32)
+    return 0;
+  return (a.G >= 32) ? a.G : 0;
+}
+
+// One layer on the tensor-pipe kernel for group size G (from fast_variant); UNSUPPORTED if G is 0.
+static int launch_fast(const LinearArgs& a, int G, cudaStream_t s) {
+  const bool z = a.zeros != nullptr;
+  switch (G) {
+    case 32: return z ? launch_gemv<32, true>(a, s) : launch_gemv<32, false>(a, s);
+    case 64: return z ? launch_gemv<64, true>(a, s) : launch_gemv<64, false>(a, s);
+    case 128: return z ? launch_gemv<128, true>(a, s) : launch_gemv<128, false>(a, s);
+    case 256: return z ? launch_gemv<256, true>(a, s) : launch_gemv<256, false>(a, s);
+    default: return OTF_ERR_UNSUPPORTED;
+  }
 }
 
 extern "C" OTF_API int otf2b_linear(const void* x, int64_t ldx, const uint8_t* packed, int64_t ld_packed,
@@ -918,11 +990,7 @@ extern "C" OTF_API int otf2b_linear(const void* x, int64_t ldx, const uint8_t* p
   if (st != OTF_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = OTF_ERR_UNSUPPORTED;
-  switch (fast_variant(a, flags)) {
-    case 4: rc = zeros ? launch_gemv<4, true>(a, s) : launch_gemv<4, false>(a, s); break;
-    case 2: rc = zeros ? launch_gemv<2, true>(a, s) : launch_gemv<2, false>(a, s); break;
-    default: break;
-  }
+  rc = launch_fast(a, fast_variant(a, flags), s);
   if (rc != OTF_ERR_UNSUPPORTED) return rc;
   return launch_generic(a, s);
 }
@@ -951,16 +1019,21 @@ extern "C" OTF_API int otf2b_linear_group(const otf2b_layer* layers, int n_layer
   for (int m = 1; m < n_layers; ++m)
     same = same && L[m].K == L[0].K && L[m].G == L[0].G && (L[m].zeros != nullptr) == (L[0].zeros != nullptr) &&
            fast_variant(L[m], layers[m].flags) == v0;
-  if (same && v0 == 4)
-    return L[0].zeros ? launch_gemv_group<4, true>(L, n_layers, s) : launch_gemv_group<4, false>(L, n_layers, s);
-  if (same && v0 == 2)
-    return L[0].zeros ? launch_gemv_group<2, true>(L, n_layers, s) : launch_gemv_group<2, false>(L, n_layers, s);
+  if (same && v0 != 0) {
+    const bool z = L[0].zeros != nullptr;
+    switch (v0) {
+      case 32: return z ? launch_gemv_group<32, true>(L, n_layers, s) : launch_gemv_group<32, false>(L, n_layers, s);
+      case 64: return z ? launch_gemv_group<64, true>(L, n_layers, s) : launch_gemv_group<64, false>(L, n_layers, s);
+      case 128: return z ? launch_gemv_group<128, true>(L, n_layers, s) : launch_gemv_group<128, false>(L, n_layers, s);
+      case 256: return z ? launch_gemv_group<256, true>(L, n_layers, s) : launch_gemv_group<256, false>(L, n_layers, s);
+      default: break;
+    }
+  }
   // Otherwise one launch per layer; transforms need the tensor-pipe kernel.
   for (int m = 0; m < n_layers; ++m) {
     const int v = fast_variant(L[m], layers[m].flags);
     int rc = OTF_ERR_UNSUPPORTED;
-    if (v == 4) rc = L[m].zeros ? launch_gemv<4, true>(L[m], s) : launch_gemv<4, false>(L[m], s);
-    else if (v == 2) rc = L[m].zeros ? launch_gemv<2, true>(L[m], s) : launch_gemv<2, false>(L[m], s);
+    if (v != 0) rc = launch_fast(L[m], v, s);
     else if (L[m].xop == OTF_XOP_NONE) rc = launch_generic(L[m], s);
     if (rc != OTF_OK) return rc;
   }
