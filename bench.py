@@ -308,20 +308,21 @@ def run_case(args):
     import torch
     from otf_llm import _native
     from otf_llm.decoder_stack import StackConfig, linear_bytes, random_quantized_linear
-    kind, a, b = args.case.split(":")
-    a, b = int(a), int(b)
+    parts = args.case.split(":")
+    kind, a, b = parts[0], int(parts[1]), int(parts[2])
+    M = int(parts[3]) if len(parts) > 3 else 1
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
-    if kind == "gemv":
+    if kind in ("gemv", "gemm"):
         cfg = StackConfig()
         lay = random_quantized_linear(a, b, cfg, seed=3, device=dev)
-        x = torch.randn(1, b, device=dev).half()
-        y = torch.empty(1, a, dtype=torch.float16, device=dev)
+        x = torch.randn(M, b, device=dev).half()
+        y = torch.empty(M, a, dtype=torch.float16, device=dev)
         n_out = lay.outlier_indices.numel()
         fn = lambda: _native.linear_2bit(x, lay.packed_uint8, lay.scales, 64, lay.codebook,
                                          mask=lay.outlier_mask_vector, outlier_idx=lay.outlier_indices,
                                          outlier_vals=lay.outliers_fp16, out=y)
-        nbytes = linear_bytes(a, b, 64, n_out)
+        nbytes = linear_bytes(a, b, 64, n_out, batch=M)
     else:
         w = torch.randint(-127, 128, (a, b), dtype=torch.int8, device=dev)
         s = (torch.rand(a, 1, device=dev) * 1e-3).half()
@@ -345,7 +346,8 @@ def run_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", default=None, help="single-kernel timing/profiling case, e.g. gemv:11008:4096")
+    ap.add_argument("--case", default=None,
+                    help="single-kernel timing/profiling case: gemv:N:K, gemm:N:K:M (batched) or head:V:D")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)

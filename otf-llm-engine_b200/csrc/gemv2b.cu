@@ -644,6 +644,390 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) k_gemv2b_group(const __gri
   gemv_body<G, ZEROS>(gp.L[m], cid - gp.prefix[m]);
 }
 
+// ---------------------------------------------------------------------------------------
+// Batched decode (2 <= M <= 8 activation rows), same packed layout and work split.  The
+// MMA's eight B columns are (batch row, limb) pairs -- four batch rows per column group,
+// MB = 4*CG -- so B is dense: every lane reads a useful table fragment, and the four code
+// words of one 64-code block fill the 32 k-slots of an MMA (lane quad t holds word t of the
+// block, loaded with ldmatrix).  Each lane quad owns one batch row of the accumulators, so
+// no cross-lane reduction is needed.  Group sizes of 64, 128 and 256 codes (a block never
+// straddles a scale group); no fused input transforms.
+
+// Table bytes of one 64-code block for one column group: 4 rows x 2 limbs x 4 quads x 32 bytes.
+constexpr int kBatchTbl = 1024;
+
+struct GemvBatchSmem {
+  int64_t stages, tbl, meta, xo, ov, fin, bars, total;
+  int stage_bytes, stage_scales, stage_zeros, ov_bytes;
+};
+
+__host__ __device__ inline GemvBatchSmem gemv_batch_smem_layout(int CG, bool zeros, int K, int G, int S, int n_out,
+                                                                int64_t ldo, int tiles_per_group) {
+  const int MB = 4 * CG;
+  const int nch = ceil_div(K, kChunkCodes);
+  const int ch_slice = ceil_div(nch, S), blk_slice = ch_slice * (kChunkCodes / 64);
+  const int frows = tiles_per_finisher(tiles_per_group, S) * kRows;
+  GemvBatchSmem L;
+  L.stage_scales = kRows * kPitch;
+  L.stage_zeros = L.stage_scales + kRows * scale_pitch(G);
+  L.stage_bytes = L.stage_zeros + (zeros ? kRows * scale_pitch(G) : 0);
+  const int64_t ovb = n_out > 0 ? ((int64_t)(frows - 1) * ldo + n_out) * 2 + 32 : 0;
+  L.ov_bytes = ovb <= kOvMax ? (int)align_up(ovb, 16) : 0;
+  int64_t off = 0;
+  L.stages = off; off = align_up(off + (int64_t)kCWarps * kSlots * L.stage_bytes, 128);
+  L.tbl = off;    off = align_up(off + (int64_t)blk_slice * CG * kBatchTbl, 128);
+  L.meta = off;   off = align_up(off + (int64_t)blk_slice * MB * 12, 16);   // (F, T) and sum x per (block, row)
+  L.xo = off;     off = align_up(off + (int64_t)MB * n_out * 4, 16);
+  L.ov = off;     off = align_up(off + L.ov_bytes, 16);
+  L.fin = off;    off = align_up(off + (int64_t)S * MB * frows * 4, 16);
+  L.bars = off;   off = align_up(off + 8, 16);
+  L.total = off;
+  return L;
+}
+
+template <int G, bool ZEROS, int CG>
+__device__ __forceinline__ void gemv_batch_body(const LinearArgs& a, const int group) {
+  constexpr int BLK = 64;                          // codes per block (four 32-bit words per row)
+  constexpr int NBC = kChunkCodes / BLK;           // 8 blocks per stage row
+  constexpr int GSHIFT = G == 64 ? 0 : (G == 128 ? 1 : 2);
+  constexpr int SGR = kChunkCodes / G;
+  constexpr int SPITCH = 2 * SGR + 4;
+  constexpr int MB = 4 * CG;
+  constexpr int TBB = CG * kBatchTbl;              // table bytes per block
+  static_assert(G == 64 || G == 128 || G == 256, "group size");
+  constexpr int kStageScales = kRows * kPitch;
+  constexpr int kStageZeros = kStageScales + kRows * SPITCH;
+  constexpr int kStageBytes = kStageZeros + (ZEROS ? kRows * SPITCH : 0);
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int K = a.K, N = a.N, M = a.M;
+  const int nblk = K / BLK, nch = ceil_div(K, kChunkCodes);
+  uint32_t cs;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
+  const int S = (int)cs;
+  const int rank = (int)cluster_ctarank();
+  const int ch_slice = ceil_div(nch, S);
+  const int cbeg = min(rank * ch_slice, nch), cend = min(cbeg + ch_slice, nch);
+  const int mych = cend - cbeg;
+  const int blk0 = cbeg * NBC;
+  const int kbeg = blk0 * BLK;
+  const int nbs = min(cend * NBC, nblk) - blk0;
+  const int nbs_pad = mych * NBC;
+  const GemvBatchSmem L = gemv_batch_smem_layout(CG, ZEROS, K, G, S, a.n_out, a.ldo, a.tiles_per_group);
+  uint8_t* tbl = smem + L.tbl;
+  float2* sFT = reinterpret_cast<float2*>(smem + L.meta);          // [block][row]
+  float* sS = reinterpret_cast<float*>(smem + L.meta) + 2 * nbs_pad * MB;
+  float* xo = reinterpret_cast<float*>(smem + L.xo);               // [row][anchor]
+  float* fin = reinterpret_cast<float*>(smem + L.fin);             // [source CTA][row][finished row]
+  const uint32_t ov_bar = smem_u32(smem + L.bars);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ntiles = ceil_div(N, kRows);
+  const int tile0 = group * a.tiles_per_group;
+  const int gtiles = max(0, min(a.tiles_per_group, ntiles - tile0));
+  const int tpf = tiles_per_finisher(a.tiles_per_group, S);
+  const int fin_rows = tpf * kRows;
+  const int ngrp = K / G;
+
+  pdl_trigger();
+
+  const int frow0 = (tile0 + rank * tpf) * kRows;
+  const int nfin = max(0, min(min(fin_rows, gtiles * kRows - rank * fin_rows), N - frow0));
+  const bool ov_smem = a.n_out > 0 && L.ov_bytes > 0 && nfin > 0;
+  uint32_t ov_skew = 0;
+  if (ov_smem) {
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(a.ovals + (int64_t)frow0 * a.ldo);
+    const uintptr_t hi = reinterpret_cast<uintptr_t>(a.ovals + (int64_t)(frow0 + nfin - 1) * a.ldo + a.n_out);
+    const uintptr_t lo16 = lo & ~(uintptr_t)15, hi16 = (hi + 15) & ~(uintptr_t)15;
+    ov_skew = (uint32_t)(lo - lo16);
+    if (tid == 0) {
+      mbar_init(ov_bar, 1);
+      mbar_fence_init();
+      mbar_arrive_expect_tx(ov_bar, (uint32_t)(hi16 - lo16));
+      bulk_load(smem_u32(smem + L.ov), reinterpret_cast<const void*>(lo16), (uint32_t)(hi16 - lo16), ov_bar);
+    }
+  }
+  cluster_arrive_relaxed();
+
+  // Stage pipeline: identical to the batch-1 kernel (tile w + 8*(k / mych), chunk k % mych).
+  const int my_tiles = warp < gtiles ? ceil_div(gtiles - warp, kCWarps) : 0;
+  const int nst = my_tiles * mych;
+  uint8_t* const wstages = smem + L.stages + warp * kSlots * kStageBytes;
+  const int kbytes = K / 4;
+  const int lr = lane >> 1, lh = lane & 1;
+  const uint32_t cdst0 = smem_u32(wstages) + lr * kPitch + 64 * lh;
+  const uint32_t sdst0 = smem_u32(wstages + kStageScales) + lr * SPITCH + lh * SGR;
+  const uint32_t zdst0 = smem_u32(wstages + kStageZeros) + lr * SPITCH + lh * SGR;
+  int is_cc = 0, is_tile = 0;
+  const uint8_t* crow = a.packed;
+  const uint16_t* srow = a.scales;
+  const uint16_t* zrow = a.zeros;
+  bool row_ok = false;
+  auto issue_tile = [&]() {
+    const int r = (tile0 + warp + kCWarps * is_tile) * kRows + lr;
+    row_ok = r < N;
+    const int64_t rr = row_ok ? r : 0;
+    crow = a.packed + rr * a.ldp + 64 * lh;
+    srow = a.scales + rr * a.lds + lh * (SGR / 2);
+    if constexpr (ZEROS) zrow = a.zeros + rr * a.ldz + lh * (SGR / 2);
+  };
+  auto issue = [&](int slot) {
+    const uint32_t so = (uint32_t)(slot * kStageBytes);
+    const int ch = cbeg + is_cc;
+    const int cb = ch * kChunk;
+    const int g0 = ch * SGR;
+    if (row_ok && cb + kChunk <= kbytes) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) cp_async16(cdst0 + so + 16 * i, crow + cb + 16 * i, 16u);
+      if (G != 256 || lh == 0) {
+#pragma unroll
+        for (int i = 0; i < (SGR >= 4 ? SGR / 4 : 1); ++i) {
+          cp_async4(sdst0 + so + 4 * i, srow + g0 + 2 * i, 4u);
+          if constexpr (ZEROS) cp_async4(zdst0 + so + 4 * i, zrow + g0 + 2 * i, 4u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int rem = row_ok ? kbytes - cb - 64 * lh - 16 * i : 0;
+        const uint32_t nb = (uint32_t)max(0, min(16, rem));
+        cp_async16(cdst0 + so + 16 * i, nb ? crow + cb + 16 * i : a.packed, nb);
+      }
+      if (G != 256 || lh == 0) {
+#pragma unroll
+        for (int i = 0; i < (SGR >= 4 ? SGR / 4 : 1); ++i) {
+          const int grp = g0 + lh * (SGR / 2) + 2 * i;
+          const uint32_t nb = row_ok ? (uint32_t)max(0, min(2 * (ngrp - grp), 4)) : 0u;
+          cp_async4(sdst0 + so + 4 * i, nb ? srow + g0 + 2 * i : a.scales, nb);
+          if constexpr (ZEROS) cp_async4(zdst0 + so + 4 * i, nb ? zrow + g0 + 2 * i : a.zeros, nb);
+        }
+      }
+    }
+    if (++is_cc == mych) {
+      is_cc = 0;
+      ++is_tile;
+      issue_tile();
+    }
+  };
+  issue_tile();
+#pragma unroll
+  for (int k = 0; k < kSlots; ++k) {
+    if (k < nst) issue(k);
+    cp_async_commit();
+  }
+
+  const int g = lane >> 2, t = lane & 3;
+  pdl_wait();
+  // Anchor activations per batch row (unmasked x at the anchor columns).
+  for (int i = tid; i < M * a.n_out; i += kCThreads) {
+    const int m = i / a.n_out, j = i - m * a.n_out;
+    xo[m * a.n_out + j] = h2f(ldg_u16(a.x + (int64_t)m * a.ldx + __ldg(a.oidx + j)));
+  }
+  // Table of the slice: for each (block, batch row), 16 lanes quantise the block's 64 codes
+  // (lane (w, j) owns codes 16w + 4i + j) and write the fragment of lane (2*row4 + limb, w).
+  {
+    const float bl = a.c1 - a.c0, bh = 0.5f * (a.c2 - a.c0);
+    const float cmax = fmaxf(fabsf(bl), fabsf(bh));
+    const int sub = lane >> 4, l = lane & 15;
+    const int wq = l >> 2, j = l & 3;
+    const int npairs = nbs_pad * MB;
+    for (int p0 = 0; p0 < npairs; p0 += 2 * kCWarps) {
+      const int p = p0 + warp * 2 + sub;
+      const int bi = p / MB, m = p - (p / MB) * MB;
+      const bool live = p < npairs;
+      const bool on = live && bi < nbs && m < M;
+      float xv[4];
+      float mx = 0.0f, sx = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = kbeg + bi * BLK + 16 * wq + 4 * i + j;
+        float v = 0.0f;
+        if (on) {
+          __half xh = __ushort_as_half(ldg_u16(a.x + (int64_t)m * a.ldx + k));
+          if (a.mask) xh = __hmul(xh, __ushort_as_half(ldg_u16(a.mask + k)));
+          v = __half2float(xh);
+        }
+        xv[i] = v;
+        mx = fmaxf(mx, fabsf(v));
+        sx += v;
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        sx += __shfl_xor_sync(0xffffffffu, sx, o);
+      }
+      const int E = fixed_point_exp(mx * cmax);
+      const float sc = exp2i(E);
+      const float kl = bl * sc, kh = bh * sc;
+      int hl[4], ll[4], hh[4], lh2[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        split_limbs(rint_small(xv[i] * kl), hl[i], ll[i]);
+        split_limbs(rint_small(xv[i] * kh), hh[i], lh2[i]);
+      }
+      if (live) {
+        const int cg = m >> 2, m4 = m & 3;
+        uint8_t* base = tbl + bi * TBB + cg * kBatchTbl + ((j >> 1) * 16) + (j & 1) * 8;
+#pragma unroll
+        for (int limb = 0; limb < 2; ++limb) {
+          const int gl = 2 * m4 + limb;                 // the lane row (g) that reads this entry
+          uint8_t* e = base + (gl * 4 + wq) * 32;
+          e = reinterpret_cast<uint8_t*>(reinterpret_cast<uintptr_t>(e) ^ (uintptr_t)(limb * 16));
+          *reinterpret_cast<uint2*>(e) = limb == 0 ? make_uint2(pack4(hl[0], hl[1], hl[2], hl[3]), pack4(hh[0], hh[1], hh[2], hh[3]))
+                                                   : make_uint2(pack4(ll[0], ll[1], ll[2], ll[3]), pack4(lh2[0], lh2[1], lh2[2], lh2[3]));
+        }
+        if (l == 0) {
+          sFT[bi * MB + m] = make_float2(exp2i(-E) * (1.0f / 64.0f), a.c0 * sx);
+          sS[bi * MB + m] = sx;
+        }
+      }
+    }
+  }
+  named_barrier_sync(1, kCThreads);
+  cluster_wait();
+
+  // Main loop.  Running accumulators per column group; each block's contribution is the
+  // difference of the folded sums (uint32 arithmetic).
+  const uint32_t ldm_off = (uint32_t)((lane & 15) * kPitch + 16 * (lane >> 4));
+  const int s_off = kStageScales + g * SPITCH;
+  const int lane_tb = (g * 4 + t) * 32;            // my table fragment inside a block / group
+  const int swz = (g & 1) * 16;
+  const float inv_tpf = 1.0f / (float)tpf;
+  int C[CG][4][4];
+  uint32_t vprev[CG][4];
+#pragma unroll
+  for (int c = 0; c < CG; ++c)
+#pragma unroll
+    for (int f = 0; f < 4; ++f) {
+      vprev[c][f] = 0u;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) C[c][jj][f] = 0;
+    }
+  float pr[CG][2];
+#pragma unroll
+  for (int c = 0; c < CG; ++c) pr[c][0] = pr[c][1] = 0.0f;
+  int cc = 0, ct = 0;
+  int s = 0;
+  const uint8_t* st = wstages;
+  for (int k = 0; k < nst; ++k) {
+    cp_async_wait<kSlots - 1>();
+    __syncwarp();
+    const uint8_t* ps = st + s_off;
+#pragma unroll
+    for (int bp = 0; bp < NBC / 2; ++bp) {
+      uint32_t r[4];
+      ldmatrix_x4(smem_u32(st) + ldm_off + 32 * bp, r[0], r[1], r[2], r[3]);
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb) {
+        const int b = 2 * bp + hb;                 // block within the stage
+        const uint32_t ra = r[2 * hb], rb = r[2 * hb + 1];
+        const int lb = cc * NBC + b;               // block within the slice
+        const int so = 2 * (b >> GSHIFT);
+        const float sg = h2f(*reinterpret_cast<const uint16_t*>(ps + so));
+        const float sg8 = h2f(*reinterpret_cast<const uint16_t*>(ps + 8 * SPITCH + so));
+#pragma unroll
+        for (int c = 0; c < CG; ++c) {
+          const uint8_t* bb = tbl + lb * TBB + c * kBatchTbl + lane_tb;
+          const uint4 bq0 = *reinterpret_cast<const uint4*>(bb + (0 ^ swz));
+          const uint4 bq1 = *reinterpret_cast<const uint4*>(bb + (16 ^ swz));
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const uint4& bq = jj < 2 ? bq0 : bq1;
+            const uint32_t b0 = (jj & 1) ? bq.z : bq.x, b1 = (jj & 1) ? bq.w : bq.y;
+            const uint32_t ml = 0x01010101u << (2 * jj), mh = 0x02020202u << (2 * jj);
+            mma_u8s8(C[c][jj], ra & ml, rb & ml, ra & mh, rb & mh, b0, b1);
+          }
+          uint32_t v[4];
+#pragma unroll
+          for (int f = 0; f < 4; ++f) {
+            const uint32_t vn = 4u * (4u * (4u * (uint32_t)C[c][0][f] + (uint32_t)C[c][1][f]) + (uint32_t)C[c][2][f]) +
+                                (uint32_t)C[c][3][f];
+            v[f] = vn - vprev[c][f];
+            vprev[c][f] = vn;
+          }
+          const float2 FT = sFT[lb * MB + 4 * c + t];
+          pr[c][0] = fmaf(sg, fmaf((float)(int)(v[0] * 256u + v[1]), FT.x, FT.y), pr[c][0]);
+          pr[c][1] = fmaf(sg8, fmaf((float)(int)(v[2] * 256u + v[3]), FT.x, FT.y), pr[c][1]);
+          if constexpr (ZEROS) {
+            const float Sx = sS[lb * MB + 4 * c + t];
+            const uint8_t* pz = ps + (kStageZeros - kStageScales);
+            pr[c][0] = fmaf(h2f(*reinterpret_cast<const uint16_t*>(pz + so)), Sx, pr[c][0]);
+            pr[c][1] = fmaf(h2f(*reinterpret_cast<const uint16_t*>(pz + 8 * SPITCH + so)), Sx, pr[c][1]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (k + kSlots < nst) issue(s);
+    cp_async_commit();
+    if (++s == kSlots) {
+      s = 0;
+      st = wstages;
+    } else {
+      st += kStageBytes;
+    }
+    if (++cc == mych) {
+      // Tile done: lane (g, t) holds batch row 4c + t of rows g, g+8; push them.
+      const int tl = warp + kCWarps * ct;
+      const int q = (int)(((float)tl + 0.5f) * inv_tpf);
+      const int slot = (tl - q * tpf) * kRows + g;
+#pragma unroll
+      for (int c = 0; c < CG; ++c) {
+        const int m = 4 * c + t;
+        if (m < M) {
+          const uint32_t f0 = smem_u32(fin + (rank * MB + m) * fin_rows + slot);
+          st_cluster_f32_plain(mapa_shared(f0, (uint32_t)q), pr[c][0]);
+          st_cluster_f32_plain(mapa_shared(f0 + 8 * 4, (uint32_t)q), pr[c][1]);
+        }
+        pr[c][0] = pr[c][1] = 0.0f;
+      }
+      cc = 0;
+      ++ct;
+#pragma unroll
+      for (int c = 0; c < CG; ++c)
+#pragma unroll
+        for (int f = 0; f < 4; ++f) {
+          vprev[c][f] = 0u;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) C[c][jj][f] = 0;
+        }
+    }
+  }
+  cp_async_wait<0>();
+  cluster_sync_all();
+  if (ov_smem)
+    if (!mbar_wait(ov_bar, 0u)) report_wait_failure();
+  // Epilogue: (finished row, batch row) pairs.
+  for (int i = tid; i < nfin * M; i += kCThreads) {
+    const int m = i / nfin, rr = i - m * nfin;
+    const int row = frow0 + rr;
+    float yv = 0.0f;
+    for (int q = 0; q < S; ++q) yv += fin[(q * MB + m) * fin_rows + rr];
+    if (a.n_out > 0) {
+      const float* xm = xo + m * a.n_out;
+      float d = 0.0f;
+      if (ov_smem) {
+        const uint16_t* ovr = reinterpret_cast<const uint16_t*>(smem + L.ov + ov_skew) + (int64_t)rr * a.ldo;
+        for (int jx = 0; jx < a.n_out; ++jx) d = fmaf(xm[jx], h2f(ovr[jx]), d);
+      } else {
+        const uint16_t* ovr = a.ovals + (int64_t)row * a.ldo;
+        for (int jx = 0; jx < a.n_out; ++jx) d = fmaf(xm[jx], h2f(ldg_u16(ovr + jx)), d);
+      }
+      yv += d;
+    }
+    if (a.bias) yv += h2f(ldg_u16(a.bias + row));
+    if (a.res) yv += h2f(ldg_u16(a.res + (int64_t)m * a.ldr + row));
+    if (a.clamp) yv = fminf(fmaxf(yv, -65504.0f), 65504.0f);
+    a.y[(int64_t)m * a.ldy + row] = f2h(yv);
+  }
+}
+
+template <int G, bool ZEROS, int CG>
+__global__ void __launch_bounds__(kThreads, kMinCtas) k_gemv2b_batch(const __grid_constant__ LinearArgs a) {
+  uint32_t cs;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(cs));
+  gemv_batch_body<G, ZEROS, CG>(a, (int)(blockIdx.x / cs));
+}
+
 // Portable CUDA-core kernel: any M, any G dividing K with G % 4 == 0, any codebook.
 // One warp per output row, lanes stride over packed bytes; MT activation rows per launch.
 template <int MT>
@@ -769,16 +1153,15 @@ static GemvPlan gemv_plan(const LinearArgs& a, int S, int budget) {
   return p;
 }
 
-// Largest number of co-resident clusters of S CTAs for a given dynamic shared memory
-// size (cached: the occupancy query is a host call we do not want per launch).
-template <int G, bool ZEROS>
-static int max_active_clusters(int S, int64_t smem) {
+// Largest number of co-resident clusters of S CTAs of a kernel for a given dynamic shared
+// memory size (cached: the occupancy query is a host call we do not want per launch).
+static int max_active_clusters_of(const void* kernel, int S, int64_t smem) {
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int64_t>, int> cache;
+  static std::map<std::tuple<int, const void*, int, int64_t>, int> cache;
   int dev = 0;
   cudaGetDevice(&dev);
   const int64_t bucket = align_up(smem, 4096);
-  const auto key = std::make_tuple(dev, S, bucket);
+  const auto key = std::make_tuple(dev, kernel, S, bucket);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -796,12 +1179,18 @@ static int max_active_clusters(int S, int64_t smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int mc = 0;
-  if (cudaOccupancyMaxActiveClusters(&mc, k_gemv2b<G, ZEROS>, &cfg) != cudaSuccess || mc <= 0)
-    mc = std::max(1, num_sms() / S);
+  if (cudaOccupancyMaxActiveClusters(&mc, kernel, &cfg) != cudaSuccess || mc <= 0) mc = std::max(1, num_sms() / S);
   cudaGetLastError();
   std::lock_guard<std::mutex> lk(mu);
   cache[key] = mc;
   return mc;
+}
+
+// Largest number of co-resident clusters of S CTAs for a given dynamic shared memory
+// size (cached: the occupancy query is a host call we do not want per launch).
+template <int G, bool ZEROS>
+static int max_active_clusters(int S, int64_t smem) {
+  return max_active_clusters_of(reinterpret_cast<const void*>(k_gemv2b<G, ZEROS>), S, smem);
 }
 
 template <int G, bool ZEROS>
@@ -880,6 +1269,44 @@ static int launch_gemv_group(LinearArgs* L, int n, cudaStream_t st) {
   if (smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
   return set_cuda_error(launch_pdl(k_gemv2b_group<G, ZEROS>, dim3((unsigned)(clusters * S)), dim3(kThreads),
                                    (size_t)smem, st, (unsigned)S, gp));
+}
+
+// Batched layers (2 <= M <= 4*CG): same geometry rules as the batch-1 launch.
+template <int G, bool ZEROS, int CG>
+static int launch_gemv_batch(LinearArgs a, cudaStream_t st) {
+  static thread_local int configured_dev[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured_dev[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemv2b_batch<G, ZEROS, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         227 * 1024);
+    if (e != cudaSuccess) return set_cuda_error(e);
+    configured_dev[dev] = 1;
+  }
+  const int S = gemv_S(a.K);
+  const int ntiles = ceil_div(a.N, kRows);
+  auto plan = [&](int budget, int& groups, int& tpg) {
+    groups = std::max(1, std::min(std::max(budget, 1), ceil_div(ntiles, kCWarps)));
+    tpg = ceil_div(ntiles, groups);
+    groups = ceil_div(ntiles, tpg);
+    return gemv_batch_smem_layout(CG, ZEROS, a.K, G, S, a.n_out, a.ldo, tpg).total;
+  };
+  int groups = 0, tpg = 0;
+  int64_t smem = plan(1 << 20, groups, tpg);
+  for (int pass = 0; pass < 3; ++pass) {
+    if (smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
+    int g2 = 0, t2 = 0;
+    const int64_t s2 = plan(max_active_clusters_of(reinterpret_cast<const void*>(k_gemv2b_batch<G, ZEROS, CG>), S, smem),
+                            g2, t2);
+    if (g2 == groups) break;
+    groups = g2;
+    tpg = t2;
+    smem = s2;
+  }
+  if (smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
+  a.tiles_per_group = tpg;
+  return set_cuda_error(launch_pdl(k_gemv2b_batch<G, ZEROS, CG>, dim3((unsigned)(groups * S)), dim3(kThreads),
+                                   (size_t)smem, st, (unsigned)S, a));
 }
 
 static int launch_generic(const LinearArgs& a, cudaStream_t st) {
@@ -962,6 +1389,34 @@ static int fast_variant(const LinearArgs& a, uint32_t flags) {
   return (a.G >= 32) ? a.G : 0;
 }
 
+// Batched tensor-pipe variant: the group size (64, 128, 256) when 2 <= M <= 8 and the layer
+// otherwise qualifies for the tensor-pipe path (no fused input transform), else 0.
+static int batch_variant(const LinearArgs& a, uint32_t flags) {
+  if (a.M < 2 || a.M > 8 || a.G < 64 || a.xop != OTF_XOP_NONE) return 0;
+  LinearArgs one = a;
+  one.M = 1;
+  const auto al = [](int64_t v, int n) { return v % n == 0; };
+  if (!al(a.ldx * 2, 16)) return 0;  // every activation row 16-byte aligned
+  return fast_variant(one, flags);
+}
+
+static int launch_batch(const LinearArgs& a, int G, cudaStream_t s) {
+  const bool z = a.zeros != nullptr;
+  const bool one = a.M <= 4;
+  switch (G) {
+    case 64:
+      return z ? (one ? launch_gemv_batch<64, true, 1>(a, s) : launch_gemv_batch<64, true, 2>(a, s))
+               : (one ? launch_gemv_batch<64, false, 1>(a, s) : launch_gemv_batch<64, false, 2>(a, s));
+    case 128:
+      return z ? (one ? launch_gemv_batch<128, true, 1>(a, s) : launch_gemv_batch<128, true, 2>(a, s))
+               : (one ? launch_gemv_batch<128, false, 1>(a, s) : launch_gemv_batch<128, false, 2>(a, s));
+    case 256:
+      return z ? (one ? launch_gemv_batch<256, true, 1>(a, s) : launch_gemv_batch<256, true, 2>(a, s))
+               : (one ? launch_gemv_batch<256, false, 1>(a, s) : launch_gemv_batch<256, false, 2>(a, s));
+    default: return OTF_ERR_UNSUPPORTED;
+  }
+}
+
 // One layer on the tensor-pipe kernel for group size G (from fast_variant); UNSUPPORTED if G is 0.
 static int launch_fast(const LinearArgs& a, int G, cudaStream_t s) {
   const bool z = a.zeros != nullptr;
@@ -990,7 +1445,25 @@ extern "C" OTF_API int otf2b_linear(const void* x, int64_t ldx, const uint8_t* p
   if (st != OTF_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = OTF_ERR_UNSUPPORTED;
-  rc = launch_fast(a, fast_variant(a, flags), s);
+  if (a.M == 1) {
+    rc = launch_fast(a, fast_variant(a, flags), s);
+  } else {
+    // Batches of up to 8 rows on the batched tensor-pipe kernel; larger batches in slices of 8.
+    LinearArgs probe = a;
+    probe.M = std::min(a.M, 8);
+    const int Gb = batch_variant(probe, flags);
+    if (Gb != 0) {
+      rc = OTF_OK;
+      for (int m0 = 0; m0 < a.M && rc == OTF_OK; m0 += 8) {
+        LinearArgs s8 = a;
+        s8.M = std::min(8, a.M - m0);
+        s8.x = a.x + (int64_t)m0 * a.ldx;
+        s8.y = a.y + (int64_t)m0 * a.ldy;
+        if (a.res) s8.res = a.res + (int64_t)m0 * a.ldr;
+        rc = s8.M == 1 ? launch_fast(s8, fast_variant(s8, flags), s) : launch_batch(s8, Gb, s);
+      }
+    }
+  }
   if (rc != OTF_ERR_UNSUPPORTED) return rc;
   return launch_generic(a, s);
 }
