@@ -164,6 +164,8 @@ def run_reference(args, cfg):
     if rank != 0:
         return
     from oracle import oracle
+    # Every host core (torchrun sets OMP_NUM_THREADS=1 for its workers; rank 0 runs alone here).
+    oracle.set_num_threads(os.cpu_count() or 1)
     cores = oracle.num_threads()
     vals = []
     for i in range(args.warmup + args.steps):
@@ -201,7 +203,8 @@ def run_b200(args, cfg):
 
     stack = Llama2BitLinearStack(cfg, device=dev, seed=1, rank=rank, world=world, process_group=pg)
     graph = DecodeGraph(stack)
-    lin_graph = DecodeGraph(stack, linears_only=True) if world == 1 else None
+    # The 2-bit projections alone (no norm/SiLU, no all-reduce): per-rank kernel time for the roofline.
+    lin_graph = DecodeGraph(stack, linears_only=True, collectives=False)
     torch.cuda.synchronize()
 
     bytes_tok_rank = stack.bytes_per_token()

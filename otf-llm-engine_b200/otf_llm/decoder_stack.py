@@ -203,8 +203,11 @@ class Llama2BitLinearStack(nn.Module):
             cur = b["h2"]
         return cur
 
-    def forward(self, h: torch.Tensor, linears_only: bool = False) -> torch.Tensor:
-        """One decode step for h [1, hidden] fp16; returns the new residual stream."""
+    def forward(self, h: torch.Tensor, linears_only: bool = False, collectives: bool = True) -> torch.Tensor:
+        """One decode step for h [1, hidden] fp16; returns the new residual stream.
+
+        linears_only drops RMSNorm and SiLU (the 2-bit projections alone, for the roofline);
+        collectives=False also drops the tensor-parallel all-reduces (per-rank kernel time)."""
         if self.fused and not linears_only:
             return self._forward_fused(h)
         b = self._buf
@@ -217,14 +220,14 @@ class Llama2BitLinearStack(nn.Module):
             attn = self._attn_passthrough(v, b["attn"])
             tp = self.world > 1
             h1 = self._lin(layer["o_proj"], attn, b["h1"], residual=None if (tp and self.rank) else cur)
-            if tp:
+            if tp and collectives:
                 torch.distributed.all_reduce(h1, group=self.pg)
             xn = h1 if linears_only else _native.rmsnorm(h1, self.norm_w, self.cfg.rms_eps, out=b["xn"])
             g = self._lin(layer["gate_proj"], xn, b["g"])
             u = self._lin(layer["up_proj"], xn, b["u"])
             a = g if linears_only else _native.silu_mul(g, u, out=b["a"])
             h2 = self._lin(layer["down_proj"], a, b["h2"], residual=None if (tp and self.rank) else h1)
-            if tp:
+            if tp and collectives:
                 torch.distributed.all_reduce(h2, group=self.pg)
             cur = h2
         return cur
@@ -233,7 +236,7 @@ class Llama2BitLinearStack(nn.Module):
 class DecodeGraph:
     """One decode step of a stack captured as a CUDA graph with static input/output."""
 
-    def __init__(self, stack: Llama2BitLinearStack, linears_only: bool = False):
+    def __init__(self, stack: Llama2BitLinearStack, linears_only: bool = False, collectives: bool = True):
         dev = stack.norm_w.device
         self.stack = stack
         self.x = torch.zeros(1, stack.cfg.hidden, dtype=torch.float16, device=dev)
@@ -242,12 +245,12 @@ class DecodeGraph:
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
             for _ in range(2):
-                self.y.copy_(stack(self.x, linears_only))
+                self.y.copy_(stack(self.x, linears_only, collectives))
         torch.cuda.current_stream(dev).wait_stream(s)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self.y.copy_(stack(self.x, linears_only))
+            self.y.copy_(stack(self.x, linears_only, collectives))
         torch.cuda.synchronize(dev)
 
     def replay(self) -> None:
