@@ -101,6 +101,33 @@ OTF_API int otf2b_linear(const void* x, int64_t ldx,
                          uint32_t flags, void* stream);
 
 /*
+ * Batched and prefill 2-bit linear on the 5th-generation tensor cores: same arguments,
+ * layouts and semantics as otf2b_linear, any M >= 1, any codebook.  The weights are
+ * dequantised per 64-code tile to fp16 exactly as the reference's LUT path does
+ * (fp16(c[q] * s), or fp32 s*c[q] + z rounded to fp16 for the asymmetric layout) and
+ * multiplied by tcgen05.mma (fp32 accumulation in tensor memory); the fp16 anchors are
+ * extra K tiles of the same accumulation.  otf2b_linear routes M >= 32 here by itself.
+ * Needs 16-byte aligned x rows (ldx % 8 == 0), code rows (ld_packed % 16 == 0) and mask,
+ * even scale strides and G in {32, 64, 128, 256}; OTF_ERR_UNSUPPORTED otherwise.
+ * Replaces: the LUT dequant + torch matmul of triton_symmetric_2bit_gemm for M > 1
+ * (otf_llm/otf_triton_2bit_kernel.py:188-194) and OTF2BitLinear.forward's batched path
+ * (otf_llm/otf_2bit_quantizer.py:193-221).
+ */
+OTF_API int otf2b_gemm_mma(const void* x, int64_t ldx,
+                           const uint8_t* packed, int64_t ld_packed,
+                           const void* scales, int64_t ld_scales,
+                           const void* zeros, int64_t ld_zeros,
+                           const float* codebook,
+                           const void* mask,
+                           const int64_t* outlier_idx, int64_t n_outliers,
+                           const void* outlier_vals, int64_t ld_outlier_vals,
+                           const void* bias,
+                           const void* residual, int64_t ld_residual,
+                           void* y, int64_t ldy,
+                           int64_t M, int64_t N, int64_t K, int64_t group_size,
+                           uint32_t flags, void* stream);
+
+/*
  * One layer of a grouped decode launch (batch 1).  Fields mean what the arguments of
  * otf2b_linear mean; x_op transforms x while the kernel stages it (this package's fusion
  * of the Llama decoder step around the reference's projections):

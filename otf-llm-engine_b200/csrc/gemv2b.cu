@@ -1028,6 +1028,271 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) k_gemv2b_batch(const __gri
   gemv_batch_body<G, ZEROS, CG>(a, (int)(blockIdx.x / cs));
 }
 
+// ---------------------------------------------------------------------------------------
+// Batched and prefill shapes (M >= 16 activation rows) on the 5th-generation tensor cores:
+// a real dense contraction, so the weights are dequantised to fp16 tiles in shared memory
+// and multiplied by tcgen05.mma (kind::f16, fp32 accumulator in tensor memory).
+//
+// CTA = 128 weight rows (the MMA M) x NB activation rows (the MMA N), 128 threads.  Per
+// 64-code K tile: cp.async brings the rows' 16 code bytes, the scale (and zero-point) pair,
+// the mask slice and the x tile (x lands directly in the 128-byte-swizzled K-major B layout);
+// thread r then dequantises row r -- W = fp16(c[q] * s) through a byte-permute table, the
+// reference's own fp16 dequant (fp32 c*s + z for the asymmetric layout), times the mask --
+// into the swizzled A tile; one thread issues four K=16 MMAs and commits them to the slot's
+// mbarrier, so the tensor core runs while the next tile is dequantised.  The fp16 anchors are
+// extra K tiles of the same accumulation: A = the anchor weights of the rows, B = x gathered
+// at the anchor columns.  The epilogue reads the accumulator with tcgen05.ld and adds bias
+// and residual.
+constexpr int kTcMinRows = 32;    // activation rows from which a layer runs on the tcgen05 GEMM
+namespace tc {
+constexpr int kRowsT = 128;       // weight rows per CTA = MMA M
+constexpr int kKT = 64;           // codes per K tile: one 128-byte row of fp16
+constexpr int kSlotsT = 4;        // A/B tile slots
+constexpr int kDistT = 2;         // copy prefetch distance (tiles)
+constexpr int kThreadsT = 128;
+}  // namespace tc
+
+struct TcSmem {
+  int64_t a, b, codes, scl, msk, sel, bars, tptr, total;
+};
+
+__host__ __device__ inline TcSmem tc_smem_layout(int nb) {
+  TcSmem L;
+  int64_t off = 0;
+  L.a = off;     off += (int64_t)tc::kSlotsT * tc::kRowsT * 128;  // 16 KB per slot, 1024-aligned
+  L.b = off;     off += (int64_t)tc::kSlotsT * nb * 128;          // nb rows x 128 B per slot
+  L.codes = off; off += (int64_t)tc::kSlotsT * tc::kRowsT * 16;   // 16 code bytes per row
+  L.scl = off;   off += (int64_t)tc::kSlotsT * tc::kRowsT * 8;    // scale pair and zero pair per row
+  L.msk = off;   off += (int64_t)tc::kSlotsT * 128;               // 64 mask values
+  L.sel = off;   off += 256 * 4;                                  // byte -> two permute selectors
+  L.bars = off;  off += tc::kSlotsT * 8;
+  L.tptr = off;  off += 16;
+  L.total = off;
+  return L;
+}
+
+// Byte-permute selector picking fp16 entries qa and qb of a 4-entry table held in two words.
+__host__ __device__ constexpr uint32_t pair_selector(uint32_t qa, uint32_t qb) {
+  return (2 * qa) | ((2 * qa + 1) << 4) | ((2 * qb) << 8) | ((2 * qb + 1) << 12);
+}
+
+template <int G, bool ZEROS, int NB>
+__global__ void __launch_bounds__(tc::kThreadsT, 1) k_gemm2b_tc(const __grid_constant__ LinearArgs a) {
+  using namespace tc;
+  constexpr int NCOLS = NB < 32 ? 32 : NB;        // tensor-memory columns (power of two >= 32)
+  // Instruction descriptor, kind::f16: D fp32, A and B fp16, both K-major, N = NB, M = 128.
+  constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(kRowsT >> 4) << 24);
+  static_assert(NB % 16 == 0 && NB >= 16 && NB <= 256, "MMA N");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // The 128-byte swizzle is keyed to absolute shared-memory address bits: start the tiles on a
+  // 1024-byte boundary (the launch adds 1 KB of slack).
+  uint8_t* const smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const TcSmem L = tc_smem_layout(NB);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int N = a.N, K = a.K, M = a.M;
+  const int row0 = blockIdx.x * kRowsT, m0 = blockIdx.y * NB;
+  const int nkt = ceil_div(K, kKT);
+  const int nat = ceil_div(a.n_out, kKT);          // anchor tiles
+  const int ntiles = nkt + nat;
+  const int ngrp = K / G;
+  uint32_t* sel = reinterpret_cast<uint32_t*>(smem + L.sel);
+  const uint32_t bars = smem_u32(smem + L.bars);
+
+  pdl_trigger();
+  for (int v = tid; v < 256; v += kThreadsT)
+    sel[v] = pair_selector(v & 3, (v >> 2) & 3) | (pair_selector((v >> 4) & 3, (v >> 6) & 3) << 16);
+  if (tid == 0) {
+    for (int s = 0; s < kSlotsT; ++s) mbar_init(bars + 8 * s, 1);
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(smem + L.tptr), NCOLS);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L.tptr);
+  pdl_wait();
+
+  // Copies of K tile t (t < nkt) into slot t % 4.
+  const int r = tid;                               // the weight row this thread dequantises
+  const int grow = row0 + r;
+  const bool rok = grow < N;
+  auto issue = [&](int t) {
+    const int slot = t & (kSlotsT - 1);
+    const int kb = t * (kKT / 4);                  // code byte offset of the tile in a row
+    const uint32_t ncb = rok ? (uint32_t)max(0, min(16, K / 4 - kb)) : 0u;
+    cp_async16(smem_u32(smem + L.codes + (slot * kRowsT + r) * 16), ncb ? a.packed + (int64_t)grow * a.ldp + kb : a.packed,
+               ncb);
+    const int gp = ((t * kKT) / G) & ~1;            // even group holding (or preceding) the tile's first group
+    const uint32_t nsb = rok ? (uint32_t)max(0, min(4, 2 * (ngrp - gp))) : 0u;
+    cp_async4(smem_u32(smem + L.scl + (slot * kRowsT + r) * 8), nsb ? a.scales + (int64_t)grow * a.lds + gp : a.scales,
+              nsb);
+    if constexpr (ZEROS)
+      cp_async4(smem_u32(smem + L.scl + (slot * kRowsT + r) * 8 + 4),
+                nsb ? a.zeros + (int64_t)grow * a.ldz + gp : a.zeros, nsb);
+    if (a.mask && tid < 8) {
+      const int k = t * kKT + 8 * tid;
+      const uint32_t nmb = (uint32_t)max(0, min(16, 2 * (K - k)));
+      cp_async16(smem_u32(smem + L.msk + slot * 128 + 16 * tid), nmb ? a.mask + k : a.mask, nmb);
+    }
+    // x tile: NB rows x 8 pieces of 16 bytes, swizzled (piece c of row n at c ^ (n & 7)).
+    uint8_t* bslot = smem + L.b + (int64_t)slot * NB * 128;
+    for (int i = tid; i < NB * 8; i += kThreadsT) {
+      const int n = i >> 3, c = i & 7;
+      const int k = t * kKT + 8 * c;
+      const uint32_t nxb = (m0 + n < M) ? (uint32_t)max(0, min(16, 2 * (K - k))) : 0u;
+      cp_async16(smem_u32(bslot + n * 128 + ((c ^ (n & 7)) << 4)),
+                 nxb ? a.x + (int64_t)(m0 + n) * a.ldx + k : a.x, nxb);
+    }
+  };
+  for (int t = 0; t < kDistT; ++t) {
+    if (t < nkt) issue(t);
+    cp_async_commit();
+  }
+
+  // fp16 codebook entries (the reference's dequant multiplies these by the fp16 scale).
+  const __half cbh[4] = {__float2half_rn(a.c0), __float2half_rn(a.c1), __float2half_rn(a.c2), __float2half_rn(a.c3)};
+  const uint32_t a_swz_row = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+  for (int t = 0; t < ntiles; ++t) {
+    const int slot = t & (kSlotsT - 1);
+    // Slot of tile t+2 was last read by the MMAs of tile t-2: wait for them, then refill it.
+    if (t + kDistT < ntiles && t >= kDistT) {
+      const int tp = t - kDistT;
+      if (!mbar_wait(bars + 8 * (tp & (kSlotsT - 1)), (uint32_t)(tp >> 2) & 1u)) report_wait_failure();
+    }
+    if (t + kDistT < nkt) issue(t + kDistT);
+    cp_async_commit();
+    cp_async_wait<kDistT>();
+    __syncthreads();
+    uint8_t* aslot = smem + L.a + (int64_t)slot * kRowsT * 128;
+    uint8_t* bslot = smem + L.b + (int64_t)slot * NB * 128;
+    if (t < nkt) {
+      // Dequantise row r of the tile: 64 codes -> 64 fp16 in 8 pieces of 16 bytes.
+      const uint4 cw = *reinterpret_cast<const uint4*>(smem + L.codes + (slot * kRowsT + r) * 16);
+      const uint32_t sp = *reinterpret_cast<const uint32_t*>(smem + L.scl + (slot * kRowsT + r) * 8);
+      const uint32_t zp = ZEROS ? *reinterpret_cast<const uint32_t*>(smem + L.scl + (slot * kRowsT + r) * 8 + 4) : 0u;
+      const int g_first = (t * kKT) / G;
+      uint32_t lut[2][2];                          // [scale group half][table word]
+#pragma unroll
+      for (int hsel = 0; hsel < 2; ++hsel) {
+        // Codes [32*hsel, 32*hsel + 32) of the tile belong to group g_first + (G == 32 ? hsel : 0).
+        const int gi = g_first + ((G == 32) ? hsel : 0);
+        const uint16_t sb = (uint16_t)((gi & 1) ? (sp >> 16) : (sp & 0xFFFFu));
+        __half e[4];
+        if constexpr (ZEROS) {
+          const uint16_t zb = (uint16_t)((gi & 1) ? (zp >> 16) : (zp & 0xFFFFu));
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            e[q] = __float2half_rn(fmaf(__half2float(cbh[q]), h2f(sb), h2f(zb)));
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) e[q] = __hmul(cbh[q], __ushort_as_half(sb));
+        }
+        lut[hsel][0] = (uint32_t)__half_as_ushort(e[0]) | ((uint32_t)__half_as_ushort(e[1]) << 16);
+        lut[hsel][1] = (uint32_t)__half_as_ushort(e[2]) | ((uint32_t)__half_as_ushort(e[3]) << 16);
+      }
+      const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {                // piece c: code bytes 2c, 2c+1 -> 8 fp16
+        const int hsel = c >> 2;
+        uint32_t o[4];
+#pragma unroll
+        for (int bb = 0; bb < 2; ++bb) {
+          const uint32_t byte = (words[c >> 1] >> (8 * (2 * (c & 1) + bb))) & 0xFFu;
+          const uint32_t sv = sel[byte];
+          o[2 * bb] = __byte_perm(lut[hsel][0], lut[hsel][1], sv & 0xFFFFu);
+          o[2 * bb + 1] = __byte_perm(lut[hsel][0], lut[hsel][1], sv >> 16);
+        }
+        if (a.mask) {
+          const uint4 mv = *reinterpret_cast<const uint4*>(smem + L.msk + slot * 128 + 16 * c);
+          const uint32_t mw[4] = {mv.x, mv.y, mv.z, mv.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const __half2 pr = __hmul2(*reinterpret_cast<const __half2*>(&o[i]), *reinterpret_cast<const __half2*>(&mw[i]));
+            o[i] = *reinterpret_cast<const uint32_t*>(&pr);
+          }
+        }
+        *reinterpret_cast<uint4*>(aslot + a_swz_row + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    } else {
+      // Anchor tile: A row r = the row's anchor weights [64*ta, 64*ta + 64), B row n = x of
+      // activation row m0+n at those anchor columns; zeros past n_out.
+      const int ta = t - nkt;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int j0 = ta * kKT + 8 * c + 2 * i;
+          const uint32_t lo = (rok && j0 < a.n_out) ? ldg_u16(a.ovals + (int64_t)grow * a.ldo + j0) : 0u;
+          const uint32_t hi = (rok && j0 + 1 < a.n_out) ? ldg_u16(a.ovals + (int64_t)grow * a.ldo + j0 + 1) : 0u;
+          o[i] = lo | (hi << 16);
+        }
+        *reinterpret_cast<uint4*>(aslot + a_swz_row + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      for (int i = tid; i < NB * 8; i += kThreadsT) {
+        const int n = i >> 3, c = i & 7;
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int j0 = ta * kKT + 8 * c + 2 * q;
+          const bool mok = m0 + n < M;
+          const uint32_t lo = (mok && j0 < a.n_out) ? ldg_u16(a.x + (int64_t)(m0 + n) * a.ldx + __ldg(a.oidx + j0)) : 0u;
+          const uint32_t hi =
+              (mok && j0 + 1 < a.n_out) ? ldg_u16(a.x + (int64_t)(m0 + n) * a.ldx + __ldg(a.oidx + j0 + 1)) : 0u;
+          o[q] = lo | (hi << 16);
+        }
+        *reinterpret_cast<uint4*>(bslot + n * 128 + ((c ^ (n & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    // Generic-proxy stores (and landed copies) must be visible to the tensor core's reads.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after_sync();
+      const uint32_t abase = smem_u32(aslot), bbase = smem_u32(bslot);
+#pragma unroll
+      for (int kk = 0; kk < kKT / 16; ++kk)
+        tc_mma_f16(tmem, tc_desc_sw128(abase + 32 * kk), tc_desc_sw128(bbase + 32 * kk), kIdesc,
+                   (t > 0 || kk > 0) ? 1u : 0u);
+      tc_commit(bars + 8 * slot);
+    }
+  }
+  cp_async_wait<0>();
+  // The last commit covers every MMA: wait for it, then read the accumulator.
+  {
+    const int tl = ntiles - 1;
+    if (!mbar_wait(bars + 8 * (tl & (kSlotsT - 1)), (uint32_t)(tl >> 2) & 1u)) report_wait_failure();
+  }
+  tc_fence_after_sync();
+  // Warp w reads tensor-memory lanes 32w..32w+31 = weight rows row0 + 32w + lane.
+  const int orow = row0 + 32 * warp + lane;
+  const bool ook = orow < N;
+  const float bias = (ook && a.bias) ? h2f(ldg_u16(a.bias + orow)) : 0.0f;
+#pragma unroll 1
+  for (int c0 = 0; c0 < NB; c0 += 8) {
+    uint32_t v[8];
+    tmem_ld8(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int m = m0 + c0 + j;
+      if (ook && m < M) {
+        float yv = __uint_as_float(v[j]) + bias;
+        if (a.res) yv += h2f(ldg_u16(a.res + (int64_t)m * a.ldr + orow));
+        if (a.clamp) yv = fminf(fmaxf(yv, -65504.0f), 65504.0f);
+        a.y[(int64_t)m * a.ldy + orow] = f2h(yv);
+      }
+    }
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, NCOLS);
+}
+
 // Portable CUDA-core kernel: any M, any G dividing K with G % 4 == 0, any codebook.
 // One warp per output row, lanes stride over packed bytes; MT activation rows per launch.
 template <int MT>
@@ -1309,6 +1574,22 @@ static int launch_gemv_batch(LinearArgs a, cudaStream_t st) {
                                    (size_t)smem, st, (unsigned)S, a));
 }
 
+template <int G, bool ZEROS, int NB>
+static int launch_gemm_tc(const LinearArgs& a, cudaStream_t st) {
+  const int64_t smem = tc_smem_layout(NB).total + 1024;
+  static thread_local int configured_dev[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured_dev[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm2b_tc<G, ZEROS, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return set_cuda_error(e);
+    configured_dev[dev] = 1;
+  }
+  const dim3 grid((unsigned)ceil_div(a.N, tc::kRowsT), (unsigned)ceil_div(a.M, NB));
+  return set_cuda_error(launch_pdl(k_gemm2b_tc<G, ZEROS, NB>, grid, dim3(tc::kThreadsT), (size_t)smem, st, 1u, a));
+}
+
 static int launch_generic(const LinearArgs& a, cudaStream_t st) {
   const int ctas = ceil_div(a.N, 8);
   for (int m0 = 0; m0 < a.M; m0 += 4) {
@@ -1389,6 +1670,37 @@ static int fast_variant(const LinearArgs& a, uint32_t flags) {
   return (a.G >= 32) ? a.G : 0;
 }
 
+// tcgen05 GEMM variant: the group size (32, 64, 128, 256) when the rows, vectors and strides are
+// aligned for its copies (any codebook: the dequant is a table lookup), else 0.
+static int tc_variant(const LinearArgs& a) {
+  const auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
+  const auto al = [](const void* p, int n) { return reinterpret_cast<uintptr_t>(p) % n == 0; };
+  const bool ok = al(a.x, 16) && a.ldx % 8 == 0 && (!a.mask || al(a.mask, 16)) && al(a.packed, 16) &&
+                  a.ldp % 16 == 0 && al(a.scales, 4) && a.lds % 2 == 0 &&
+                  (!a.zeros || (al(a.zeros, 4) && a.ldz % 2 == 0)) && a.xop == OTF_XOP_NONE;
+  if (!ok || !pow2(a.G) || a.G < 32 || a.G > 256) return 0;
+  return a.G;
+}
+
+template <int G, bool ZEROS>
+static int launch_tc_g(const LinearArgs& a, cudaStream_t s) {
+  if (a.M <= 16) return launch_gemm_tc<G, ZEROS, 16>(a, s);
+  if (a.M <= 32) return launch_gemm_tc<G, ZEROS, 32>(a, s);
+  if (a.M <= 64) return launch_gemm_tc<G, ZEROS, 64>(a, s);
+  return launch_gemm_tc<G, ZEROS, 128>(a, s);
+}
+
+static int launch_tc(const LinearArgs& a, int G, cudaStream_t s) {
+  const bool z = a.zeros != nullptr;
+  switch (G) {
+    case 32: return z ? launch_tc_g<32, true>(a, s) : launch_tc_g<32, false>(a, s);
+    case 64: return z ? launch_tc_g<64, true>(a, s) : launch_tc_g<64, false>(a, s);
+    case 128: return z ? launch_tc_g<128, true>(a, s) : launch_tc_g<128, false>(a, s);
+    case 256: return z ? launch_tc_g<256, true>(a, s) : launch_tc_g<256, false>(a, s);
+    default: return OTF_ERR_UNSUPPORTED;
+  }
+}
+
 // Batched tensor-pipe variant: the group size (64, 128, 256) when 2 <= M <= 8 and the layer
 // otherwise qualifies for the tensor-pipe path (no fused input transform), else 0.
 static int batch_variant(const LinearArgs& a, uint32_t flags) {
@@ -1445,7 +1757,10 @@ extern "C" OTF_API int otf2b_linear(const void* x, int64_t ldx, const uint8_t* p
   if (st != OTF_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = OTF_ERR_UNSUPPORTED;
-  if (a.M == 1) {
+  const int Gt = (a.M >= kTcMinRows && !(flags & OTF_FLAG_FORCE_GENERIC)) ? tc_variant(a) : 0;
+  if (Gt != 0) {
+    rc = launch_tc(a, Gt, s);
+  } else if (a.M == 1) {
     rc = launch_fast(a, fast_variant(a, flags), s);
   } else {
     // Batches of up to 8 rows on the batched tensor-pipe kernel; larger batches in slices of 8.
@@ -1466,6 +1781,25 @@ extern "C" OTF_API int otf2b_linear(const void* x, int64_t ldx, const uint8_t* p
   }
   if (rc != OTF_ERR_UNSUPPORTED) return rc;
   return launch_generic(a, s);
+}
+
+extern "C" OTF_API int otf2b_gemm_mma(const void* x, int64_t ldx, const uint8_t* packed, int64_t ld_packed,
+                                      const void* scales, int64_t ld_scales, const void* zeros, int64_t ld_zeros,
+                                      const float* codebook, const void* mask, const int64_t* outlier_idx,
+                                      int64_t n_outliers, const void* outlier_vals, int64_t ld_outlier_vals,
+                                      const void* bias, const void* residual, int64_t ld_residual, void* y,
+                                      int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size,
+                                      uint32_t flags, void* stream) {
+  LinearArgs a;
+  int st = build_args(a, x, ldx, packed, ld_packed, scales, ld_scales, zeros, ld_zeros, codebook, mask, outlier_idx,
+                      n_outliers, outlier_vals, ld_outlier_vals, bias, residual, ld_residual, y, ldy, M, N, K,
+                      group_size, flags);
+  if (st != OTF_OK) return st;
+  st = check_device();
+  if (st != OTF_OK) return st;
+  const int G = tc_variant(a);
+  if (G == 0) return OTF_ERR_UNSUPPORTED;
+  return launch_tc(a, G, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" OTF_API int otf2b_linear_group(const otf2b_layer* layers, int n_layers, void* stream) {

@@ -52,6 +52,7 @@ EXPORTS = (
     "otf_last_cuda_error",
     "otf_device_error",
     "otf2b_linear",
+    "otf2b_gemm_mma",
     "otf2b_linear_group",
     "otf2b_unpack_codes",
     "otf_i8_head",
@@ -85,6 +86,8 @@ def lib() -> ctypes.CDLL:
     L.otf2b_linear.argtypes = [vp, i64, vp, i64, vp, i64, vp, i64, vp, vp, vp, i64, vp, i64, vp, vp, i64, vp, i64,
                                i64, i64, i64, i64, u32, vp]
     L.otf2b_linear.restype = i32
+    L.otf2b_gemm_mma.argtypes = L.otf2b_linear.argtypes
+    L.otf2b_gemm_mma.restype = i32
     L.otf2b_linear_group.argtypes = [ctypes.POINTER(Layer), ctypes.c_int, vp]
     L.otf2b_linear_group.restype = i32
     L.otf2b_unpack_codes.argtypes = [vp, i64, i64, i64, vp, i64, vp]
@@ -165,8 +168,12 @@ def linear_2bit(x2d: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, g
                 *, zeros: Optional[torch.Tensor] = None, mask: Optional[torch.Tensor] = None,
                 outlier_idx: Optional[torch.Tensor] = None, outlier_vals: Optional[torch.Tensor] = None,
                 bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None, clamp: bool = True,
-                out: Optional[torch.Tensor] = None, force_generic: bool = False) -> torch.Tensor:
-    """y[M, N] fp16 = fused 2-bit linear over x2d [M, K] fp16 (see otf2b_linear)."""
+                out: Optional[torch.Tensor] = None, force_generic: bool = False,
+                gemm_mma: bool = False) -> torch.Tensor:
+    """y[M, N] fp16 = fused 2-bit linear over x2d [M, K] fp16 (see otf2b_linear).
+
+    gemm_mma=True forces the tcgen05 dequant GEMM (otf2b_gemm_mma) whatever M is; otherwise
+    the library picks the kernel (tcgen05 GEMM from 32 activation rows)."""
     _need_cuda(x2d, "x")
     dev = x2d.device
     M, K = x2d.shape
@@ -212,10 +219,11 @@ def linear_2bit(x2d: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, g
     cb = (ctypes.c_float * 4)(*codebook_floats(codebook4))
     flags = (OTF_FLAG_CLAMP if clamp else 0) | (OTF_FLAG_FORCE_GENERIC if force_generic else 0)
     with torch.cuda.device(dev):
-        st = lib().otf2b_linear(_ptr(x2d), ldx, _ptr(packed), ldp, _ptr(scales), lds, _ptr(zeros), ldz, cb,
-                                _ptr(mask), _ptr(outlier_idx), n_out, _ptr(outlier_vals), ldo, _ptr(bias),
-                                _ptr(residual), ldr, _ptr(out), ldy, M, N, K, group_size, flags, _stream(dev))
-    _check(st, "otf2b_linear")
+        fn = lib().otf2b_gemm_mma if gemm_mma else lib().otf2b_linear
+        st = fn(_ptr(x2d), ldx, _ptr(packed), ldp, _ptr(scales), lds, _ptr(zeros), ldz, cb,
+                _ptr(mask), _ptr(outlier_idx), n_out, _ptr(outlier_vals), ldo, _ptr(bias),
+                _ptr(residual), ldr, _ptr(out), ldy, M, N, K, group_size, flags, _stream(dev))
+    _check(st, "otf2b_gemm_mma" if gemm_mma else "otf2b_linear")
     return out
 
 
