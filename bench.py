@@ -347,6 +347,75 @@ def run_case(args):
                       "GBps_l2_warm": round(nbytes / us / 1e3, 1)}), flush=True)
 
 
+def run_sweep(args):
+    """Batch sweep of the skinny 2-bit GEMM at Llama-3-70B MLP shapes (K=8192 -> N=28672 and
+    K=28672 -> N=8192, B in 1..64): one JSON line per (shape, B).  Codes/scales/anchors are
+    uniform random (the kernels' time does not depend on the values); four weight copies
+    rotate (235 MB > L2); CUDA graphs of the rotating launches, CUDA events."""
+    import torch
+    from otf_llm import _native
+    from otf_llm.decoder_stack import linear_bytes
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(0)
+
+    def layer(N, K, G=64):
+        k = max(1, int(K * 0.005))
+        packed = torch.randint(0, 256, (N, K // 4), dtype=torch.uint8, device=dev, generator=gen)
+        scales = (torch.rand(N, K // G, device=dev, generator=gen) * 0.03 + 0.002).half()
+        idx = torch.randperm(K, device=dev, generator=gen)[:k]
+        ov = (torch.randn(N, k, device=dev, generator=gen) * 0.05).half()
+        mask = torch.ones(K, dtype=torch.float16, device=dev)
+        mask[idx] = 0
+        return packed, scales, idx, ov, mask
+
+    for (N, K) in [(28672, 8192), (8192, 28672)]:
+        R = 4
+        Ls = [layer(N, K) for _ in range(R)]
+        for M in [1, 2, 4, 8, 16, 32, 64]:
+            x = torch.randn(M, K, device=dev, generator=gen).half()
+            y = torch.empty(M, N, dtype=torch.float16, device=dev)
+
+            def run(i):
+                p, sc, idx, ov, m = Ls[i % R]
+                _native.linear_2bit(x, p, sc, 64, None, mask=m, outlier_idx=idx, outlier_vals=ov, out=y)
+
+            for i in range(R):
+                run(i)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            st = torch.cuda.Stream()
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                for i in range(R):
+                    run(i)
+            torch.cuda.current_stream().wait_stream(st)
+            with torch.cuda.graph(g):
+                for i in range(R):
+                    run(i)
+            for _ in range(max(3, args.warmup)):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = max(1, args.steps // R)
+            e0.record()
+            for _ in range(reps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * R)
+            nb = linear_bytes(N, K, 64, max(1, int(K * 0.005)), batch=M)
+            kernel = ("k_gemm2b_tc (tcgen05)" if M >= 32 else "k_gemv2b" if M == 1 else
+                      "k_gemv2b_batch (8-row slices)")
+            print(json.dumps({"sweep": "70B MLP 2-bit GEMM", "N": N, "K": K, "B": M, "us": round(us, 2),
+                              "GBps": round(nb / us / 1e3, 1), "TFLOPs": round(2 * M * N * K / us / 1e6, 1),
+                              "kernel": kernel, "data": "synthetic codes/scales, 4 rotating copies",
+                              "device_error": _native.device_error(True)}), flush=True)
+            del g
+        del Ls
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None,
@@ -358,11 +427,14 @@ def main():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="batch sweep at Llama-3-70B MLP shapes (JSON lines)")
     args = ap.parse_args()
     from otf_llm.decoder_stack import StackConfig
     cfg = StackConfig(layers=args.layers)
     if args.case:
         run_case(args)
+    elif args.sweep:
+        run_sweep(args)
     elif args.impl == "reference":
         run_reference(args, cfg)
     else:

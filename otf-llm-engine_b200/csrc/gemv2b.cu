@@ -1090,9 +1090,17 @@ __global__ void __launch_bounds__(tc::kThreadsT, 1) k_gemm2b_tc(const __grid_con
   const TcSmem L = tc_smem_layout(NB);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int N = a.N, K = a.K, M = a.M;
-  const int row0 = blockIdx.x * kRowsT, m0 = blockIdx.y * NB;
-  const int nkt = ceil_div(K, kKT);
-  const int nat = ceil_div(a.n_out, kKT);          // anchor tiles
+  // Split over K: a cluster of S CTAs (S in {1, 2, 4}) shares one 128-row tile; CTA q takes
+  // K tiles [kt0, kt1) and the last CTA also the anchor tiles.
+  uint32_t csz;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(csz));
+  const int S = (int)csz;
+  const int q = (int)cluster_ctarank();
+  const int row0 = (int)(blockIdx.x / csz) * kRowsT, m0 = blockIdx.y * NB;
+  const int nkt_all = ceil_div(K, kKT);
+  const int kt0 = (int)(((int64_t)q * nkt_all) / S), kt1 = (int)(((int64_t)(q + 1) * nkt_all) / S);
+  const int nkt = kt1 - kt0;                       // my K tiles (local index t -> tile kt0 + t)
+  const int nat = (q == S - 1) ? ceil_div(a.n_out, kKT) : 0;  // anchor tiles
   const int ntiles = nkt + nat;
   const int ngrp = K / G;
   uint32_t* sel = reinterpret_cast<uint32_t*>(smem + L.sel);
@@ -1115,17 +1123,29 @@ __global__ void __launch_bounds__(tc::kThreadsT, 1) k_gemm2b_tc(const __grid_con
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L.tptr);
   pdl_wait();
 
+  // Per-thread x-copy geometry (fixed for the whole K loop).
+  const int xn0 = tid >> 3, xc = tid & 7;
+  const uint32_t xdst0 = (uint32_t)(xn0 * 128 + ((xc ^ (xn0 & 7)) << 4));
+  int64_t xoff[NB / 16];
+  uint32_t xrows = 0;
+#pragma unroll
+  for (int j = 0; j < NB / 16; ++j) {
+    const int m = m0 + xn0 + 16 * j;
+    xrows |= (m < M ? 1u : 0u) << j;
+    xoff[j] = (int64_t)(m < M ? m : 0) * a.ldx;
+  }
   // Copies of K tile t (t < nkt) into slot t % 4.
   const int r = tid;                               // the weight row this thread dequantises
   const int grow = row0 + r;
   const bool rok = grow < N;
   auto issue = [&](int t) {
     const int slot = t & (kSlotsT - 1);
-    const int kb = t * (kKT / 4);                  // code byte offset of the tile in a row
+    const int tg = kt0 + t;                        // global K tile
+    const int kb = tg * (kKT / 4);                 // code byte offset of the tile in a row
     const uint32_t ncb = rok ? (uint32_t)max(0, min(16, K / 4 - kb)) : 0u;
     cp_async16(smem_u32(smem + L.codes + (slot * kRowsT + r) * 16), ncb ? a.packed + (int64_t)grow * a.ldp + kb : a.packed,
                ncb);
-    const int gp = ((t * kKT) / G) & ~1;            // even group holding (or preceding) the tile's first group
+    const int gp = ((tg * kKT) / G) & ~1;           // even group holding (or preceding) the tile's first group
     const uint32_t nsb = rok ? (uint32_t)max(0, min(4, 2 * (ngrp - gp))) : 0u;
     cp_async4(smem_u32(smem + L.scl + (slot * kRowsT + r) * 8), nsb ? a.scales + (int64_t)grow * a.lds + gp : a.scales,
               nsb);
@@ -1133,18 +1153,21 @@ __global__ void __launch_bounds__(tc::kThreadsT, 1) k_gemm2b_tc(const __grid_con
       cp_async4(smem_u32(smem + L.scl + (slot * kRowsT + r) * 8 + 4),
                 nsb ? a.zeros + (int64_t)grow * a.ldz + gp : a.zeros, nsb);
     if (a.mask && tid < 8) {
-      const int k = t * kKT + 8 * tid;
+      const int k = tg * kKT + 8 * tid;
       const uint32_t nmb = (uint32_t)max(0, min(16, 2 * (K - k)));
       cp_async16(smem_u32(smem + L.msk + slot * 128 + 16 * tid), nmb ? a.mask + k : a.mask, nmb);
     }
     // x tile: NB rows x 8 pieces of 16 bytes, swizzled (piece c of row n at c ^ (n & 7)).
-    uint8_t* bslot = smem + L.b + (int64_t)slot * NB * 128;
-    for (int i = tid; i < NB * 8; i += kThreadsT) {
-      const int n = i >> 3, c = i & 7;
-      const int k = t * kKT + 8 * c;
-      const uint32_t nxb = (m0 + n < M) ? (uint32_t)max(0, min(16, 2 * (K - k))) : 0u;
-      cp_async16(smem_u32(bslot + n * 128 + ((c ^ (n & 7)) << 4)),
-                 nxb ? a.x + (int64_t)(m0 + n) * a.ldx + k : a.x, nxb);
+    // Thread (n0 = tid/8, c = tid%8) copies rows n0 + 16j: same swizzle, 2 KB apart.
+    const uint32_t bdst = smem_u32(smem + L.b) + (uint32_t)(slot * NB * 128) + xdst0;
+    const int kx = tg * kKT + 8 * xc;
+    const uint32_t kbytes_x = (uint32_t)max(0, min(16, 2 * (K - kx)));
+    const uint16_t* xs = a.x + kx;
+#pragma unroll
+    for (int j = 0; j < NB / 16; ++j) {
+      const uint32_t nxb = ((xrows >> j) & 1u) ? kbytes_x : 0u;
+      cp_async16(bdst + 2048u * j, nxb ? reinterpret_cast<const void*>(xs + xoff[j]) : reinterpret_cast<const void*>(a.x),
+                 nxb);
     }
   };
   for (int t = 0; t < kDistT; ++t) {
@@ -1173,10 +1196,10 @@ __global__ void __launch_bounds__(tc::kThreadsT, 1) k_gemm2b_tc(const __grid_con
       const uint4 cw = *reinterpret_cast<const uint4*>(smem + L.codes + (slot * kRowsT + r) * 16);
       const uint32_t sp = *reinterpret_cast<const uint32_t*>(smem + L.scl + (slot * kRowsT + r) * 8);
       const uint32_t zp = ZEROS ? *reinterpret_cast<const uint32_t*>(smem + L.scl + (slot * kRowsT + r) * 8 + 4) : 0u;
-      const int g_first = (t * kKT) / G;
+      const int g_first = ((kt0 + t) * kKT) / G;
       uint32_t lut[2][2];                          // [scale group half][table word]
 #pragma unroll
-      for (int hsel = 0; hsel < 2; ++hsel) {
+      for (int hsel = 0; hsel < (G == 32 ? 2 : 1); ++hsel) {
         // Codes [32*hsel, 32*hsel + 32) of the tile belong to group g_first + (G == 32 ? hsel : 0).
         const int gi = g_first + ((G == 32) ? hsel : 0);
         const uint16_t sb = (uint16_t)((gi & 1) ? (sp >> 16) : (sp & 0xFFFFu));
@@ -1193,6 +1216,10 @@ __global__ void __launch_bounds__(tc::kThreadsT, 1) k_gemm2b_tc(const __grid_con
         lut[hsel][0] = (uint32_t)__half_as_ushort(e[0]) | ((uint32_t)__half_as_ushort(e[1]) << 16);
         lut[hsel][1] = (uint32_t)__half_as_ushort(e[2]) | ((uint32_t)__half_as_ushort(e[3]) << 16);
       }
+      if constexpr (G != 32) {
+        lut[1][0] = lut[0][0];
+        lut[1][1] = lut[0][1];
+      }
       const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
       for (int c = 0; c < 8; ++c) {                // piece c: code bytes 2c, 2c+1 -> 8 fp16
@@ -1205,16 +1232,19 @@ __global__ void __launch_bounds__(tc::kThreadsT, 1) k_gemm2b_tc(const __grid_con
           o[2 * bb] = __byte_perm(lut[hsel][0], lut[hsel][1], sv & 0xFFFFu);
           o[2 * bb + 1] = __byte_perm(lut[hsel][0], lut[hsel][1], sv >> 16);
         }
-        if (a.mask) {
-          const uint4 mv = *reinterpret_cast<const uint4*>(smem + L.msk + slot * 128 + 16 * c);
-          const uint32_t mw[4] = {mv.x, mv.y, mv.z, mv.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const __half2 pr = __hmul2(*reinterpret_cast<const __half2*>(&o[i]), *reinterpret_cast<const __half2*>(&mw[i]));
-            o[i] = *reinterpret_cast<const uint32_t*>(&pr);
+        *reinterpret_cast<uint4*>(aslot + a_swz_row + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      // The mask (0 at the anchor columns, else 1) multiplies x: zero those columns of the x
+      // tile (a handful per layer) instead of scaling every weight.
+      if (a.mask && tid < kKT) {
+        const __half mv = *reinterpret_cast<const __half*>(smem + L.msk + slot * 128 + 2 * tid);
+        if (__half2float(mv) != 1.0f) {
+          const int kc = tid >> 3, ke = tid & 7;
+          for (int n = 0; n < NB; ++n) {
+            __half* e = reinterpret_cast<__half*>(bslot + n * 128 + ((kc ^ (n & 7)) << 4)) + ke;
+            *e = __hmul(*e, mv);
           }
         }
-        *reinterpret_cast<uint4*>(aslot + a_swz_row + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     } else {
       // Anchor tile: A row r = the row's anchor weights [64*ta, 64*ta + 64), B row n = x of
@@ -1263,35 +1293,68 @@ __global__ void __launch_bounds__(tc::kThreadsT, 1) k_gemm2b_tc(const __grid_con
   }
   cp_async_wait<0>();
   // The last commit covers every MMA: wait for it, then read the accumulator.
-  {
+  if (ntiles > 0) {
     const int tl = ntiles - 1;
     if (!mbar_wait(bars + 8 * (tl & (kSlotsT - 1)), (uint32_t)(tl >> 2) & 1u)) report_wait_failure();
   }
   tc_fence_after_sync();
   // Warp w reads tensor-memory lanes 32w..32w+31 = weight rows row0 + 32w + lane.
-  const int orow = row0 + 32 * warp + lane;
-  const bool ook = orow < N;
-  const float bias = (ook && a.bias) ? h2f(ldg_u16(a.bias + orow)) : 0.0f;
+  const int lrow = 32 * warp + lane;
+  const int orow = row0 + lrow;
+  auto finish = [&](int row, int m, float acc) {
+    if (row < N && m < M) {
+      float yv = acc;
+      if (a.bias) yv += h2f(ldg_u16(a.bias + row));
+      if (a.res) yv += h2f(ldg_u16(a.res + (int64_t)m * a.ldr + row));
+      if (a.clamp) yv = fminf(fmaxf(yv, -65504.0f), 65504.0f);
+      a.y[(int64_t)m * a.ldy + row] = f2h(yv);
+    }
+  };
+  if (S == 1) {
 #pragma unroll 1
-  for (int c0 = 0; c0 < NB; c0 += 8) {
-    uint32_t v[8];
-    tmem_ld8(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
-    tmem_wait_ld();
+    for (int c0 = 0; c0 < NB; c0 += 8) {
+      uint32_t v[8];
+      tmem_ld8(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
+      tmem_wait_ld();
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int m = m0 + c0 + j;
-      if (ook && m < M) {
-        float yv = __uint_as_float(v[j]) + bias;
-        if (a.res) yv += h2f(ldg_u16(a.res + (int64_t)m * a.ldr + orow));
-        if (a.clamp) yv = fminf(fmaxf(yv, -65504.0f), 65504.0f);
-        a.y[(int64_t)m * a.ldy + orow] = f2h(yv);
-      }
+      for (int j = 0; j < 8; ++j) finish(orow, m0 + c0 + j, __uint_as_float(v[j]));
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, NCOLS);
+  } else {
+    // Every CTA of the cluster is past its last MMA before any shared memory is reused.
+    cluster_sync_all();
+    // CTA o owns rows [o*128/S, (o+1)*128/S): warp w's 32 rows belong to CTA w*S/4.  Partials
+    // land in the owner's (now idle) A-tile area as recv[source][owned row][column] fp32.
+    const int rows_own = kRowsT / S;
+    const int owner = warp * S / 4;
+    float* recv = reinterpret_cast<float*>(smem + L.a);
+#pragma unroll 1
+    for (int c0 = 0; c0 < NB; c0 += 8) {
+      uint32_t v[8];
+      tmem_ld8(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
+      tmem_wait_ld();
+      const uint32_t dst = smem_u32(recv + ((q * rows_own + (lrow - owner * rows_own)) * NB + c0));
+      const uint32_t rdst = mapa_shared(dst, (uint32_t)owner);
+      asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rdst), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+                   "r"(v[3]) : "memory");
+      asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rdst + 16), "r"(v[4]), "r"(v[5]),
+                   "r"(v[6]), "r"(v[7]) : "memory");
+    }
+    tc_fence_before_sync();
+    cluster_sync_all();
+    if (warp == 0) tmem_dealloc(tmem, NCOLS);
+    // Owned rows: sum the S partials in rank order (deterministic), then the epilogue.
+    for (int i = tid; i < rows_own * NB; i += kThreadsT) {
+      const int rr = i / NB, c = i - rr * NB;
+      float acc = 0.0f;
+      for (int src = 0; src < S; ++src) acc += recv[(src * rows_own + rr) * NB + c];
+      finish(row0 + q * rows_own + rr, m0 + c, acc);
     }
   }
-  tc_fence_before_sync();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, NCOLS);
 }
+
 
 // Portable CUDA-core kernel: any M, any G dividing K with G % 4 == 0, any codebook.
 // One warp per output row, lanes stride over packed bytes; MT activation rows per launch.
@@ -1586,8 +1649,14 @@ static int launch_gemm_tc(const LinearArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return set_cuda_error(e);
     configured_dev[dev] = 1;
   }
-  const dim3 grid((unsigned)ceil_div(a.N, tc::kRowsT), (unsigned)ceil_div(a.M, NB));
-  return set_cuda_error(launch_pdl(k_gemm2b_tc<G, ZEROS, NB>, grid, dim3(tc::kThreadsT), (size_t)smem, st, 1u, a));
+  // Split K over a cluster of S in {1, 2, 4} CTAs while the grid is under two CTAs per SM and
+  // every CTA keeps at least 8 K tiles.
+  const int rt = ceil_div(a.N, tc::kRowsT), bt = ceil_div(a.M, NB), nkt = ceil_div(a.K, tc::kKT);
+  int S = 1;
+  while (S < 4 && (int64_t)rt * bt * S * 2 <= 2 * num_sms() && nkt >= 16 * S) S *= 2;
+  const dim3 grid((unsigned)(rt * S), (unsigned)bt);
+  return set_cuda_error(launch_pdl(k_gemm2b_tc<G, ZEROS, NB>, grid, dim3(tc::kThreadsT), (size_t)smem, st,
+                                   (unsigned)S, a));
 }
 
 static int launch_generic(const LinearArgs& a, cudaStream_t st) {

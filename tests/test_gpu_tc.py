@@ -50,7 +50,7 @@ def _run(N, K, G, M, n_out, zeros, bias, dev, codebook=None, forced=False, resid
     (129, 192, 32, 17, 0, False, True),
 ])
 def test_tc_gemm(N, K, G, M, n_out, zeros, bias, cuda_dev):
-    y, ref = _run(N, K, G, M, n_out, zeros, bias, cuda_dev)
+    y, ref = _run(N, K, G, M, n_out, zeros, bias, cuda_dev, forced=True)
     assert rel_err(y, ref) < TOL, (N, K, G, M, rel_err(y, ref))
 
 
@@ -62,7 +62,7 @@ def test_tc_gemm_forced_small_batch(M, cuda_dev):
 
 def test_tc_gemm_any_codebook(cuda_dev):
     # The table-lookup dequant needs no affine codebook (the integer-MMA GEMV does).
-    y, ref = _run(384, 2048, 64, 32, 10, False, False, cuda_dev, codebook=[-1.0, -0.3, 0.5, 1.7])
+    y, ref = _run(384, 2048, 64, 32, 10, False, False, cuda_dev, codebook=[-1.0, -0.3, 0.5, 1.7], forced=True)
     assert rel_err(y, ref) < TOL
 
 
@@ -89,3 +89,14 @@ def test_tc_gemm_deterministic(cuda_dev):
     args = (packed.to(cuda_dev), scales.to(cuda_dev), G, None)
     kw = dict(mask=mask.to(cuda_dev), outlier_idx=idx.to(cuda_dev), outlier_vals=ov.to(cuda_dev))
     assert torch.equal(_native.linear_2bit(x, *args, **kw), _native.linear_2bit(x, *args, **kw))
+
+
+def test_tc_auto_route_matches_forced(cuda_dev):
+    # otf2b_linear sends 64 rows to the tcgen05 GEMM by itself: same bits as the forced call.
+    from otf_llm import _native
+    N, K, G, M = 2048, 8192, 64, 64
+    packed, scales, _, idx, ov, _, mask = _random_layer(N, K, G, 40, cuda_dev, seed=6)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(8)).half().to(cuda_dev)
+    args = (packed.to(cuda_dev), scales.to(cuda_dev), G, None)
+    kw = dict(mask=mask.to(cuda_dev), outlier_idx=idx.to(cuda_dev), outlier_vals=ov.to(cuda_dev))
+    assert torch.equal(_native.linear_2bit(x, *args, **kw), _native.linear_2bit(x, *args, gemm_mma=True, **kw))
