@@ -39,16 +39,69 @@ __device__ __forceinline__ float head_finish(float v, float s) {
   return fminf(fmaxf(r, -65504.0f), 65504.0f);
 }
 
+// Pipelined head: every warp streams its own stages of 16 rows x 128 weight bytes with
+// cp.async (4 stages in flight, 144-byte row pitch so the consumers' 16-byte reads are
+// bank-conflict-free), consumed as two block-diagonal MMA sets of four 16-value blocks.
+constexpr int kHeadSlots = 4;
+constexpr int kHeadChunk = 128;                     // weight bytes per row per stage
+constexpr int kHeadPitch = kHeadChunk + 16;
+constexpr int kHeadStage = 16 * kHeadPitch;
+
+__host__ __device__ inline int64_t head_pipe_smem_bytes(int D) {
+  return (int64_t)kHeadWarps * kHeadSlots * kHeadStage + head_smem_bytes(D);
+}
+
 __global__ void __launch_bounds__(kHeadWarps * 32) k_i8_head_imma(const HeadArgs a) {
   pdl_trigger();
-  pdl_wait();
   extern __shared__ __align__(16) uint8_t smem[];
   const int nb = a.D / 16;
-  const int nch = ceil_div(nb, 4);
-  uint8_t* tbl = smem;
-  float* metaF = reinterpret_cast<float*>(smem + align_up((int64_t)nb * kHeadSB, 16));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* const wst = smem + warp * kHeadSlots * kHeadStage;   // this warp's stages
+  uint8_t* tbl = smem + (int64_t)kHeadWarps * kHeadSlots * kHeadStage;
+  float* metaF = reinterpret_cast<float*>(tbl + align_up((int64_t)nb * kHeadSB, 16));
   uint8_t* zblk = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(metaF + nb), 16));
 
+  // Work: warp gw of the grid takes the tiles [gw*T/W, (gw+1)*T/W) (balanced), every chunk of
+  // the row in order.
+  const int ntiles = ceil_div(a.V, 16);
+  const int nch = ceil_div(a.D, kHeadChunk);
+  const int nwarps = gridDim.x * kHeadWarps, gw = blockIdx.x * kHeadWarps + warp;
+  const int t_beg = (int)(((int64_t)gw * ntiles) / nwarps), t_end = (int)(((int64_t)(gw + 1) * ntiles) / nwarps);
+  const int nst = (t_end - t_beg) * nch;
+  const int lr = lane >> 1, lh = lane & 1;
+  const uint32_t cdst0 = smem_u32(wst) + lr * kHeadPitch + 64 * lh;
+  int is_cc = 0, is_tile = t_beg;
+  const int8_t* crow = a.w;
+  bool row_ok = false;
+  auto issue_tile = [&]() {
+    const int r = is_tile * 16 + lr;
+    row_ok = r < a.V;
+    crow = a.w + (int64_t)(row_ok ? r : 0) * a.ldw + 64 * lh;
+  };
+  auto issue = [&](int slot) {
+    const uint32_t so = (uint32_t)(slot * kHeadStage);
+    const int cb = is_cc * kHeadChunk;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rem = row_ok ? a.D - cb - 64 * lh - 16 * i : 0;
+      const uint32_t nbytes = (uint32_t)max(0, min(16, rem));
+      cp_async16(cdst0 + so + 16 * i, nbytes ? reinterpret_cast<const void*>(crow + cb + 16 * i)
+                                             : reinterpret_cast<const void*>(a.w), nbytes);
+    }
+    if (++is_cc == nch) {
+      is_cc = 0;
+      ++is_tile;
+      issue_tile();
+    }
+  };
+  issue_tile();
+#pragma unroll
+  for (int k = 0; k < kHeadSlots; ++k) {
+    if (k < nst) issue(k);
+    cp_async_commit();
+  }
+
+  pdl_wait();
   // Activation table for the whole D (every CTA builds its own; rows amortise it).
   for (int it = threadIdx.x; it < 2 * nb; it += blockDim.x) {
     const int b = it >> 1, limb = it & 1;
@@ -76,55 +129,58 @@ __global__ void __launch_bounds__(kHeadWarps * 32) k_i8_head_imma(const HeadArgs
   if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(zblk)[threadIdx.x] = 0u;
   __syncthreads();
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int ntiles = ceil_div(a.V, 16);
-  for (int tile = blockIdx.x * kHeadWarps + warp; tile < ntiles; tile += gridDim.x * kHeadWarps) {
-    const int rg = tile * 16 + g, rg8 = rg + 8;
-    const bool vg = rg < a.V, vg8 = rg8 < a.V;
-    const int8_t* pg = a.w + (int64_t)(vg ? rg : 0) * a.ldw;
-    const int8_t* pg8 = a.w + (int64_t)(vg8 ? rg8 : 0) * a.ldw;
-    float acc0 = 0.0f, acc1 = 0.0f;
-    uint4 cw = make_uint4(0, 0, 0, 0), cw8 = make_uint4(0, 0, 0, 0);
-    {
-      const bool act = t < nb;
-      ld_stream16_pred(cw, pg + 16 * t, act && vg);
-      ld_stream16_pred(cw8, pg8 + 16 * t, act && vg8);
-    }
-    for (int c = 0; c < nch; ++c) {
-      const int blk = 4 * c + t;
-      const bool act = blk < nb;
-      uint4 nw = make_uint4(0, 0, 0, 0), nw8 = make_uint4(0, 0, 0, 0);
-      {
-        const int blk2 = blk + 4;
-        const bool act2 = blk2 < nb;
-        ld_stream16_pred(nw, pg + 16 * (int64_t)blk2, act2 && vg);
-        ld_stream16_pred(nw8, pg8 + 16 * (int64_t)blk2, act2 && vg8);
-      }
-      const int bblk = 4 * c + (g >> 1);
-      const uint8_t* bp = ((g >> 1) == t && bblk < nb) ? (tbl + bblk * kHeadSB + (g & 1) * kHeadSL) : zblk;
+  const bool breal = (g >> 1) == t;
+  float acc0 = 0.0f, acc1 = 0.0f;
+  int cc = 0, tile = t_beg, s = 0;
+  const uint8_t* st = wst;
+  for (int k = 0; k < nst; ++k) {
+    cp_async_wait<kHeadSlots - 1>();
+    __syncwarp();
+    const uint8_t* pa = st + g * kHeadPitch + 32 * t;
+#pragma unroll
+    for (int set = 0; set < 2; ++set) {
+      const uint4 cw = *reinterpret_cast<const uint4*>(pa + 16 * set);
+      const uint4 cw8 = *reinterpret_cast<const uint4*>(pa + 8 * kHeadPitch + 16 * set);
+      const int blk = cc * 8 + 2 * t + set;        // my block (this quad's)
+      const int bblk = cc * 8 + 2 * (g >> 1) + set;  // the block whose B rows this lane supplies
+      const uint8_t* bp = (breal && bblk < nb) ? (tbl + bblk * kHeadSB + (g & 1) * kHeadSL) : zblk;
       const uint2 b01 = *reinterpret_cast<const uint2*>(bp);
       const uint2 b23 = *reinterpret_cast<const uint2*>(bp + 8);
       int C[4] = {0, 0, 0, 0};
       mma_s8s8(C, cw.x, cw8.x, cw.y, cw8.y, b01.x, b01.y);
       mma_s8s8(C, cw.z, cw8.z, cw.w, cw8.w, b23.x, b23.y);
-      if (act) {
+      if (blk < nb) {
         const float F = metaF[blk];
         acc0 = fmaf((float)(256 * C[0] + C[1]), F, acc0);
         acc1 = fmaf((float)(256 * C[2] + C[3]), F, acc1);
       }
-      cw = nw;
-      cw8 = nw8;
     }
-    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-    if (t == 0) {
-      if (vg) a.out[rg] = head_finish(acc0, h2f(a.scales[rg]));
-      if (vg8) a.out[rg8] = head_finish(acc1, h2f(a.scales[rg8]));
+    __syncwarp();
+    if (k + kHeadSlots < nst) issue(s);
+    cp_async_commit();
+    if (++s == kHeadSlots) {
+      s = 0;
+      st = wst;
+    } else {
+      st += kHeadStage;
+    }
+    if (++cc == nch) {
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+      const int rg = tile * 16 + g, rg8 = rg + 8;
+      if (t == 0) {
+        if (rg < a.V) a.out[rg] = head_finish(acc0, h2f(a.scales[rg]));
+        if (rg8 < a.V) a.out[rg8] = head_finish(acc1, h2f(a.scales[rg8]));
+      }
+      acc0 = acc1 = 0.0f;
+      cc = 0;
+      ++tile;
     }
   }
+  cp_async_wait<0>();
 }
 
 // Portable head for any D / stride: one warp per vocabulary row.
@@ -173,7 +229,7 @@ extern "C" OTF_API int otf_i8_head(const void* x, int64_t ldx, const int8_t* w, 
   if (st != OTF_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool fast = D % 16 == 0 && ldw % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
-                    head_smem_bytes((int)D) <= 200 * 1024;
+                    head_pipe_smem_bytes((int)D) <= 220 * 1024;
   if (fast) {
     static thread_local int configured_dev[64] = {};
     int dev = 0;
@@ -195,9 +251,11 @@ extern "C" OTF_API int otf_i8_head(const void* x, int64_t ldx, const int8_t* w, 
     a.V = (int)V;
     a.D = (int)D;
 
-    cudaError_t e = fast ? launch_pdl(k_i8_head_imma, dim3(std::max(1, std::min(ceil_div(ceil_div((int)V, 16), kHeadWarps),
-                                                                               sms * 2))),
-                                      dim3(kHeadWarps * 32), (size_t)head_smem_bytes((int)D), s, 1u, a)
+    const int ctas_per_sm = head_pipe_smem_bytes((int)D) <= 110 * 1024 ? 2 : 1;
+    cudaError_t e = fast ? launch_pdl(k_i8_head_imma,
+                                      dim3(std::max(1, std::min(ceil_div(ceil_div((int)V, 16), kHeadWarps),
+                                                                sms * ctas_per_sm))),
+                                      dim3(kHeadWarps * 32), (size_t)head_pipe_smem_bytes((int)D), s, 1u, a)
                          : launch_pdl(k_i8_head_generic, dim3(ceil_div((int)V, 8)), dim3(256), 0, s, 1u, a);
     if (e != cudaSuccess) return set_cuda_error(e);
   }
