@@ -189,6 +189,18 @@ OTF_API int otf_i8_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw
                         float* logits, int64_t ldl, int64_t M, int64_t V, int64_t D, void* stream);
 
 /*
+ * Greedy decode step on the INT8 head: argmax[m] = the first index of the largest logit of
+ * row m (torch.argmax semantics over QuantizedLinearHead.forward's output, after its
+ * nan_to_num), int64 [M], 8-byte aligned; it is also the kernel's reduction buffer.
+ * logits may be NULL (then they are not stored).  No reference counterpart as one call:
+ * replaces QuantizedLinearHead.forward (otf_llm/symmetric_2bit_engine.py:75-91) followed by
+ * torch.argmax over its logits (greedy decoding).
+ */
+OTF_API int otf_i8_head_argmax(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scales,
+                               float* logits, int64_t ldl, int64_t* argmax, int64_t M, int64_t V, int64_t D,
+                               void* stream);
+
+/*
  * INT8 embedding gather: out[t,:] = fp16(w[ids[t],:]) * scales[ids[t]] in fp16,
  * bit-identical to QuantizedEmbedding.forward (otf_llm/symmetric_2bit_engine.py:41-47).
  * Ids outside [0, V) produce a zero row and set *bad_ids (device int32, may be NULL) to 1.

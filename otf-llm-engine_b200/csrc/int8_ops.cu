@@ -24,9 +24,18 @@ struct HeadArgs {
   const int8_t* w;
   int64_t ldw;
   const uint16_t* scales;
-  float* out;
+  float* out;                 // logits (may be null when only the argmax is wanted)
+  unsigned long long* amax;   // packed (ordered logit, ~index) maximum, or null
   int V, D;
 };
+
+// Order-preserving 64-bit key of (logit, index): larger logit wins, then the smaller index
+// (the first maximum, like torch.argmax).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (unsigned long long)(~(uint32_t)idx);
+}
 
 __host__ __device__ inline int64_t head_smem_bytes(int D) {
   const int nb = D / 16;
@@ -171,9 +180,19 @@ __global__ void __launch_bounds__(kHeadWarps * 32) k_i8_head_imma(const HeadArgs
       acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
       acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
       const int rg = tile * 16 + g, rg8 = rg + 8;
-      if (t == 0) {
-        if (rg < a.V) a.out[rg] = head_finish(acc0, h2f(a.scales[rg]));
-        if (rg8 < a.V) a.out[rg8] = head_finish(acc1, h2f(a.scales[rg8]));
+      const float l0 = rg < a.V ? head_finish(acc0, h2f(a.scales[rg])) : 0.0f;
+      const float l1 = rg8 < a.V ? head_finish(acc1, h2f(a.scales[rg8])) : 0.0f;
+      if (t == 0 && a.out) {
+        if (rg < a.V) a.out[rg] = l0;
+        if (rg8 < a.V) a.out[rg8] = l1;
+      }
+      if (a.amax) {
+        unsigned long long key = 0ull;
+        if (rg < a.V) key = argmax_key(l0, rg);
+        if (rg8 < a.V) key = max(key, argmax_key(l1, rg8));
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+        if (lane == 0) atomicMax(a.amax, key);
       }
       acc0 = acc1 = 0.0f;
       cc = 0;
@@ -194,7 +213,19 @@ __global__ void __launch_bounds__(256) k_i8_head_generic(const HeadArgs a) {
   for (int d = lane; d < a.D; d += 32) acc = fmaf(h2f(a.x[d]), (float)a.w[(int64_t)row * a.ldw + d], acc);
 #pragma unroll
   for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
-  if (lane == 0) a.out[row] = head_finish(acc, h2f(a.scales[row]));
+  if (lane == 0) {
+    const float l = head_finish(acc, h2f(a.scales[row]));
+    if (a.out) a.out[row] = l;
+    if (a.amax) atomicMax(a.amax, argmax_key(l, row));
+  }
+}
+
+// Packed maximum -> vocabulary index, in place.
+__global__ void k_argmax_finish(unsigned long long* key, int64_t* idx, int M) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_trigger();
+  pdl_wait();
+  if (m < M) idx[m] = (int64_t)(~(uint32_t)(key[m] & 0xffffffffull));
 }
 
 __global__ void k_i8_embed(const int64_t* ids, int n, const int8_t* w, int64_t ldw, const uint16_t* scales,
@@ -220,14 +251,8 @@ __global__ void k_i8_embed(const int64_t* ids, int n, const int8_t* w, int64_t l
 
 using namespace otf;
 
-extern "C" OTF_API int otf_i8_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scales,
-                                   float* logits, int64_t ldl, int64_t M, int64_t V, int64_t D, void* stream) {
-  if (!x || !w || !scales || !logits || M <= 0 || V <= 0 || D <= 0) return OTF_ERR_INVALID;
-  if (ldx < D || ldw < D || ldl < V) return OTF_ERR_INVALID;
-  if (V > INT32_MAX / 2 || D > (1 << 20)) return OTF_ERR_UNSUPPORTED;
-  int st = check_device();
-  if (st != OTF_OK) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+static int head_launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scales, float* logits,
+                       int64_t ldl, unsigned long long* keys, int64_t M, int64_t V, int64_t D, cudaStream_t s) {
   const bool fast = D % 16 == 0 && ldw % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
                     head_pipe_smem_bytes((int)D) <= 220 * 1024;
   if (fast) {
@@ -247,10 +272,10 @@ extern "C" OTF_API int otf_i8_head(const void* x, int64_t ldx, const int8_t* w, 
     a.w = w;
     a.ldw = ldw;
     a.scales = static_cast<const uint16_t*>(scales);
-    a.out = logits + m * ldl;
+    a.out = logits ? logits + m * ldl : nullptr;
+    a.amax = keys ? keys + m : nullptr;
     a.V = (int)V;
     a.D = (int)D;
-
     const int ctas_per_sm = head_pipe_smem_bytes((int)D) <= 110 * 1024 ? 2 : 1;
     cudaError_t e = fast ? launch_pdl(k_i8_head_imma,
                                       dim3(std::max(1, std::min(ceil_div(ceil_div((int)V, 16), kHeadWarps),
@@ -260,6 +285,36 @@ extern "C" OTF_API int otf_i8_head(const void* x, int64_t ldx, const int8_t* w, 
     if (e != cudaSuccess) return set_cuda_error(e);
   }
   return OTF_OK;
+}
+
+extern "C" OTF_API int otf_i8_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scales,
+                                   float* logits, int64_t ldl, int64_t M, int64_t V, int64_t D, void* stream) {
+  if (!x || !w || !scales || !logits || M <= 0 || V <= 0 || D <= 0) return OTF_ERR_INVALID;
+  if (ldx < D || ldw < D || ldl < V) return OTF_ERR_INVALID;
+  if (V > INT32_MAX / 2 || D > (1 << 20)) return OTF_ERR_UNSUPPORTED;
+  int st = check_device();
+  if (st != OTF_OK) return st;
+  return head_launch(x, ldx, w, ldw, scales, logits, ldl, nullptr, M, V, D, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" OTF_API int otf_i8_head_argmax(const void* x, int64_t ldx, const int8_t* w, int64_t ldw,
+                                          const void* scales, float* logits, int64_t ldl, int64_t* argmax,
+                                          int64_t M, int64_t V, int64_t D, void* stream) {
+  if (!x || !w || !scales || !argmax || M <= 0 || V <= 0 || D <= 0) return OTF_ERR_INVALID;
+  if (ldx < D || ldw < D || (logits && ldl < V)) return OTF_ERR_INVALID;
+  if (V > INT32_MAX / 2 || D > (1 << 20) || M > INT32_MAX) return OTF_ERR_UNSUPPORTED;
+  if (reinterpret_cast<uintptr_t>(argmax) % 8) return OTF_ERR_INVALID;
+  int st = check_device();
+  if (st != OTF_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The int64 output doubles as the packed-maximum scratch: cleared, reduced, converted.
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(argmax);
+  cudaError_t e = cudaMemsetAsync(keys, 0, (size_t)M * sizeof(unsigned long long), s);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  st = head_launch(x, ldx, w, ldw, scales, logits, ldl, keys, M, V, D, s);
+  if (st != OTF_OK) return st;
+  return set_cuda_error(launch_pdl(k_argmax_finish, dim3((unsigned)ceil_div((int)M, 128)), dim3(128), 0, s, 1u, keys,
+                                   argmax, (int)M));
 }
 
 extern "C" OTF_API int otf_i8_embed(const int64_t* ids, int64_t n, const int8_t* w, int64_t ldw, const void* scales,

@@ -56,6 +56,7 @@ EXPORTS = (
     "otf2b_linear_group",
     "otf2b_unpack_codes",
     "otf_i8_head",
+    "otf_i8_head_argmax",
     "otf_i8_embed",
     "otf_rmsnorm",
     "otf_silu_mul",
@@ -93,6 +94,8 @@ def lib() -> ctypes.CDLL:
     L.otf2b_unpack_codes.argtypes = [vp, i64, i64, i64, vp, i64, vp]
     L.otf2b_unpack_codes.restype = i32
     L.otf_i8_head.argtypes = [vp, i64, vp, i64, vp, vp, i64, i64, i64, i64, vp]
+    L.otf_i8_head_argmax.argtypes = [vp, i64, vp, i64, vp, vp, i64, vp, i64, i64, i64, vp]
+    L.otf_i8_head_argmax.restype = i32
     L.otf_i8_head.restype = i32
     L.otf_i8_embed.argtypes = [vp, i64, vp, i64, vp, vp, i64, i64, i64, vp, vp]
     L.otf_i8_embed.restype = i32
@@ -260,6 +263,29 @@ def i8_head(x2d: torch.Tensor, w_i8: torch.Tensor, scales: torch.Tensor,
                                _stream(x2d.device))
     _check(st, "otf_i8_head")
     return out
+
+
+def i8_head_argmax(x2d: torch.Tensor, w_i8: torch.Tensor, scales: torch.Tensor,
+                   logits: Optional[torch.Tensor] = None):
+    """Greedy step: int64 [M] first index of the largest logit per row (see otf_i8_head_argmax);
+    also fills `logits` (fp32 [M, V]) when given."""
+    _need_cuda(x2d, "x")
+    M, D = x2d.shape
+    V = w_i8.shape[0]
+    ldx = _rows(x2d, "x", torch.float16, D)
+    ldw = _rows(w_i8, "weight_int8", torch.int8, D)
+    s = scales.reshape(-1)
+    if s.dtype != torch.float16 or s.numel() != V or not s.is_contiguous():
+        raise ValueError("scales must hold V contiguous fp16 values")
+    for name, t in (("weight_int8", w_i8), ("scales", s)):
+        _need_cuda(t, name)
+    ldl = _rows(logits, "logits", torch.float32, V) if logits is not None else 0
+    ids = torch.empty(M, dtype=torch.int64, device=x2d.device)
+    with torch.cuda.device(x2d.device):
+        st = lib().otf_i8_head_argmax(_ptr(x2d), ldx, _ptr(w_i8), ldw, _ptr(s), _ptr(logits), ldl, _ptr(ids), M, V, D,
+                                      _stream(x2d.device))
+    _check(st, "otf_i8_head_argmax")
+    return ids
 
 
 def i8_embed(ids: torch.Tensor, w_i8: torch.Tensor, scales: torch.Tensor,

@@ -64,3 +64,25 @@ def test_head_shapes(V, D, M, cuda_dev):
     lg = _native.i8_head(x.to(cuda_dev), w.to(cuda_dev), s.to(cuda_dev)).cpu().numpy()
     ref = oracle.i8_head(x.numpy(), w.numpy(), s.numpy())
     assert rel_err(lg, ref) < 1e-3
+
+
+@pytest.mark.parametrize("V,D,M", [(128256, 3072, 1), (1000, 256, 3), (50000, 4096, 2), (777, 272, 2)])
+def test_head_argmax(V, D, M, cuda_dev):
+    """Fused greedy step: the index of the largest logit of each row (first maximum)."""
+    from otf_llm import _native
+    g = torch.Generator().manual_seed(V + D)
+    w = torch.randint(-127, 128, (V, D), generator=g, dtype=torch.int32).to(torch.int8)
+    s = (torch.rand(V, 1, generator=g) * 2e-3 + 1e-4).half()
+    x = torch.randn(M, D, generator=g).half()
+    wd, sd, xd = w.to(cuda_dev), s.to(cuda_dev), x.to(cuda_dev)
+    logits = torch.empty(M, V, dtype=torch.float32, device=cuda_dev)
+    ids = _native.i8_head_argmax(xd, wd, sd, logits)
+    ref_logits = _native.i8_head(xd, wd, sd)
+    assert torch.equal(logits, ref_logits)
+    assert torch.equal(ids, torch.argmax(ref_logits, dim=1))
+    ids2 = _native.i8_head_argmax(xd, wd, sd)          # logits not stored
+    assert torch.equal(ids, ids2)
+    # against the oracle: the chosen logit is the maximum up to the head's tolerance
+    ref = oracle.i8_head(x.numpy(), w.numpy(), s.numpy())
+    picked = ref[np.arange(M), ids.cpu().numpy()]
+    assert np.all(picked >= ref.max(axis=1) - 1e-3 * np.abs(ref).max())
