@@ -167,6 +167,21 @@ def codebook_floats(codebook) -> Sequence[float]:
     return vals
 
 
+def tensor_pipe_shape_ok(module) -> bool:
+    """Whether a 2-bit module's batch-1 shapes meet the tensor-pipe GEMV's layout rules (the
+    host-side half of fast_variant in gemv2b.cu): power-of-two group of 32..256, K a
+    multiple of 8, even scale stride, packed row stride a multiple of 16 bytes, and an
+    affine codebook (c3 - c2 == c1 - c0).  Pointer alignment is checked at launch.  Only
+    layers that pass can take the fused RMSNorm / SiLU input transforms."""
+    G, K = int(module.group_size), int(module.d_in)
+    if G < 32 or G > 256 or G & (G - 1) or K % 8:
+        return False
+    if module.scales.stride(0) % 2 or module.packed_uint8.stride(0) % 16:
+        return False
+    c = codebook_floats(module.codebook)
+    return abs((c[3] - c[2]) - (c[1] - c[0])) <= 1e-6 * max(1.0, abs(c[1] - c[0]))
+
+
 def linear_2bit(x2d: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, group_size: int, codebook4,
                 *, zeros: Optional[torch.Tensor] = None, mask: Optional[torch.Tensor] = None,
                 outlier_idx: Optional[torch.Tensor] = None, outlier_vals: Optional[torch.Tensor] = None,

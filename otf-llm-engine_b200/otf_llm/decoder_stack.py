@@ -17,7 +17,7 @@ Tensor-parallel ranks hold column shards of q/k/v/gate/up and row shards of o/do
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Dict, List, Optional
+from typing import Dict, List, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -108,7 +108,12 @@ class Llama2BitLinearStack(nn.Module):
     """Random-init, 2-bit quantized decoder linear stack (batch-1 decode step)."""
 
     def __init__(self, cfg: StackConfig = LLAMA2_7B, device="cuda", seed: int = 0, rank: int = 0, world: int = 1,
-                 process_group=None, fused: bool = True):
+                 process_group=None, fused: bool = True,
+                 layers: Optional[List[Dict[str, SymmetricOTF2BitLinear]]] = None,
+                 norms: Optional[List[Tuple[torch.Tensor, torch.Tensor]]] = None):
+        """Random-init layers from ``cfg`` and ``seed``, or the given (already sharded)
+        ``layers`` keyed by q_proj ... down_proj with per-layer (input, post-attention)
+        RMSNorm weights ``norms`` (default: all ones)."""
         super().__init__()
         self.cfg = cfg
         self.fused = fused
@@ -116,18 +121,35 @@ class Llama2BitLinearStack(nn.Module):
         dev = torch.device(device)
         shapes = cfg.shapes()
         self.layers = nn.ModuleList()
-        for li in range(cfg.layers):
-            mods = {}
-            for pi, name in enumerate(PROJECTIONS):
-                N, K = shapes[name]
-                full = random_quantized_linear(N, K, cfg, seed * 100003 + li * 7 + pi, dev)
-                if world > 1:
-                    full = shard_linear(full, rank, world, "in" if name in ("o_proj", "down_proj") else "out")
-                mods[name] = full
-            self.layers.append(nn.ModuleDict(mods))
-            torch.cuda.synchronize(dev)
+        if layers is not None:
+            for mods in layers:
+                missing = [n for n in PROJECTIONS if n not in mods]
+                if missing:
+                    raise ValueError(f"decoder layer lacks {missing}")
+                self.layers.append(nn.ModuleDict({n: mods[n] for n in PROJECTIONS}))
+        else:
+            for li in range(cfg.layers):
+                mods = {}
+                for pi, name in enumerate(PROJECTIONS):
+                    N, K = shapes[name]
+                    full = random_quantized_linear(N, K, cfg, seed * 100003 + li * 7 + pi, dev)
+                    if world > 1:
+                        full = shard_linear(full, rank, world, "in" if name in ("o_proj", "down_proj") else "out")
+                    mods[name] = full
+                self.layers.append(nn.ModuleDict(mods))
+                torch.cuda.synchronize(dev)
         h = cfg.hidden
         self.norm_w = torch.ones(h, dtype=torch.float16, device=dev)
+        if norms is None:
+            norms = [(self.norm_w, self.norm_w)] * len(self.layers)
+        if len(norms) != len(self.layers):
+            raise ValueError(f"{len(norms)} norm pairs for {len(self.layers)} layers")
+        self.in_norms = [a.to(device=dev, dtype=torch.float16).contiguous() for a, _ in norms]
+        self.post_norms = [b.to(device=dev, dtype=torch.float16).contiguous() for _, b in norms]
+        # The fused input transforms run only in the tensor-pipe GEMV; a layer outside its
+        # layout rules (e.g. an odd number of groups per row) runs the unfused sequence.
+        if self.fused and not all(_native.tensor_pipe_shape_ok(m) for layer in self.layers for m in layer.values()):
+            self.fused = False
         sh = {n: (m.out_features, m.d_in) for n, m in self.layers[0].items()}
         self._buf = {
             "xn": torch.empty(1, h, dtype=torch.float16, device=dev),
@@ -141,6 +163,24 @@ class Llama2BitLinearStack(nn.Module):
             "h1": torch.empty(1, h, dtype=torch.float16, device=dev),
             "h2": torch.empty(1, h, dtype=torch.float16, device=dev),
         }
+
+    @classmethod
+    def from_checkpoint(cls, ck, head_dim: int, rms_eps: float = 1e-5, process_group=None, fused: bool = True):
+        """The stack of a loaded checkpoint (otf_llm.checkpoint.load_checkpoint), this rank's shard
+        when the checkpoint was loaded tensor-parallel.  head_dim comes from the model config."""
+        layers = [{p.split(".")[-1]: m for p, m in mods.items()} for mods in ck.layers]
+        if not layers:
+            raise ValueError("checkpoint has no decoder layers")
+        l0, w = layers[0], ck.world
+        hidden = l0["q_proj"].d_in
+        cfg = StackConfig(layers=len(layers), hidden=hidden, intermediate=l0["gate_proj"].out_features * w,
+                          heads=l0["q_proj"].out_features * w // head_dim,
+                          kv_heads=l0["k_proj"].out_features * w // head_dim, head_dim=head_dim,
+                          group_size=ck.group_size, rms_eps=rms_eps)
+        ones = torch.ones(hidden, dtype=torch.float16)
+        norms = [(n.get("input_layernorm", ones), n.get("post_attention_layernorm", ones)) for n in ck.layer_norms]
+        return cls(cfg, device=l0["q_proj"].packed_uint8.device, rank=ck.rank, world=w, process_group=process_group,
+                   fused=fused, layers=layers, norms=norms or None)
 
     # -- accounting -----------------------------------------------------------------
     def bytes_per_token(self) -> int:
@@ -168,7 +208,7 @@ class Llama2BitLinearStack(nn.Module):
             mask=m.outlier_mask_vector if m.has_outliers else None,
             outlier_idx=m.outlier_indices if m.has_outliers else None,
             outlier_vals=m.outliers_fp16 if m.has_outliers else None,
-            residual=residual, clamp=True, out=out)
+            bias=m.bias if m.has_bias else None, residual=residual, clamp=True, out=out)
 
     def _attn_passthrough(self, v: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         cfg = self.cfg
@@ -187,14 +227,14 @@ class Llama2BitLinearStack(nn.Module):
         tp = self.world > 1
         G = _native.GroupItem
         cur = h
-        for layer in self.layers:
-            _native.linear_group([G(layer[n], cur, b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.norm_w,
+        for li, layer in enumerate(self.layers):
+            _native.linear_group([G(layer[n], cur, b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.in_norms[li],
                                     eps=cfg.rms_eps) for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"))])
             attn = self._attn_passthrough(b["v"], b["attn"])
             _native.linear_group([G(layer["o_proj"], attn, b["h1"], residual=None if (tp and self.rank) else cur)])
             if tp:
                 torch.distributed.all_reduce(b["h1"], group=self.pg)
-            _native.linear_group([G(layer[n], b["h1"], b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.norm_w,
+            _native.linear_group([G(layer[n], b["h1"], b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.post_norms[li],
                                     eps=cfg.rms_eps) for n, o in (("gate_proj", "g"), ("up_proj", "u"))])
             _native.linear_group([G(layer["down_proj"], b["g"], b["h2"], residual=None if (tp and self.rank) else b["h1"],
                                     x_op=_native.OTF_XOP_SILU_MUL, x_aux=b["u"])])
@@ -213,7 +253,7 @@ class Llama2BitLinearStack(nn.Module):
         b = self._buf
         cur = h
         for li, layer in enumerate(self.layers):
-            xn = cur if linears_only else _native.rmsnorm(cur, self.norm_w, self.cfg.rms_eps, out=b["xn"])
+            xn = cur if linears_only else _native.rmsnorm(cur, self.in_norms[li], self.cfg.rms_eps, out=b["xn"])
             self._lin(layer["q_proj"], xn, b["q"])
             self._lin(layer["k_proj"], xn, b["k"])
             v = self._lin(layer["v_proj"], xn, b["v"])
@@ -222,7 +262,7 @@ class Llama2BitLinearStack(nn.Module):
             h1 = self._lin(layer["o_proj"], attn, b["h1"], residual=None if (tp and self.rank) else cur)
             if tp and collectives:
                 torch.distributed.all_reduce(h1, group=self.pg)
-            xn = h1 if linears_only else _native.rmsnorm(h1, self.norm_w, self.cfg.rms_eps, out=b["xn"])
+            xn = h1 if linears_only else _native.rmsnorm(h1, self.post_norms[li], self.cfg.rms_eps, out=b["xn"])
             g = self._lin(layer["gate_proj"], xn, b["g"])
             u = self._lin(layer["up_proj"], xn, b["u"])
             a = g if linears_only else _native.silu_mul(g, u, out=b["a"])
@@ -261,3 +301,44 @@ class DecodeGraph:
         self.x.copy_(x_host, non_blocking=True)
         self.graph.replay()
         y_host.copy_(self.y, non_blocking=True)
+
+
+class CheckpointDecoder:
+    """Greedy decode steps through a loaded checkpoint at batch 1: INT8 embedding row ->
+    2-bit decoder stack (single-position attention) -> final RMSNorm -> INT8 head argmax.
+
+    Under tensor parallelism the embedding is replicated, the stack all-reduces after o
+    and down, and the head is vocabulary-parallel with one (max, index) exchange per step.
+    """
+
+    def __init__(self, ck, head_dim: int, rms_eps: float = 1e-5, process_group=None, fused: bool = True):
+        if ck.embed is None or ck.head is None:
+            raise ValueError("checkpoint was loaded without its embedding / head")
+        self.ck = ck
+        self.stack = Llama2BitLinearStack.from_checkpoint(ck, head_dim, rms_eps, process_group, fused)
+        dev = self.stack.norm_w.device
+        fn = ck.final_norm if ck.final_norm is not None else self.stack.norm_w
+        self.final_norm = fn.to(device=dev, dtype=torch.float16).contiguous()
+        self.eps = rms_eps
+        self.xn = torch.empty(1, self.stack.cfg.hidden, dtype=torch.float16, device=dev)
+
+    def step(self, ids: torch.Tensor, logits: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """ids int64 [1] on the device -> next ids int64 [1]; fills ``logits`` (fp32 [1, V]
+        on one device, this rank's [1, V/world] shard under tensor parallelism) when given."""
+        h = self.ck.embed(ids.view(1)).view(1, -1)
+        h = self.stack(h)
+        xn = _native.rmsnorm(h, self.final_norm, self.eps, out=self.xn)
+        head = self.ck.head
+        if hasattr(head, "shard"):
+            return head.argmax(xn, logits=logits)
+        return _native.i8_head_argmax(xn, head.weight_int8, head.scales, logits=logits)
+
+    def generate(self, prompt_last: int, steps: int) -> List[int]:
+        """``steps`` greedy tokens after ``prompt_last`` (ids stay on the device until the end)."""
+        dev = self.final_norm.device
+        cur = torch.tensor([prompt_last], dtype=torch.int64, device=dev)
+        out = []
+        for _ in range(steps):
+            cur = self.step(cur)
+            out.append(cur)
+        return [int(t) for t in torch.cat(out).cpu()] if out else []

@@ -95,3 +95,60 @@ def test_row_shard_rebases_anchors():
             assert int(s.outlier_indices.min()) >= 0 and int(s.outlier_indices.max()) < 1024
             seen.extend((s.outlier_indices + r * 1024).tolist())
     assert sorted(seen) == sorted(gd["outlier_idx"].tolist())
+
+
+def _ckpt_worker(rank, world, port, q):
+    """Sharded checkpoint load + vocabulary-parallel greedy pick on gloo ranks."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from conftest import GOLDEN
+        from otf_llm.checkpoint import load_checkpoint
+        from otf_llm.vocab_parallel import combine_argmax
+        d = os.path.join(GOLDEN, "ckpt_tied")
+        ck = load_checkpoint(d, device="cpu", rank=rank, world=world)
+        x = np.random.default_rng(5).standard_normal((3, 128)).astype(np.float16)
+        # row-parallel down_proj: this rank's input slice, partial sums all-reduced
+        m = ck.layers[1]["mlp.down_proj"]
+        part = torch.from_numpy(_oracle_layer(m, x[:, rank * m.d_in:(rank + 1) * m.d_in]).astype(np.float32))
+        dist.all_reduce(part)
+        # greedy pick over vocabulary shards: equal maxima straddle the shard boundary
+        V, M = 64, 6
+        logits = torch.from_numpy(np.random.default_rng(9).standard_normal((M, V)).astype(np.float32))
+        logits[1, 10] = logits[1, 40] = 9.0        # tie across ranks: the lower index wins
+        logits[2, 33] = logits[2, 35] = 9.0        # tie inside rank 1
+        logits[3, :] = -1.0                        # all equal: index 0
+        logits[4, 63] = 50.0                       # maximum in the last row of the last shard
+        logits[5, 31] = logits[5, 32] = 7.0        # tie on the shard boundary
+        v0 = ck.head.row0
+        loc = logits[:, v0:v0 + V // world]
+        lm, li = loc.max(dim=1)
+        ids = combine_argmax(lm, li, v0)
+        if rank == 0:
+            q.put((part.numpy(), ids.numpy(), torch.argmax(logits, dim=1).numpy()))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put(e)
+        raise
+
+
+def test_sharded_checkpoint_and_vocab_argmax():
+    from conftest import GOLDEN
+    from otf_llm.checkpoint import load_checkpoint
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ckpt_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=180)
+    for p in procs:
+        p.join(timeout=60)
+    assert not isinstance(res, Exception), res
+    part, ids, ref_ids = res
+    full = load_checkpoint(os.path.join(GOLDEN, "ckpt_tied"), device="cpu").layers[1]["mlp.down_proj"]
+    x = np.random.default_rng(5).standard_normal((3, 128)).astype(np.float16)
+    assert rel_err(part, _oracle_layer(full, x)) < 1e-5
+    assert np.array_equal(ids, ref_ids)
