@@ -201,7 +201,12 @@ def run_b200(args, cfg):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = dist.group.WORLD
 
-    stack = Llama2BitLinearStack(cfg, device=dev, seed=1, rank=rank, world=world, process_group=pg)
+    peer_ar = None
+    if world > 1 and args.tp_exchange == "peer":
+        from otf_llm.tp_allreduce import PeerAllReduce
+        peer_ar = PeerAllReduce(cfg.hidden, group=pg, device=dev)
+    stack = Llama2BitLinearStack(cfg, device=dev, seed=1, rank=rank, world=world, process_group=pg,
+                                 peer_ar=peer_ar, persistent=args.decode == "persistent")
     graph = DecodeGraph(stack)
     # The 2-bit projections alone (no norm/SiLU, no all-reduce): per-rank kernel time for the roofline.
     lin_graph = DecodeGraph(stack, linears_only=True, collectives=False)
@@ -292,6 +297,8 @@ def run_b200(args, cfg):
                            "intermediate": cfg.intermediate, "group_size": cfg.group_size,
                            "outlier_ratio": cfg.outlier_ratio, "batch": 1,
                            "parallelism": f"tp{world}" if world > 1 else "single",
+                           "tp_exchange": (args.tp_exchange if world > 1 else None),
+                           "decode": "persistent" if stack.mk is not None else "grouped launches",
                            "l2": "weights 1.89 GB >> 126 MB L2 (no flush needed)"},
                 "tokens_per_s": round(tok_s, 1), "frac_of_peak": round(value / world / peak, 4),
                 "peak_gbs": peak, "peak_kind": kind,
@@ -301,6 +308,10 @@ def run_b200(args, cfg):
     del graph, lin_graph
     if world > 1:
         dist.barrier(device_ids=[local])
+        if peer_ar is not None:
+            torch.cuda.synchronize()
+            peer_ar.close()
+            dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if line is not None:
         print(json.dumps(line), flush=True)
@@ -427,6 +438,10 @@ def main():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode", choices=("grouped", "persistent"), default="grouped",
+                    help="decode step as 4 grouped launches per layer, or one persistent launch per token")
+    ap.add_argument("--tp-exchange", choices=("peer", "nccl"), default="peer",
+                    help="tensor-parallel exchange after o/down: fused NVLink peer stores, or NCCL all_reduce")
     ap.add_argument("--sweep", action="store_true", help="batch sweep at Llama-3-70B MLP shapes (JSON lines)")
     args = ap.parse_args()
     from otf_llm.decoder_stack import StackConfig

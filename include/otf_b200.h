@@ -3,7 +3,8 @@
  *
  * Every entry point takes plain device pointers, element strides, sizes and a
  * cudaStream_t passed as void*, launches asynchronously on that stream and
- * returns an int status (OTF_OK == 0).  Nothing allocates device memory;
+ * returns an int status (OTF_OK == 0).  Nothing allocates device memory except
+ * otf_ar_create (the tensor-parallel receive buffers, once per process group);
  * outputs are caller-owned.  Half-precision tensors are IEEE binary16 bit
  * patterns (uint16_t).  No exceptions cross this boundary.
  *
@@ -45,6 +46,12 @@ extern "C" {
 #define OTF_XOP_SILU_MUL 2  /* x <- fp16(fp16(silu(x)) * aux) */
 
 /* Flags for otf2b_linear. */
+#define OTF_AR_NONE 0
+#define OTF_AR_PRODUCE 1
+#define OTF_AR_CONSUME 2
+#define OTF_AR_MAX_WORLD 8
+#define OTF_AR_HANDLE_BYTES 64  /* one cudaIpcMemHandle_t */
+
 #define OTF_FLAG_CLAMP 1u          /* clamp output to [-65504, 65504] (SymmetricOTF2BitLinear) */
 #define OTF_FLAG_FORCE_GENERIC 2u  /* use the portable CUDA-core kernel (testing) */
 
@@ -160,6 +167,17 @@ typedef struct otf2b_layer {
   int32_t x_op;
   const void* x_aux;
   float eps;
+  /* Tensor-parallel peer all-reduce (see otf_ar_create; ar == NULL: none).
+   *   ar_mode OTF_AR_PRODUCE: the finished rows (fp32, after bias, anchors and residual,
+   *     before the clamp) go to receive buffer ar_buf of every rank instead of y; the
+   *     layer must be launched alone (n_layers == 1).
+   *   ar_mode OTF_AR_CONSUME: x is the sum over ranks of receive buffer ar_buf (rounded to
+   *     fp16, clamped), read after every rank has produced all K rows into it; x itself is
+   *     not read.  ar_out (fp16 [K], may be NULL) receives that sum once per launch. */
+  void* ar;
+  int32_t ar_mode;
+  int32_t ar_buf;
+  void* ar_out;
 } otf2b_layer;
 
 /*
@@ -223,6 +241,80 @@ OTF_API int otf_rmsnorm(const void* x, int64_t ldx, const void* w, float eps, vo
  * fp16 values (act_fn(gate_proj(x)) * up_proj(x) in transformers LlamaMLP).
  */
 OTF_API int otf_silu_mul(const void* g, const void* u, void* out, int64_t n, void* stream);
+
+/*
+ * Tensor-parallel peer all-reduce over NVLink (one process per GPU).  No reference
+ * counterpart as a library: it replaces the NCCL all_reduce after each row-parallel
+ * o_proj / down_proj that tensor parallelism adds around the reference's
+ * SymmetricOTF2BitLinear (otf_llm/symmetric_2bit_engine.py:214-235).
+ *
+ * otf_ar_create allocates this rank's receive region (two buffers of world x max_elems
+ * fp32 slots plus arrival counters) on the current device and writes its CUDA IPC handle
+ * (OTF_AR_HANDLE_BYTES) to ipc_handle; the caller exchanges the handles (e.g. an
+ * all-gather over the process group) and passes all of them, in rank order, to
+ * otf_ar_open, which maps every peer's region.  Producers write rows straight into every
+ * peer's region and then add the row count to the peer's arrival counter (release, system
+ * scope); a consumer waits until the counter reaches world x rows (bounded: on time-out it
+ * raises the otf_device_error flag and carries on), sums the world slots in rank order
+ * (identical on every rank) and, as the last consumer CTA of its launch, resets the
+ * counter.  Consecutive exchanges must alternate buffers 0 and 1.
+ */
+typedef struct otf_ar otf_ar;
+OTF_API int otf_ar_create(int rank, int world, int64_t max_elems, void* ipc_handle, otf_ar** out);
+OTF_API int otf_ar_open(otf_ar* ar, const void* all_handles);
+OTF_API int otf_ar_destroy(otf_ar* ar);
+/* Push an fp16 vector x[n] (this rank's partial sum) into buffer buf of every rank. */
+OTF_API int otf_ar_push(otf_ar* ar, int buf, const void* x, int64_t n, void* stream);
+/* Wait for all ranks' n rows in buffer buf and write their fp16 sum to out[n]. */
+OTF_API int otf_ar_finish(otf_ar* ar, int buf, void* out, int64_t n, void* stream);
+
+/*
+ * A whole batch-1 decode step of a Llama-shaped 2-bit decoder stack in ONE persistent
+ * launch (one CTA per SM): per layer RMSNorm -> q/k/v -> (single-position attention:
+ * the output of each query head is its KV head's v) -> o + residual -> RMSNorm ->
+ * gate/up -> fp16(silu(g)) * u -> down + residual, every projection the fused
+ * 2-bit linear of otf2b_linear (mask, anchors, bias, clamp).  Stages are separated by a
+ * device-wide barrier; each warp streams its share of every stage's weight tiles through
+ * its own copy ring, so the next stage's weights arrive while the barrier and the
+ * activation staging run.  No reference counterpart as one call: it replaces the
+ * per-module SymmetricOTF2BitLinear.forward calls (otf_llm/symmetric_2bit_engine.py:
+ * 214-235) that HF's LlamaDecoderLayer makes for one generated token
+ * (otf_llm/run_symmetric_2bit.py:150-187 injects them).
+ */
+typedef struct otf2b_proj {
+  const uint8_t* packed;     /* uint8 [N, ld_packed], ld_packed % 16 == 0 */
+  int64_t ld_packed;
+  const void* scales;        /* fp16 [N, ld_scales], ld_scales even */
+  int64_t ld_scales;
+  const void* mask;          /* fp16 [K] or NULL */
+  const int64_t* outlier_idx;
+  int64_t n_outliers;
+  const void* outlier_vals;  /* fp16 [N, ld_outlier_vals] */
+  int64_t ld_outlier_vals;
+  const void* bias;          /* fp16 [N] or NULL */
+  int64_t N, K;
+} otf2b_proj;
+
+typedef struct otf2b_decoder_layer {
+  otf2b_proj q, k, v, o, gate, up, down;
+  const void* input_norm;    /* fp16 [hidden] or NULL (ones) */
+  const void* post_norm;     /* fp16 [hidden] or NULL (ones) */
+} otf2b_decoder_layer;
+
+typedef struct otf2b_decode_dims {
+  int64_t n_layers, hidden, intermediate, heads, kv_heads, head_dim, group_size;
+  float eps;
+  float codebook[4];         /* affine: c3 - c2 == c1 - c0 */
+} otf2b_decode_dims;
+
+/* Bytes of the caller-owned device workspace for these dimensions (16-byte aligned). */
+OTF_API int64_t otf2b_decode_workspace_bytes(const otf2b_decode_dims* dims);
+/* Validate the layers (host array) and copy their descriptors into the workspace
+ * (synchronous; once per stack).  OTF_ERR_UNSUPPORTED for shapes the kernel does not take. */
+OTF_API int otf2b_decode_prepare(const otf2b_decoder_layer* layers, const otf2b_decode_dims* dims, void* workspace,
+                                 int64_t workspace_bytes);
+/* One decode step: h (fp16 [hidden], 16-byte aligned) is the residual stream in and out. */
+OTF_API int otf2b_decode_step(const otf2b_decode_dims* dims, void* h, void* workspace, void* stream);
 
 #ifdef __cplusplus
 }

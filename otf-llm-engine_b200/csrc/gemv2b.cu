@@ -41,17 +41,14 @@
 #include <tuple>
 
 #include "otf_common.cuh"
+#include "tp_ar.cuh"
 
 namespace otf {
 
 constexpr int kCWarps = 8;                  // warps per CTA (each pipelines its own stages)
 constexpr int kThreads = kCWarps * 32;
 constexpr int kCThreads = kCWarps * 32;
-constexpr int kRows = 16;                   // rows per tile (the m16 of the MMA)
 constexpr int kSlots = 3;                   // stages in flight per warp
-constexpr int kChunk = 128;                 // code bytes per row per stage (512 codes)
-constexpr int kChunkCodes = 4 * kChunk;
-constexpr int kPitch = kChunk + 16;         // shared-memory row pitch of a stage
 constexpr int kMaxCluster = 8;              // K slices per cluster
 #ifndef OTF_GEMV_MIN_CTAS
 #define OTF_GEMV_MIN_CTAS 2
@@ -87,6 +84,10 @@ struct LinearArgs {
   int xop;              // OTF_XOP_*: transform applied to x while staging it
   const uint16_t* xaux; // RMSNorm weight or the SiLU gate's second operand
   float eps;            // RMSNorm epsilon
+  const ArPeers* ar;    // tensor-parallel peer table (device), or null
+  int ar_mode;          // OTF_AR_*: produce rows into the peers' buffers / consume their sum as x
+  int ar_buf;           // receive buffer 0 or 1
+  uint16_t* ar_out;     // consumer: fp16 copy of the reduced x (written by cluster 0), or null
 };
 
 // A group of layers launched together (decode-step fusion: q/k/v or gate/up share an
@@ -98,12 +99,6 @@ struct GroupParams {
   int prefix[kMaxGroup + 1];
 };
 
-// Table geometry for W words per block: limb row SL = 32W+16 bytes (hi row, then lo row),
-// block stride SB a multiple of 128 so that every block's two real reads fall on the same
-// two 16-byte bank groups, and the all-zero block read by the other lanes sits 64 bytes off
-// them (no bank conflict between the real and the zero reads of one instruction).
-__host__ __device__ constexpr int tbl_sl(int W) { return 32 * W + 16; }
-__host__ __device__ constexpr int tbl_sb(int W) { return (2 * tbl_sl(W) + 127) / 128 * 128; }
 
 // Rows a CTA of the cluster finishes: tiles are dealt out in contiguous blocks of tpf.
 __host__ __device__ inline int tiles_per_finisher(int tiles_per_group, int S) { return ceil_div(tiles_per_group, S); }
@@ -117,9 +112,6 @@ struct GemvSmem {
   int stage_bytes, stage_scales, stage_zeros, ov_bytes;
 };
 
-// Bytes of scales per row of a stage: the stage's 512/G groups plus 4 bytes of padding
-// (rows of a stage then start on distinct banks).
-__host__ __device__ inline int scale_pitch(int G) { return 2 * (kChunkCodes / G) + 4; }
 
 __host__ __device__ inline GemvSmem gemv_smem_layout(int W, bool zeros, int K, int G, int S, int n_out, int64_t ldo,
                                                       int tiles_per_group) {
@@ -150,17 +142,6 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int W, bool zeros, int K, i
   return L;
 }
 
-// 2^e as a float for -126 <= e <= 127 (exact).
-__device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
-
-// Round-to-nearest-even of |v| < 2^22 via the 1.5*2^23 magic constant.
-__device__ __forceinline__ int rint_small(float v) { return __float_as_int(v + 12582912.0f) - 0x4B400000; }
-
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-  const uint32_t p01 = __byte_perm((uint32_t)a, (uint32_t)b, 0x0040);
-  const uint32_t p23 = __byte_perm((uint32_t)c, (uint32_t)d, 0x0040);
-  return __byte_perm(p01, p23, 0x5410);
-}
 
 __device__ __forceinline__ uint16_t ldg_u16(const uint16_t* p) { return __ldg(p); }
 
@@ -181,8 +162,6 @@ __device__ __forceinline__ __half xform_v(__half x, int xop, uint16_t aux_v, boo
   return x;
 }
 
-// Words per 16W-code block for group size G (the block never straddles a group).
-__host__ __device__ constexpr int words_for(int G) { return G >= 64 ? 4 : 2; }
 
 template <int G, bool ZEROS>
 __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) {
@@ -341,10 +320,20 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
     // Weights, scales and bias are in flight; from here on we read the predecessor's output.
     pdl_wait();
     if (fin_ok && a.res) ep += h2f(ldg_u16(a.res + frow));
+    // Tensor-parallel consumer: x is the sum of every rank's rows in the receive buffer,
+    // each word polled until it carries this exchange's tag (bounded per thread).
+    const bool ar_cons = a.ar_mode == OTF_AR_CONSUME;
+    const unsigned ar_tg = ar_cons ? ar_tag(a.ar, a.ar_buf) : 0u;
+    uint32_t ar_budget = kArSpinLimit;
+    int ar_err = 0;
     // x at this thread's anchor column (and the transform's second operand there), issued
     // together with the staging loads below.
     uint32_t x_k = 0u, xaux_k = 0u;
-    ld_u16_pred(x_k, a.x + kcol, tid < a.n_out);
+    if (ar_cons) {
+      if (tid < a.n_out) x_k = ar_sum1(a.ar, a.ar_buf, kcol, ar_tg, ar_budget, ar_err);
+    } else {
+      ld_u16_pred(x_k, a.x + kcol, tid < a.n_out);
+    }
     ld_u16_pred(xaux_k, a.xaux + kcol, tid < a.n_out && a.xaux != nullptr && a.xop != OTF_XOP_NONE);
     // Stage my slice of x (fp16); padded tail = 0.  The SiLU gate and the mask apply on the
     // way in; RMSNorm first needs the sum of squares of all K, combined across the cluster
@@ -357,7 +346,12 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
       for (int v = tid; v < nbs_pad * BLK / 8; v += kCThreads) {
         uint4 xv = make_uint4(0, 0, 0, 0);
         if (v < nbs * BLK / 8) {
-          xv = __ldg(xsrc + v);
+          if (ar_cons) {
+            xv = ar_sum8(a.ar, a.ar_buf, (int64_t)kbeg + 8 * v, ar_tg, ar_budget, ar_err);
+            if (a.ar_out && group == 0) reinterpret_cast<uint4*>(a.ar_out + kbeg)[v] = xv;
+          } else {
+            xv = __ldg(xsrc + v);
+          }
           __half2* xh = reinterpret_cast<__half2*>(&xv);
           if (norm) {
 #pragma unroll
@@ -431,6 +425,10 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
     }
     for (int i = tid; i < 32; i += kCThreads) reinterpret_cast<uint32_t*>(zblk)[i] = 0u;
     named_barrier_sync(1, kCThreads);  // the staged slice of x is complete
+    if (ar_cons) {
+      if (ar_err) report_wait_failure();
+      if (tid == 0) ar_consumed(a.ar, a.ar_buf);  // every read of the buffer is done
+    }
     // Quantise the table slice: 4W lanes per block, lane (w, j) owns codes 16w+4i+j.
     {
       constexpr int LPB = 4 * W;
@@ -618,12 +616,19 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
     cp_async_wait<0>();
     // One cluster barrier below: every partial has landed in its finisher's shared memory.
     cluster_sync_all();
+    const bool ar_prod = a.ar_mode == OTF_AR_PRODUCE;
     if (fin_ok) {
       float yv = ep + (a.n_out > 0 ? afin_sum[tid] : 0.0f);
       for (int q = 0; q < S; ++q) yv += fin[q * fin_rows + tid];
-      if (a.clamp) yv = fminf(fmaxf(yv, -65504.0f), 65504.0f);
-      a.y[frow] = f2h(yv);
+      if (ar_prod) {
+        // Tensor-parallel producer: the fp32 row goes to every rank (clamped after the sum).
+        ar_put(a.ar, a.ar_buf, frow, yv, ar_tag(a.ar, a.ar_buf));
+      } else {
+        if (a.clamp) yv = fminf(fmaxf(yv, -65504.0f), 65504.0f);
+        a.y[frow] = f2h(yv);
+      }
     }
+
   }
 }
 
@@ -1439,6 +1444,10 @@ __global__ void k_unpack_codes(const uint8_t* packed, int64_t ldp, int N, int K,
 
 int set_cuda_error(cudaError_t e);  // capi.cu
 int check_device();                 // capi.cu
+const void* ar_device_table(const otf_ar* ar);  // tp_ar.cu
+int64_t ar_max_elems(const otf_ar* ar);         // tp_ar.cu
+int ar_device_error(int clear);                 // tp_ar.cu
+int mk_device_error(int clear);                 // decode_step.cu
 
 static int num_sms() {
   static thread_local int cached[64] = {};
@@ -1885,6 +1894,28 @@ extern "C" OTF_API int otf2b_linear_group(const otf2b_layer* layers, int n_layer
     L[m].xop = d.x_op;
     L[m].xaux = static_cast<const uint16_t*>(d.x_aux);
     L[m].eps = d.eps;
+    // Tensor-parallel exchange: one producing layer per launch; consuming layers share
+    // their x, so all of them consume the same buffer.
+    if (d.ar && d.ar_mode != OTF_AR_NONE) {
+      const otf_ar* ar = static_cast<const otf_ar*>(d.ar);
+      const void* tbl = ar_device_table(ar);
+      if (!tbl || (d.ar_buf != 0 && d.ar_buf != 1)) return OTF_ERR_INVALID;
+      if (d.ar_mode == OTF_AR_PRODUCE) {
+        if (n_layers != 1 || d.N > ar_max_elems(ar)) return OTF_ERR_INVALID;
+      } else if (d.ar_mode == OTF_AR_CONSUME) {
+        if (d.K > ar_max_elems(ar) || d.x_op == OTF_XOP_SILU_MUL) return OTF_ERR_INVALID;
+        if (d.n_outliers > kCThreads) return OTF_ERR_UNSUPPORTED;
+        if (m == 0 && d.ar_out && reinterpret_cast<uintptr_t>(d.ar_out) % 16) return OTF_ERR_INVALID;
+      } else {
+        return OTF_ERR_INVALID;
+      }
+      L[m].ar = static_cast<const ArPeers*>(tbl);
+      L[m].ar_mode = d.ar_mode;
+      L[m].ar_buf = d.ar_buf;
+      L[m].ar_out = m == 0 ? static_cast<uint16_t*>(d.ar_out) : nullptr;
+    }
+    if (m > 0 && (L[m].ar_mode != L[0].ar_mode || L[m].ar != L[0].ar || L[m].ar_buf != L[0].ar_buf))
+      return OTF_ERR_INVALID;
   }
   int st = check_device();
   if (st != OTF_OK) return st;
@@ -1895,6 +1926,9 @@ extern "C" OTF_API int otf2b_linear_group(const otf2b_layer* layers, int n_layer
   for (int m = 1; m < n_layers; ++m)
     same = same && L[m].K == L[0].K && L[m].G == L[0].G && (L[m].zeros != nullptr) == (L[0].zeros != nullptr) &&
            fast_variant(L[m], layers[m].flags) == v0;
+  // The exchange needs the whole group in the one tensor-pipe grid (its consumer CTAs
+  // count themselves to re-arm the buffer).
+  if (L[0].ar_mode != OTF_AR_NONE && !(same && v0 != 0)) return OTF_ERR_UNSUPPORTED;
   if (same && v0 != 0) {
     const bool z = L[0].zeros != nullptr;
     switch (v0) {
@@ -1935,5 +1969,8 @@ extern "C" OTF_API int otf_device_error(int clear) {
     const int z = 0;
     cudaMemcpyToSymbol(otf::g_otf_device_error, &z, sizeof(int));
   }
-  return v;
+  const int w = ar_device_error(clear);
+  const int x = mk_device_error(clear);
+  if (w < 0 || x < 0) return -1;
+  return v | w | x;
 }

@@ -228,6 +228,41 @@ __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 
+// Geometry shared by the 2-bit GEMV kernels (gemv2b.cu) and the decode-step kernel
+// (decode_step.cu): a stage is 16 rows x 128 code bytes (512 codes) staged at a 144-byte
+// row pitch (the consumers' 16-byte reads are bank-conflict-free), followed by the rows'
+// scales.
+constexpr int kRows = 16;                   // rows per tile (the m16 of the MMA)
+constexpr int kChunk = 128;                 // code bytes per row per stage (512 codes)
+constexpr int kChunkCodes = 4 * kChunk;
+constexpr int kPitch = kChunk + 16;         // shared-memory row pitch of a stage
+
+// Table geometry for W words per block: limb row SL = 32W+16 bytes (hi row, then lo row),
+// block stride SB a multiple of 128 so that every block's two real reads fall on the same
+// two 16-byte bank groups, and the all-zero block read by the other lanes sits 64 bytes off
+// them (no bank conflict between the real and the zero reads of one instruction).
+__host__ __device__ constexpr int tbl_sl(int W) { return 32 * W + 16; }
+__host__ __device__ constexpr int tbl_sb(int W) { return (2 * tbl_sl(W) + 127) / 128 * 128; }
+
+// Bytes of scales per row of a stage: the stage's 512/G groups plus 4 bytes of padding
+// (rows of a stage then start on distinct banks).
+__host__ __device__ inline int scale_pitch(int G) { return 2 * (kChunkCodes / G) + 4; }
+
+// Words per 16W-code block for group size G (the block never straddles a group).
+__host__ __device__ constexpr int words_for(int G) { return G >= 64 ? 4 : 2; }
+
+// 2^e as a float for -126 <= e <= 127 (exact).
+__device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
+
+// Round-to-nearest-even of |v| < 2^22 via the 1.5*2^23 magic constant.
+__device__ __forceinline__ int rint_small(float v) { return __float_as_int(v + 12582912.0f) - 0x4B400000; }
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  const uint32_t p01 = __byte_perm((uint32_t)a, (uint32_t)b, 0x0040);
+  const uint32_t p23 = __byte_perm((uint32_t)c, (uint32_t)d, 0x0040);
+  return __byte_perm(p01, p23, 0x5410);
+}
+
 // Choose the power-of-two exponent E for 16-bit fixed point so that
 // maxabs * 2^E lies in [8192, 16384): |X| <= 16384 keeps both s8 limbs of X
 // (X = 256*hi + lo, lo in [-128,127]) inside the s8 range.

@@ -22,6 +22,10 @@ OTF_FLAG_FORCE_GENERIC = 2
 OTF_XOP_NONE = 0
 OTF_XOP_RMSNORM = 1
 OTF_XOP_SILU_MUL = 2
+OTF_AR_NONE = 0
+OTF_AR_PRODUCE = 1
+OTF_AR_CONSUME = 2
+OTF_AR_HANDLE_BYTES = 64
 
 
 class Layer(ctypes.Structure):
@@ -43,7 +47,35 @@ class Layer(ctypes.Structure):
         ("x_op", ctypes.c_int32),
         ("x_aux", ctypes.c_void_p),
         ("eps", ctypes.c_float),
+        ("ar", ctypes.c_void_p), ("ar_mode", ctypes.c_int32), ("ar_buf", ctypes.c_int32),
+        ("ar_out", ctypes.c_void_p),
     ]
+
+class Proj(ctypes.Structure):
+    """Mirror of `otf2b_proj` (include/otf_b200.h)."""
+    _fields_ = [
+        ("packed", ctypes.c_void_p), ("ld_packed", ctypes.c_int64),
+        ("scales", ctypes.c_void_p), ("ld_scales", ctypes.c_int64),
+        ("mask", ctypes.c_void_p),
+        ("outlier_idx", ctypes.c_void_p), ("n_outliers", ctypes.c_int64),
+        ("outlier_vals", ctypes.c_void_p), ("ld_outlier_vals", ctypes.c_int64),
+        ("bias", ctypes.c_void_p),
+        ("N", ctypes.c_int64), ("K", ctypes.c_int64),
+    ]
+
+
+class DecoderLayer(ctypes.Structure):
+    """Mirror of `otf2b_decoder_layer`."""
+    _fields_ = [(n, Proj) for n in ("q", "k", "v", "o", "gate", "up", "down")] + [
+        ("input_norm", ctypes.c_void_p), ("post_norm", ctypes.c_void_p)]
+
+
+class DecodeDims(ctypes.Structure):
+    """Mirror of `otf2b_decode_dims`."""
+    _fields_ = [("n_layers", ctypes.c_int64), ("hidden", ctypes.c_int64), ("intermediate", ctypes.c_int64),
+                ("heads", ctypes.c_int64), ("kv_heads", ctypes.c_int64), ("head_dim", ctypes.c_int64),
+                ("group_size", ctypes.c_int64), ("eps", ctypes.c_float), ("codebook", ctypes.c_float * 4)]
+
 
 # Names exported by the library; kept in step with include/otf_b200.h.
 EXPORTS = (
@@ -60,6 +92,14 @@ EXPORTS = (
     "otf_i8_embed",
     "otf_rmsnorm",
     "otf_silu_mul",
+    "otf_ar_create",
+    "otf_ar_open",
+    "otf_ar_destroy",
+    "otf_ar_push",
+    "otf_ar_finish",
+    "otf2b_decode_workspace_bytes",
+    "otf2b_decode_prepare",
+    "otf2b_decode_step",
 )
 
 
@@ -103,6 +143,22 @@ def lib() -> ctypes.CDLL:
     L.otf_rmsnorm.restype = i32
     L.otf_silu_mul.argtypes = [vp, vp, vp, i64, vp]
     L.otf_silu_mul.restype = i32
+    L.otf_ar_create.argtypes = [i32, i32, i64, vp, ctypes.POINTER(vp)]
+    L.otf_ar_create.restype = i32
+    L.otf_ar_open.argtypes = [vp, vp]
+    L.otf_ar_open.restype = i32
+    L.otf_ar_destroy.argtypes = [vp]
+    L.otf_ar_destroy.restype = i32
+    L.otf_ar_push.argtypes = [vp, i32, vp, i64, vp]
+    L.otf_ar_push.restype = i32
+    L.otf_ar_finish.argtypes = [vp, i32, vp, i64, vp]
+    L.otf_ar_finish.restype = i32
+    L.otf2b_decode_workspace_bytes.argtypes = [ctypes.POINTER(DecodeDims)]
+    L.otf2b_decode_workspace_bytes.restype = i64
+    L.otf2b_decode_prepare.argtypes = [ctypes.POINTER(DecoderLayer), ctypes.POINTER(DecodeDims), vp, i64]
+    L.otf2b_decode_prepare.restype = i32
+    L.otf2b_decode_step.argtypes = [ctypes.POINTER(DecodeDims), vp, vp, vp]
+    L.otf2b_decode_step.restype = i32
     _lib = L
     return L
 
@@ -367,9 +423,13 @@ class GroupItem:
 
     def __init__(self, module, x: torch.Tensor, out: torch.Tensor, residual: Optional[torch.Tensor] = None,
                  x_op: int = OTF_XOP_NONE, x_aux: Optional[torch.Tensor] = None, eps: float = 0.0,
-                 clamp: bool = True):
+                 clamp: bool = True, ar=None, ar_mode: int = OTF_AR_NONE, ar_buf: int = 0,
+                 ar_out: Optional[torch.Tensor] = None):
         self.m, self.x, self.out, self.residual = module, x, out, residual
         self.x_op, self.x_aux, self.eps, self.clamp = x_op, x_aux, eps, clamp
+        # tensor-parallel exchange (otf_llm.tp_allreduce.PeerAllReduce): produce this layer's
+        # rows into every rank's buffer ar_buf, or consume their sum as x (ar_out: its fp16 copy)
+        self.ar, self.ar_mode, self.ar_buf, self.ar_out = ar, ar_mode, ar_buf, ar_out
 
 
 def _layer_struct(it: GroupItem, keep: list) -> Layer:
@@ -409,6 +469,13 @@ def _layer_struct(it: GroupItem, keep: list) -> Layer:
             raise ValueError("x_aux must be a contiguous fp16 vector of length K")
         L.x_aux = it.x_aux.data_ptr()
     L.eps = float(it.eps)
+    if it.ar is not None and it.ar_mode != OTF_AR_NONE:
+        L.ar, L.ar_mode, L.ar_buf = it.ar.handle, int(it.ar_mode), int(it.ar_buf)
+        if it.ar_out is not None:
+            _need_cuda(it.ar_out, "ar_out")
+            if it.ar_out.dtype != torch.float16 or it.ar_out.numel() != K or not it.ar_out.is_contiguous():
+                raise ValueError("ar_out must be a contiguous fp16 vector of length K")
+            L.ar_out = it.ar_out.data_ptr()
     return L
 
 
@@ -422,3 +489,65 @@ def linear_group(items: Sequence[GroupItem]) -> None:
     with torch.cuda.device(dev):
         st = lib().otf2b_linear_group(arr, len(items), _stream(dev))
     _check(st, "otf2b_linear_group")
+
+
+def proj_struct(m) -> Proj:
+    """otf2b_proj view of a SymmetricOTF2BitLinear's buffers (pointers only; keep m alive)."""
+    K, N, G = m.d_in, m.out_features, m.group_size
+    p = Proj()
+    p.packed, p.ld_packed = m.packed_uint8.data_ptr(), _rows(m.packed_uint8, "packed", torch.uint8, K // 4)
+    p.scales, p.ld_scales = m.scales.data_ptr(), _rows(m.scales, "scales", torch.float16, K // G)
+    if m.has_outliers:
+        p.mask = m.outlier_mask_vector.data_ptr()
+        p.outlier_idx, p.n_outliers = m.outlier_indices.data_ptr(), m.outlier_indices.numel()
+        p.outlier_vals = m.outliers_fp16.data_ptr()
+        p.ld_outlier_vals = _rows(m.outliers_fp16, "outlier_vals", torch.float16, p.n_outliers)
+    if m.has_bias:
+        p.bias = m.bias.data_ptr()
+    p.N, p.K = N, K
+    return p
+
+
+class DecodeStep:
+    """One persistent launch per decode step of a Llama-shaped 2-bit stack (otf2b_decode_step).
+
+    layers: per decoder layer a mapping q_proj ... down_proj -> SymmetricOTF2BitLinear;
+    norms: per layer (input, post-attention) RMSNorm weights (fp16 [hidden]).
+    """
+
+    def __init__(self, layers, norms, hidden: int, intermediate: int, heads: int, kv_heads: int, head_dim: int,
+                 group_size: int, eps: float, codebook, device):
+        self.device = torch.device(device)
+        d = DecodeDims()
+        d.n_layers, d.hidden, d.intermediate = len(layers), hidden, intermediate
+        d.heads, d.kv_heads, d.head_dim, d.group_size, d.eps = heads, kv_heads, head_dim, group_size, float(eps)
+        for i, c in enumerate(codebook_floats(codebook)):
+            d.codebook[i] = c
+        self.dims = d
+        n = lib().otf2b_decode_workspace_bytes(ctypes.byref(d))
+        if n < 0:
+            raise ValueError("dimensions not supported by otf2b_decode_step")
+        self.ws = torch.zeros(int(n), dtype=torch.uint8, device=self.device)
+        arr = (DecoderLayer * len(layers))()
+        keep = []
+        for i, (mods, (wi, wp)) in enumerate(zip(layers, norms)):
+            for name, field in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"), ("o_proj", "o"),
+                                ("gate_proj", "gate"), ("up_proj", "up"), ("down_proj", "down")):
+                setattr(arr[i], field, proj_struct(mods[name]))
+            wi = wi.to(device=self.device, dtype=torch.float16).contiguous()
+            wp = wp.to(device=self.device, dtype=torch.float16).contiguous()
+            keep += [wi, wp]
+            arr[i].input_norm, arr[i].post_norm = wi.data_ptr(), wp.data_ptr()
+        self._keep = (keep, layers)
+        with torch.cuda.device(self.device):
+            _check(lib().otf2b_decode_prepare(arr, ctypes.byref(d), self.ws.data_ptr(), self.ws.numel()),
+                   "otf2b_decode_prepare")
+        self.h = torch.zeros(hidden, dtype=torch.float16, device=self.device)
+
+    def __call__(self, h: torch.Tensor) -> torch.Tensor:
+        """h fp16 [1, hidden] -> the residual stream after every layer ([1, hidden], an internal buffer)."""
+        self.h.copy_(h.reshape(-1))
+        with torch.cuda.device(self.device):
+            _check(lib().otf2b_decode_step(ctypes.byref(self.dims), self.h.data_ptr(), self.ws.data_ptr(),
+                                           _stream(self.device)), "otf2b_decode_step")
+        return self.h.view(1, -1)

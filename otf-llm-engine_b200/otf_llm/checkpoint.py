@@ -24,8 +24,9 @@ head to the embedding's int8 buffer and scales by reference, not by copy (:128-1
 
 Tensor-parallel loads read only this rank's part of each tensor (safetensors slices):
 q/k/v/gate/up are split by output rows, o/down by input columns at group boundaries
-with the anchor columns inside the slice re-based to slice-local indices and the bias
-kept on rank 0 only (it must be added once before the all-reduce of the partial sums).
+(balanced when the group count does not divide evenly; gate/up rows are cut at the same
+points) with the anchor columns inside the slice re-based to slice-local indices and the
+bias kept on rank 0 only (it must be added once before the all-reduce of the partial sums).
 The INT8 head is split by vocabulary rows; a tied head's shard is a row view of the
 replicated embedding.
 """
@@ -63,6 +64,7 @@ DEFAULT_PROJECTIONS = [
 # Projections whose input dimension is split under tensor parallelism (their outputs are
 # partial sums that an all-reduce completes); every other projection is split by rows.
 ROW_PARALLEL = ("self_attn.o_proj", "mlp.down_proj")
+FEEDS_ROW_PARALLEL_BY_GROUP = ("mlp.gate_proj", "mlp.up_proj")
 LAYER_NORMS = ("input_layernorm", "post_attention_layernorm")
 DEFAULT_GROUP_SIZE = 32
 
@@ -77,11 +79,10 @@ def read_config(model_dir: str) -> dict:
 
 
 def shard_bounds(n: int, rank: int, world: int, align: int = 1) -> Tuple[int, int]:
-    """[lo, hi) of an even split of n items over world ranks, in units of align."""
-    if n % (world * align):
-        raise ValueError(f"{n} does not split into {world} shards of whole {align}-blocks")
-    step = n // world
-    return rank * step, (rank + 1) * step
+    """[lo, hi) of rank's part of n items cut at multiples of align, as evenly as the
+    alignment allows (the split the decoder stack uses, decoder_stack.split_bounds)."""
+    from .decoder_stack import split_bounds
+    return split_bounds(n, rank, world, align)
 
 
 def _get(f, key: str, rows: Optional[Tuple[int, int]] = None, cols: Optional[Tuple[int, int]] = None):
@@ -101,6 +102,7 @@ class LinearShard:
     dim: Optional[str] = None
     rank: int = 0
     world: int = 1
+    align: int = 1          # column shards: cut rows at multiples of this
 
 
 def load_linear(f, keys: set, prefix: str, group_size: int, device, shard: LinearShard = LinearShard()
@@ -122,7 +124,7 @@ def load_linear(f, keys: set, prefix: str, group_size: int, device, shard: Linea
     rows = cols = None
     k0, k1 = 0, K
     if shard.world > 1 and shard.dim == "out":
-        rows = shard_bounds(N, shard.rank, shard.world)
+        rows = shard_bounds(N, shard.rank, shard.world, shard.align)
     elif shard.world > 1 and shard.dim == "in":
         k0, k1 = shard_bounds(K, shard.rank, shard.world, G)
         cols = (k0, k1)
@@ -145,7 +147,8 @@ def load_linear(f, keys: set, prefix: str, group_size: int, device, shard: Linea
         bias = _get(f, f"{prefix}.bias", rows)
     dev = torch.device(device)
     to = lambda t: None if t is None else t.contiguous().to(dev)  # noqa: E731
-    return SymmetricOTF2BitLinear(to(packed), to(scales), k1 - k0, G, to(ov), to(oi), to(bias))
+    from .decoder_stack import even_scale_rows
+    return even_scale_rows(SymmetricOTF2BitLinear(to(packed), to(scales), k1 - k0, G, to(ov), to(oi), to(bias)))
 
 
 @dataclass
@@ -204,7 +207,11 @@ def load_checkpoint(model_dir: str, device="cuda", rank: int = 0, world: int = 1
         for i in range(L):
             mods: Dict[str, SymmetricOTF2BitLinear] = {}
             for proj in projections:
-                shard = LinearShard("in" if proj in ROW_PARALLEL else "out", rank, world) if world > 1 else LinearShard()
+                # gate/up rows are cut at down_proj's group boundaries, so each rank's slice
+                # of the intermediate activation is exactly its down_proj input slice
+                align = G if proj in FEEDS_ROW_PARALLEL_BY_GROUP else 1
+                shard = (LinearShard("in" if proj in ROW_PARALLEL else "out", rank, world, align) if world > 1
+                         else LinearShard())
                 m = load_linear(f, keys, f"model.layers.{i}.{proj}", G, dev, shard)
                 if m is not None:
                     mods[proj] = m

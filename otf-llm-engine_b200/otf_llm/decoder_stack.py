@@ -72,27 +72,52 @@ def random_quantized_linear(N: int, K: int, cfg: StackConfig, seed: int, device)
     act = activation_profile(K, gen, device)
     q = Symmetric2BitQuantizer(group_size=cfg.group_size, outlier_ratio=cfg.outlier_ratio)
     packed, scales, ov, oi = q.quantize_tensor(W, act)
-    return SymmetricOTF2BitLinear(packed, scales, K, cfg.group_size, ov, oi)
+    return even_scale_rows(SymmetricOTF2BitLinear(packed, scales, K, cfg.group_size, ov, oi))
 
 
-def shard_linear(lay: SymmetricOTF2BitLinear, rank: int, world: int, dim: str) -> SymmetricOTF2BitLinear:
+def split_bounds(n: int, rank: int, world: int, align: int = 1):
+    """[lo, hi) of rank's part of n items cut at multiples of align, as evenly as the
+    alignment allows (parts differ by at most one align-block)."""
+    if n % align:
+        raise ValueError(f"{n} is not a multiple of {align}")
+    units = n // align
+    if units < world:
+        raise ValueError(f"{n} items in blocks of {align} cannot be split over {world} ranks")
+    return rank * units // world * align, (rank + 1) * units // world * align
+
+
+def even_scale_rows(m: SymmetricOTF2BitLinear) -> SymmetricOTF2BitLinear:
+    """Give the scale rows a 16-byte row stride (a multiple of 8 groups; padding columns are
+    zero), so the GEMV kernels can copy scales in 4-byte pieces and the decode-step kernel
+    in 16-byte TMA boxes.  The buffer keeps its [N, K/G] shape; only its storage grows."""
+    N, ng = m.scales.shape
+    if m.scales.stride(0) % 8:
+        padded = torch.zeros(N, (ng + 7) // 8 * 8, dtype=m.scales.dtype, device=m.scales.device)
+        padded[:, :ng] = m.scales
+        m.scales = padded[:, :ng]
+    return m
+
+
+def shard_linear(lay: SymmetricOTF2BitLinear, rank: int, world: int, dim: str, align: int = 1) -> SymmetricOTF2BitLinear:
     """Column (dim='out') or row (dim='in') shard of a 2-bit layer for tensor parallelism.
 
-    Row shards cut K at group boundaries; the anchor columns falling inside a shard keep
-    their values and are re-based to shard-local indices (a shard may have none).
+    Row shards cut K at group boundaries (balanced over ranks when the group count does
+    not divide evenly); the anchor columns falling inside a shard keep their values and are
+    re-based to shard-local indices (a shard may have none); a bias stays on rank 0 (it is
+    added once, before the partial sums are reduced).  Column shards cut N at multiples of
+    ``align`` -- the consuming row-parallel layer's group size for gate/up, so that each
+    rank's slice of the intermediate activation is exactly its down_proj's K slice; the
+    head size for q/k/v.
     """
     N, K, G = lay.out_features, lay.d_in, lay.group_size
     if dim == "out":
-        if N % world:
-            raise ValueError(f"out_features {N} not divisible by {world}")
-        n0, n1 = rank * N // world, (rank + 1) * N // world
+        n0, n1 = split_bounds(N, rank, world, align)
         ov = lay.outliers_fp16[n0:n1] if lay.has_outliers else None
         oi = lay.outlier_indices if lay.has_outliers else None
+        bias = lay.bias[n0:n1].contiguous() if lay.has_bias else None
         return SymmetricOTF2BitLinear(lay.packed_uint8[n0:n1].contiguous(), lay.scales[n0:n1].contiguous(), K, G,
-                                      None if ov is None else ov.contiguous(), oi)
-    if K % (world * G):
-        raise ValueError(f"in_features {K} not divisible into {world} shards of whole groups of {G}")
-    k0, k1 = rank * K // world, (rank + 1) * K // world
+                                      None if ov is None else ov.contiguous(), oi, bias)
+    k0, k1 = split_bounds(K, rank, world, G)
     packed = lay.packed_uint8[:, k0 // 4:k1 // 4].contiguous()
     scales = lay.scales[:, k0 // G:k1 // G].contiguous()
     ov = oi = None
@@ -101,7 +126,8 @@ def shard_linear(lay: SymmetricOTF2BitLinear, rank: int, world: int, dim: str) -
         if bool(sel.any()):
             oi = (lay.outlier_indices[sel] - k0).contiguous()
             ov = lay.outliers_fp16[:, sel].contiguous()
-    return SymmetricOTF2BitLinear(packed, scales, k1 - k0, G, ov, oi)
+    bias = lay.bias if (lay.has_bias and rank == 0) else None
+    return even_scale_rows(SymmetricOTF2BitLinear(packed, scales, k1 - k0, G, ov, oi, bias))
 
 
 class Llama2BitLinearStack(nn.Module):
@@ -110,14 +136,20 @@ class Llama2BitLinearStack(nn.Module):
     def __init__(self, cfg: StackConfig = LLAMA2_7B, device="cuda", seed: int = 0, rank: int = 0, world: int = 1,
                  process_group=None, fused: bool = True,
                  layers: Optional[List[Dict[str, SymmetricOTF2BitLinear]]] = None,
-                 norms: Optional[List[Tuple[torch.Tensor, torch.Tensor]]] = None):
+                 norms: Optional[List[Tuple[torch.Tensor, torch.Tensor]]] = None, peer_ar=None,
+                 persistent: bool = False):
         """Random-init layers from ``cfg`` and ``seed``, or the given (already sharded)
         ``layers`` keyed by q_proj ... down_proj with per-layer (input, post-attention)
-        RMSNorm weights ``norms`` (default: all ones)."""
+        RMSNorm weights ``norms`` (default: all ones).  Under tensor parallelism ``peer_ar``
+        (otf_llm.tp_allreduce.PeerAllReduce) replaces the NCCL all-reduces of the fused step
+        by the exchange fused into the o/down and following grouped launches.  ``persistent``
+        runs a whole single-GPU step as one launch (``_native.DecodeStep``) when the shapes
+        allow it (else the grouped launches)."""
         super().__init__()
         self.cfg = cfg
         self.fused = fused
         self.rank, self.world, self.pg = rank, world, process_group
+        self.peer_ar = peer_ar
         dev = torch.device(device)
         shapes = cfg.shapes()
         self.layers = nn.ModuleList()
@@ -134,7 +166,11 @@ class Llama2BitLinearStack(nn.Module):
                     N, K = shapes[name]
                     full = random_quantized_linear(N, K, cfg, seed * 100003 + li * 7 + pi, dev)
                     if world > 1:
-                        full = shard_linear(full, rank, world, "in" if name in ("o_proj", "down_proj") else "out")
+                        if name in ("o_proj", "down_proj"):
+                            full = shard_linear(full, rank, world, "in")
+                        else:
+                            full = shard_linear(full, rank, world, "out",
+                                                cfg.group_size if name in ("gate_proj", "up_proj") else cfg.head_dim)
                     mods[name] = full
                 self.layers.append(nn.ModuleDict(mods))
                 torch.cuda.synchronize(dev)
@@ -147,9 +183,25 @@ class Llama2BitLinearStack(nn.Module):
         self.in_norms = [a.to(device=dev, dtype=torch.float16).contiguous() for a, _ in norms]
         self.post_norms = [b.to(device=dev, dtype=torch.float16).contiguous() for _, b in norms]
         # The fused input transforms run only in the tensor-pipe GEMV; a layer outside its
-        # layout rules (e.g. an odd number of groups per row) runs the unfused sequence.
+        # layout rules runs the unfused sequence.  Every rank must take the same path (the
+        # collectives differ), so the ranks agree on it.
         if self.fused and not all(_native.tensor_pipe_shape_ok(m) for layer in self.layers for m in layer.values()):
             self.fused = False
+        self.mk = None
+        if world == 1 and persistent and self.fused and dev.type == "cuda":
+            try:
+                cb = self.layers[0]["q_proj"].codebook
+                self.mk = _native.DecodeStep(
+                    [dict(layer) for layer in self.layers], list(zip(self.in_norms, self.post_norms)), cfg.hidden,
+                    self.layers[0]["gate_proj"].out_features, cfg.heads, cfg.kv_heads, cfg.head_dim,
+                    self.layers[0]["q_proj"].group_size, cfg.rms_eps, cb, dev)
+            except (ValueError, RuntimeError):
+                self.mk = None
+        if world > 1 and process_group is not None and torch.distributed.is_initialized():
+            flag = torch.tensor([1 if self.fused else 0], dtype=torch.int32,
+                                device=dev if torch.distributed.get_backend(process_group) == "nccl" else "cpu")
+            torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN, group=process_group)
+            self.fused = bool(int(flag.item()))
         sh = {n: (m.out_features, m.d_in) for n, m in self.layers[0].items()}
         self._buf = {
             "xn": torch.empty(1, h, dtype=torch.float16, device=dev),
@@ -165,7 +217,8 @@ class Llama2BitLinearStack(nn.Module):
         }
 
     @classmethod
-    def from_checkpoint(cls, ck, head_dim: int, rms_eps: float = 1e-5, process_group=None, fused: bool = True):
+    def from_checkpoint(cls, ck, head_dim: int, rms_eps: float = 1e-5, process_group=None, fused: bool = True,
+                        persistent: bool = False, peer_ar=None):
         """The stack of a loaded checkpoint (otf_llm.checkpoint.load_checkpoint), this rank's shard
         when the checkpoint was loaded tensor-parallel.  head_dim comes from the model config."""
         layers = [{p.split(".")[-1]: m for p, m in mods.items()} for mods in ck.layers]
@@ -180,7 +233,7 @@ class Llama2BitLinearStack(nn.Module):
         ones = torch.ones(hidden, dtype=torch.float16)
         norms = [(n.get("input_layernorm", ones), n.get("post_attention_layernorm", ones)) for n in ck.layer_norms]
         return cls(cfg, device=l0["q_proj"].packed_uint8.device, rank=ck.rank, world=w, process_group=process_group,
-                   fused=fused, layers=layers, norms=norms or None)
+                   fused=fused, layers=layers, norms=norms or None, persistent=persistent, peer_ar=peer_ar)
 
     # -- accounting -----------------------------------------------------------------
     def bytes_per_token(self) -> int:
@@ -198,7 +251,10 @@ class Llama2BitLinearStack(nn.Module):
                 for layer in self.layers for m in layer.values()]
 
     def launches_per_token(self) -> int:
-        return (4 if self.fused else 10) * len(self.layers)
+        if self.mk is not None:
+            return 1
+        n = (4 if self.fused else 10) * len(self.layers)
+        return n + (1 if (self.fused and self.world > 1 and self.peer_ar is not None) else 0)
 
     # -- forward ----------------------------------------------------------------------
     def _lin(self, m: SymmetricOTF2BitLinear, x: torch.Tensor, out: torch.Tensor,
@@ -219,9 +275,52 @@ class Llama2BitLinearStack(nn.Module):
         out.view(-1, rep, hd).copy_(v.view(-1, 1, hd).expand(-1, rep, hd))
         return out
 
+    def _forward_fused_ar(self, h: torch.Tensor) -> torch.Tensor:
+        """The fused step under tensor parallelism with the exchange inside the launches:
+        o and down produce their rows into every rank's receive buffer (rank 0 adds the
+        residual), and the next grouped launch consumes the sum while staging its input,
+        writing the reduced hidden state once for the residual path.  One standalone
+        finish ends the step."""
+        b = self._buf
+        cfg = self.cfg
+        ar = self.peer_ar
+        G = _native.GroupItem
+        PROD, CONS = _native.OTF_AR_PRODUCE, _native.OTF_AR_CONSUME
+        lead = self.rank == 0
+        cur = h
+        pending = None                       # buffer holding the previous down's rows
+        for li, layer in enumerate(self.layers):
+            if pending is None:
+                items = [G(layer[n], cur, b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.in_norms[li], eps=cfg.rms_eps)
+                         for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"))]
+            else:
+                items = [G(layer[n], b["h2"], b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.in_norms[li],
+                           eps=cfg.rms_eps, ar=ar, ar_mode=CONS, ar_buf=pending,
+                           ar_out=b["h2"].view(-1) if n == "q_proj" else None)
+                         for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"))]
+                cur = b["h2"]
+            _native.linear_group(items)
+            attn = self._attn_passthrough(b["v"], b["attn"])
+            ob = ar.next_buffer()
+            _native.linear_group([G(layer["o_proj"], attn, b["h1"], residual=cur if lead else None,
+                                    ar=ar, ar_mode=PROD, ar_buf=ob)])
+            _native.linear_group([G(layer[n], b["h1"], b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.post_norms[li],
+                                    eps=cfg.rms_eps, ar=ar, ar_mode=CONS, ar_buf=ob,
+                                    ar_out=b["h1"].view(-1) if n == "gate_proj" else None)
+                                  for n, o in (("gate_proj", "g"), ("up_proj", "u"))])
+            pending = ar.next_buffer()
+            _native.linear_group([G(layer["down_proj"], b["g"], b["h2"], residual=b["h1"] if lead else None,
+                                    x_op=_native.OTF_XOP_SILU_MUL, x_aux=b["u"], ar=ar, ar_mode=PROD, ar_buf=pending)])
+        if pending is not None:
+            ar.finish(b["h2"].view(-1), pending)
+            return b["h2"]
+        return cur
+
     def _forward_fused(self, h: torch.Tensor) -> torch.Tensor:
         """Four launches per layer: [rmsnorm + q/k/v], [o + residual], [rmsnorm + gate/up],
         [silu gate + down + residual] (the norms and the gate run inside the GEMV prologue)."""
+        if self.world > 1 and self.peer_ar is not None:
+            return self._forward_fused_ar(h)
         b = self._buf
         cfg = self.cfg
         tp = self.world > 1
@@ -248,6 +347,8 @@ class Llama2BitLinearStack(nn.Module):
 
         linears_only drops RMSNorm and SiLU (the 2-bit projections alone, for the roofline);
         collectives=False also drops the tensor-parallel all-reduces (per-rank kernel time)."""
+        if self.mk is not None and not linears_only:
+            return self.mk(h)
         if self.fused and not linears_only:
             return self._forward_fused(h)
         b = self._buf
@@ -311,11 +412,13 @@ class CheckpointDecoder:
     and down, and the head is vocabulary-parallel with one (max, index) exchange per step.
     """
 
-    def __init__(self, ck, head_dim: int, rms_eps: float = 1e-5, process_group=None, fused: bool = True):
+    def __init__(self, ck, head_dim: int, rms_eps: float = 1e-5, process_group=None, fused: bool = True,
+                 persistent: bool = False, peer_ar=None):
         if ck.embed is None or ck.head is None:
             raise ValueError("checkpoint was loaded without its embedding / head")
         self.ck = ck
-        self.stack = Llama2BitLinearStack.from_checkpoint(ck, head_dim, rms_eps, process_group, fused)
+        self.stack = Llama2BitLinearStack.from_checkpoint(ck, head_dim, rms_eps, process_group, fused, persistent,
+                                                          peer_ar)
         dev = self.stack.norm_w.device
         fn = ck.final_norm if ck.final_norm is not None else self.stack.norm_w
         self.final_norm = fn.to(device=dev, dtype=torch.float16).contiguous()

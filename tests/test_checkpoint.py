@@ -163,10 +163,25 @@ def test_tensor_parallel_shards_reassemble(world):
         assert w.data_ptr() == s.embed.weight_int8.data_ptr() + r * (V // world) * w.shape[1]
 
 
-def test_uneven_row_shard_is_an_error():
+def test_uneven_group_count_splits_balanced():
+    """down_proj has 3 groups of 64 per row: ranks take 1 and 2 groups, and gate/up rows are
+    cut at the same points, so each rank's intermediate slice is its down_proj input."""
+    from otf_llm.checkpoint import load_checkpoint
+    full = load_checkpoint(_dir("ckpt_untied"), device="cpu")
+    parts = [load_checkpoint(_dir("ckpt_untied"), device="cpu", rank=r, world=2) for r in range(2)]
+    for r, p in enumerate(parts):
+        down, gate, up = (p.layers[0][k] for k in ("mlp.down_proj", "mlp.gate_proj", "mlp.up_proj"))
+        assert down.d_in == gate.out_features == up.out_features == 64 * (r + 1)
+    for key in ("mlp.down_proj",):
+        assert torch.equal(torch.cat([p.layers[0][key].packed_uint8 for p in parts], 1), full.layers[0][key].packed_uint8)
+    for key in ("mlp.gate_proj", "mlp.up_proj"):
+        assert torch.equal(torch.cat([p.layers[0][key].packed_uint8 for p in parts], 0), full.layers[0][key].packed_uint8)
+
+
+def test_too_many_ranks_is_an_error():
     from otf_llm.checkpoint import load_checkpoint
     with pytest.raises(ValueError, match="split"):
-        load_checkpoint(_dir("ckpt_untied"), device="cpu", rank=0, world=2)   # down_proj has 3 groups of 64
+        load_checkpoint(_dir("ckpt_tied"), device="cpu", rank=0, world=4)   # o_proj input: 2 groups of 32
 
 
 def test_build_hf_model_injects_modules():
@@ -200,6 +215,12 @@ def test_stack_from_checkpoint_shapes():
     st = Llama2BitLinearStack.from_checkpoint(ck, head_dim=16)
     assert (st.cfg.hidden, st.cfg.intermediate, st.cfg.heads, st.cfg.kv_heads) == (64, 128, 4, 2)
     assert st.fused and all(torch.equal(a, ck.layer_norms[i]["input_layernorm"]) for i, a in enumerate(st.in_norms))
-    # three groups of 64 per down_proj row: outside the tensor-pipe layout, so the unfused sequence
-    st = Llama2BitLinearStack.from_checkpoint(load_checkpoint(_dir("ckpt_untied"), device="cpu"), head_dim=32)
-    assert not st.fused
+    # three groups of 64 per down_proj row: the loader pads the scale rows to a 16-byte stride
+    # (shape unchanged), which keeps the layer inside the tensor-pipe layout
+    ck = load_checkpoint(_dir("ckpt_untied"), device="cpu")
+    down = ck.layers[0]["mlp.down_proj"]
+    assert down.scales.shape == (128, 3) and down.scales.stride(0) == 8
+    assert torch.equal(down.scales, _tensors(os.path.join(_dir("ckpt_untied"), "otf_2bit_model.safetensors"))
+                       ["model.layers.0.mlp.down_proj.scales"])
+    st = Llama2BitLinearStack.from_checkpoint(ck, head_dim=32)
+    assert st.fused

@@ -128,14 +128,16 @@ def _cpu_decode_step(ck, tok, head_dim, eps=1e-5):
     return oracle.i8_head(xn.numpy(), _np(ck.head.weight_int8), _np(ck.head.scales))
 
 
+@pytest.mark.parametrize("persistent", [False, True])
 @pytest.mark.parametrize("name", list(MODELS))
-def test_checkpoint_decoder_matches_cpu_step(name, cuda_dev):
+def test_checkpoint_decoder_matches_cpu_step(name, persistent, cuda_dev):
     from otf_llm.checkpoint import load_checkpoint
     from otf_llm.decoder_stack import CheckpointDecoder
     d = os.path.join(GOLDEN, name)
     hd = MODELS[name][1]
     ck = load_checkpoint(d, device=cuda_dev)
-    dec = CheckpointDecoder(ck, head_dim=hd)
+    dec = CheckpointDecoder(ck, head_dim=hd, persistent=persistent)
+    assert (dec.stack.mk is not None) == persistent
     V = ck.head.out_features
     tok = 5
     for _ in range(3):

@@ -152,3 +152,18 @@ def test_sharded_checkpoint_and_vocab_argmax():
     x = np.random.default_rng(5).standard_normal((3, 128)).astype(np.float16)
     assert rel_err(part, _oracle_layer(full, x)) < 1e-5
     assert np.array_equal(ids, ref_ids)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_llama7b_shards_cover_every_group(world):
+    """7B shapes at TP 2/4/8: the 172 groups of 64 of down_proj's input split into whole
+    groups per rank (21 or 22 at TP 8), gate/up rows at the same points, q/k/v by heads."""
+    from otf_llm.decoder_stack import LLAMA2_7B, split_bounds
+    cfg = LLAMA2_7B
+    inter = [split_bounds(cfg.intermediate, r, world, cfg.group_size) for r in range(world)]
+    assert inter[0][0] == 0 and inter[-1][1] == cfg.intermediate
+    assert all(a[1] == b[0] for a, b in zip(inter, inter[1:]))
+    sizes = {hi - lo for lo, hi in inter}
+    assert all(s % cfg.group_size == 0 for s in sizes) and max(sizes) - min(sizes) <= cfg.group_size
+    heads = [split_bounds(cfg.heads * cfg.head_dim, r, world, cfg.head_dim) for r in range(world)]
+    assert {hi - lo for lo, hi in heads} == {cfg.heads * cfg.head_dim // world}
