@@ -427,6 +427,89 @@ def run_sweep(args):
         torch.cuda.empty_cache()
 
 
+def run_e2e(args):
+    """Greedy batch-1 decode of a random-init Llama-3.2-3B-architecture 2-bit model
+    (28 layers, hidden 3072, intermediate 8192, 24 q / 8 KV heads of 128, RoPE theta 5e5,
+    vocabulary 128256 with a tied INT8 embedding / head): P prompt tokens, then T generated
+    tokens, every token step one CUDA graph of native kernels (otf_llm.decode_model)."""
+    import torch
+    from otf_llm import _native
+    from otf_llm.decode_model import LLAMA32_3B, GreedyDecoder, ModelConfig
+    from otf_llm.decoder_stack import StackConfig, random_quantized_linear
+    from otf_llm.symmetric_2bit_engine import QuantizedEmbedding, QuantizedLinearHead
+    P, T = args.e2e_prompt, args.e2e_tokens
+    base = LLAMA32_3B
+    cfg = ModelConfig(layers=base.layers, hidden=base.hidden, intermediate=base.intermediate, heads=base.heads,
+                      kv_heads=base.kv_heads, head_dim=base.head_dim, vocab=base.vocab, rope_theta=base.rope_theta,
+                      max_pos=P + T + 8)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    qcfg = StackConfig(group_size=64, outlier_ratio=0.005, weight_std=0.02)
+    shapes = {"q_proj": (cfg.heads * cfg.head_dim, cfg.hidden), "k_proj": (cfg.kv_heads * cfg.head_dim, cfg.hidden),
+              "v_proj": (cfg.kv_heads * cfg.head_dim, cfg.hidden), "o_proj": (cfg.hidden, cfg.heads * cfg.head_dim),
+              "gate_proj": (cfg.intermediate, cfg.hidden), "up_proj": (cfg.intermediate, cfg.hidden),
+              "down_proj": (cfg.hidden, cfg.intermediate)}
+    layers = []
+    for li in range(cfg.layers):
+        layers.append({n: random_quantized_linear(N, K, qcfg, 7000 + li * 7 + pi, dev)
+                       for pi, (n, (N, K)) in enumerate(shapes.items())})
+    ones = torch.ones(cfg.hidden, dtype=torch.float16, device=dev)
+    # tied INT8 embedding / head from W_emb ~ N(0, 0.02^2): row absmax / 127 on the device
+    gen = torch.Generator(device=dev).manual_seed(11)
+    w8 = torch.empty(cfg.vocab, cfg.hidden, dtype=torch.int8, device=dev)
+    sc = torch.empty(cfg.vocab, 1, dtype=torch.float16, device=dev)
+    for lo in range(0, cfg.vocab, 16384):
+        hi = min(lo + 16384, cfg.vocab)
+        w = (torch.randn(hi - lo, cfg.hidden, generator=gen, device=dev) * 0.02).half().float()
+        step = w.abs().amax(dim=1, keepdim=True).div(127.0).clamp_min(1e-8)
+        w8[lo:hi] = w.div(step).round().clamp(-127, 127).to(torch.int8)
+        sc[lo:hi] = step.half()
+    with torch.device("meta"):
+        emb = QuantizedEmbedding(cfg.vocab, cfg.hidden)
+        head = QuantizedLinearHead(cfg.hidden, cfg.vocab)
+    emb.weight_int8, emb.scales = w8, sc
+    head.weight_int8, head.scales = w8, sc
+    dec = GreedyDecoder(cfg, layers, [(ones, ones)] * cfg.layers, emb, head, ones, dev)
+    dec.capture()
+    prompt = torch.randint(0, cfg.vocab, (P,), generator=torch.Generator().manual_seed(5)).to(dev)
+    for _ in range(max(1, args.warmup // 2)):
+        dec.generate(prompt[:16], 8)
+    torch.cuda.synchronize()
+    dec.reset()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record()
+    for i in range(P):
+        dec.ids.copy_(prompt[i:i + 1])
+        dec.graph.replay()
+    e1.record()
+    out = torch.empty(T, dtype=torch.int64, device=dev)
+    for i in range(T):
+        out[i:i + 1].copy_(dec.ids)
+        dec.graph.replay()
+    e2.record()
+    torch.cuda.synchronize()
+    t_pre = e0.elapsed_time(e1) / 1e3
+    t_dec = e1.elapsed_time(e2) / 1e3
+    lin_bytes = sum(m.packed_uint8.numel() + m.scales.shape[0] * m.scales.shape[1] * 2 +
+                    (m.outliers_fp16.numel() * 2 + m.outlier_indices.numel() * 8 if m.has_outliers else 0)
+                    for l in layers for m in l.values())
+    head_bytes = cfg.vocab * cfg.hidden + cfg.vocab * 2
+    line = {"metric": "decode tokens/s, Llama-3.2-3B architecture 2-bit (random init), batch 1",
+            "value": round(T / t_dec, 1), "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True,
+            "prompt_tokens": P, "new_tokens": T, "ms_per_token": round(t_dec / T * 1e3, 4),
+            "prefill_tokens_per_s": round(P / t_pre, 1),
+            "hbm_gbs": round((lin_bytes + head_bytes) * T / t_dec / 1e9, 1),
+            "bytes_per_token": {"linears": lin_bytes, "int8_head": head_bytes,
+                                "kv_cache_at_end": 2 * cfg.layers * (P + T) * cfg.kv_heads * cfg.head_dim * 2},
+            "data": "synthetic (random-init weights quantised on device; prompt = seeded uniform ids)",
+            "config": {"workload": "Llama-3.2-3B 2-bit greedy decode", "layers": cfg.layers, "hidden": cfg.hidden,
+                       "intermediate": cfg.intermediate, "heads": cfg.heads, "kv_heads": cfg.kv_heads,
+                       "vocab": cfg.vocab, "rope": "default, theta 5e5", "group_size": 64, "outlier_ratio": 0.005},
+            "gpu_launches_per_token": 6 * cfg.layers + 5, "device_error": _native.device_error(),
+            "first_tokens": [int(t) for t in out[:8].cpu()]}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default=None,
@@ -443,6 +526,9 @@ def main():
     ap.add_argument("--tp-exchange", choices=("peer", "nccl"), default="peer",
                     help="tensor-parallel exchange after o/down: fused NVLink peer stores, or NCCL all_reduce")
     ap.add_argument("--sweep", action="store_true", help="batch sweep at Llama-3-70B MLP shapes (JSON lines)")
+    ap.add_argument("--e2e", action="store_true", help="greedy decode of a Llama-3.2-3B-architecture 2-bit model")
+    ap.add_argument("--e2e-prompt", type=int, default=512)
+    ap.add_argument("--e2e-tokens", type=int, default=256)
     args = ap.parse_args()
     from otf_llm.decoder_stack import StackConfig
     cfg = StackConfig(layers=args.layers)
@@ -450,6 +536,8 @@ def main():
         run_case(args)
     elif args.sweep:
         run_sweep(args)
+    elif args.e2e:
+        run_e2e(args)
     elif args.impl == "reference":
         run_reference(args, cfg)
     else:

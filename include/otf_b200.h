@@ -316,6 +316,31 @@ OTF_API int otf2b_decode_prepare(const otf2b_decoder_layer* layers, const otf2b_
 /* One decode step: h (fp16 [hidden], 16-byte aligned) is the residual stream in and out. */
 OTF_API int otf2b_decode_step(const otf2b_decode_dims* dims, void* h, void* workspace, void* stream);
 
+/*
+ * Decode attention for a decoder stack with a KV cache (batch 1, grouped-query heads).
+ * Replaces the attention of HF's LlamaAttention that the reference runner keeps around its
+ * injected projections (otf_llm/run_symmetric_2bit.py:150-187); no reference counterpart
+ * as a library.  pos: int32 [1] in device memory, the position of the token being decoded.
+ *
+ * otf_rope_kv: rotate q (fp16 [heads, head_dim]) and k (fp16 [kv_heads, head_dim]) in place
+ * with cos_sin (fp16 [max_pos, 2, head_dim]: HF's cos then sin rows, halves duplicated;
+ * rotate_half form, fp16 arithmetic) and write k and v to row pos of the caches
+ * (fp16 [max_pos, kv_heads * head_dim]).
+ * otf_attn_decode: out (fp16 [heads * head_dim]) = softmax(q k^T * scale) v over cache rows
+ * 0..pos, query head j reading KV head j / (heads / kv_heads) (<= 8); split over groups of
+ * 64 positions, fp32 arithmetic.  head_dim 64 or 128.  workspace: caller-owned, zeroed once,
+ * otf_attn_workspace_bytes(...) bytes.
+ * otf_pos_advance: *pos += 1 (the last launch of a token step).
+ */
+OTF_API int otf_rope_kv(void* q, void* k, const void* v, const void* cos_sin, const int32_t* pos, void* k_cache,
+                        void* v_cache, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t max_pos,
+                        void* stream);
+OTF_API int64_t otf_attn_workspace_bytes(int64_t kv_heads, int64_t head_dim, int64_t max_pos);
+OTF_API int otf_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int32_t* pos, void* out,
+                            float scale, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t max_pos,
+                            void* workspace, int64_t workspace_bytes, void* stream);
+OTF_API int otf_pos_advance(int32_t* pos, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,251 @@
+// Batch-1 decode attention around the 2-bit projections: rotary embedding + KV-cache write,
+// split-KV attention over the cached positions, and the device-side position counter.
+//
+// These run between the q/k/v and o launches of a decoder layer when the decoder stack
+// does real attention (a growing fp16 KV cache, grouped-query heads, RoPE).  The position
+// of the token being decoded lives in device memory, so a whole token step -- embedding,
+// every layer, final norm, head argmax, position advance -- replays as one CUDA graph.
+//
+// Reference behaviour replaced: the attention of HF's LlamaAttention that the reference
+// runner keeps around its injected projections (otf_llm/run_symmetric_2bit.py:150-187):
+// RoPE with rotate_half in the projections' dtype (fp16), repeat_kv for grouped heads,
+// softmax(q k^T / sqrt(d)) v.  Here the dot products and the softmax run in fp32 (as the
+// fused SDPA kernels do); RoPE rounds like HF's fp16 elementwise ops.
+#include <algorithm>
+
+#include "otf_common.cuh"
+
+namespace otf {
+
+int set_cuda_error(cudaError_t e);  // capi.cu
+int check_device();                 // capi.cu
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kAttnMaxRep = 8;       // query heads per KV head
+constexpr int kAttnSplitPos = 64;    // cached positions per CTA (split-KV)
+
+// q (heads x D), k (kv_heads x D) rotated in place with cos/sin of position *pos; k and v
+// copied into the caches at row *pos.  HF rotate_half form, fp16 arithmetic:
+//   out[i]     = fp16(fp16(x[i] * c[i])         + fp16(-x[i + D/2] * s[i]))
+//   out[i+D/2] = fp16(fp16(x[i + D/2] * c[i+D/2]) + fp16( x[i] * s[i+D/2]))
+// cos_sin: fp16 [max_pos, 2, D] (cos row, then sin row; both halves duplicated as in HF).
+__global__ void k_rope_kv(uint16_t* q, uint16_t* k, const uint16_t* v, const uint16_t* cos_sin, const int* pos,
+                          uint16_t* kc, uint16_t* vc, int heads, int kv_heads, int D, int max_pos) {
+  pdl_trigger();
+  pdl_wait();
+  const int p = *pos;
+  if (p < 0 || p >= max_pos) return;  // the host sized the cache; an out-of-range position writes nothing
+  const int half = D / 2;
+  const uint16_t* cs = cos_sin + (int64_t)p * 2 * D;
+  const int nvec = (heads + kv_heads) * half;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < nvec; e += gridDim.x * blockDim.x) {
+    const int hh = e / half, i = e - hh * half;
+    uint16_t* x = hh < heads ? q + (int64_t)hh * D : k + (int64_t)(hh - heads) * D;
+    const __half a = __ushort_as_half(x[i]), b = __ushort_as_half(x[i + half]);
+    const __half c0 = __ushort_as_half(cs[i]), c1 = __ushort_as_half(cs[i + half]);
+    const __half s0 = __ushort_as_half(cs[D + i]), s1 = __ushort_as_half(cs[D + i + half]);
+    // _rn forms: each product and the sum round separately (no fused multiply-add), as the
+    // separate fp16 tensor ops do
+    const __half lo = __hadd_rn(__hmul_rn(a, c0), __hmul_rn(__hneg(b), s0));
+    const __half hi = __hadd_rn(__hmul_rn(b, c1), __hmul_rn(a, s1));
+    x[i] = __half_as_ushort(lo);
+    x[i + half] = __half_as_ushort(hi);
+    if (hh >= heads) {
+      uint16_t* krow = kc + (int64_t)p * kv_heads * D + (int64_t)(hh - heads) * D;
+      krow[i] = __half_as_ushort(lo);
+      krow[i + half] = __half_as_ushort(hi);
+    }
+  }
+  const int nv = kv_heads * D;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < nv; e += gridDim.x * blockDim.x)
+    vc[(int64_t)p * nv + e] = v[e];
+}
+
+// Split-KV attention: CTA (g, sp) takes KV head g and cached positions [sp*64, sp*64+64) for
+// the rep query heads of g; each warp walks a quarter of those positions with an online
+// softmax per query head (lane l holds dims 4l..4l+3 when D = 128, 2l..2l+1 when D = 64).
+// Partials (max, sum, acc) go to the workspace; the last CTA of head g (an atomic ticket,
+// no waiting) merges them and writes fp16 out.
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
+                                                              const int* pos, uint16_t* out, float scale, int heads,
+                                                              int kv_heads, int max_pos, float* ws, unsigned* tickets,
+                                                              int max_split) {
+  constexpr int PL = D / 32;  // dims per lane
+  pdl_trigger();
+  pdl_wait();
+  const int rep = heads / kv_heads;
+  const int g = blockIdx.x, sp = blockIdx.y;
+  const int L = min(*pos + 1, max_pos);
+  const int nsplit = min((L + kAttnSplitPos - 1) / kAttnSplitPos, max_split);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float sm_m[kAttnWarps][kAttnMaxRep], sm_l[kAttnWarps][kAttnMaxRep];
+  __shared__ float sm_acc[kAttnWarps][kAttnMaxRep][D];
+  __shared__ unsigned s_last;
+  if (sp >= nsplit) return;  // uniform per CTA: positions beyond the cache length
+  const int per = (L + nsplit - 1) / nsplit;
+  const int p0 = sp * per, p1 = min(L, p0 + per);
+  // (loops over query heads run to kAttnMaxRep with a guard, so the arrays stay in registers)
+  float qv[kAttnMaxRep][PL];
+#pragma unroll
+  for (int r = 0; r < kAttnMaxRep; ++r)
+#pragma unroll
+    for (int i = 0; i < PL; ++i) qv[r][i] = r < rep ? h2f(q[(int64_t)(g * rep + r) * D + lane * PL + i]) * scale : 0.0f;
+  float m[kAttnMaxRep], l[kAttnMaxRep], acc[kAttnMaxRep][PL];
+#pragma unroll
+  for (int r = 0; r < kAttnMaxRep; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) acc[r][i] = 0.0f;
+  }
+  const int64_t stride = (int64_t)kv_heads * D;
+  for (int p = p0 + warp; p < p1; p += kAttnWarps) {
+    const uint16_t* kr = kc + p * stride + (int64_t)g * D + lane * PL;
+    const uint16_t* vr = vc + p * stride + (int64_t)g * D + lane * PL;
+    float kf[PL], vf[PL];
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      kf[i] = h2f(kr[i]);
+      vf[i] = h2f(vr[i]);
+    }
+#pragma unroll
+    for (int r = 0; r < kAttnMaxRep; ++r) {
+      if (r >= rep) break;
+      float d = 0.0f;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) d = fmaf(qv[r][i], kf[i], d);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      const float mn = fmaxf(m[r], d);
+      const float corr = __expf(m[r] - mn), w = __expf(d - mn);
+      l[r] = l[r] * corr + w;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) acc[r][i] = fmaf(acc[r][i], corr, w * vf[i]);
+      m[r] = mn;
+    }
+  }
+  // Merge the warps of this CTA.
+#pragma unroll
+  for (int r = 0; r < kAttnMaxRep; ++r) {
+    if (r >= rep) break;
+    if (lane == 0) {
+      sm_m[warp][r] = m[r];
+      sm_l[warp][r] = l[r];
+    }
+#pragma unroll
+    for (int i = 0; i < PL; ++i) sm_acc[warp][r][lane * PL + i] = acc[r][i];
+  }
+  __syncthreads();
+  float* part = ws + ((int64_t)g * max_split + sp) * kAttnMaxRep * (D + 2);
+  for (int e = threadIdx.x; e < rep * D; e += kAttnThreads) {
+    const int r = e / D, dd = e - r * D;
+    float mm = -INFINITY;
+    for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, sm_m[w][r]);
+    float ll = 0.0f, aa = 0.0f;
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float c = sm_m[w][r] == -INFINITY ? 0.0f : __expf(sm_m[w][r] - mm);
+      ll += sm_l[w][r] * c;
+      aa += sm_acc[w][r][dd] * c;
+    }
+    part[r * (D + 2) + 2 + dd] = aa;
+    if (dd == 0) {
+      part[r * (D + 2)] = mm;
+      part[r * (D + 2) + 1] = ll;
+    }
+  }
+  // Last CTA of this KV head merges the splits (it reads partials the others published).
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(tickets + g, 1u) == (unsigned)nsplit - 1u) ? 1u : 0u;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < rep * D; e += kAttnThreads) {
+    const int r = e / D, dd = e - r * D;
+    float mm = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) mm = fmaxf(mm, __ldcg(ws + ((int64_t)g * max_split + s) * kAttnMaxRep * (D + 2) + r * (D + 2)));
+    float ll = 0.0f, aa = 0.0f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float* ps = ws + ((int64_t)g * max_split + s) * kAttnMaxRep * (D + 2) + r * (D + 2);
+      const float ms = __ldcg(ps);
+      const float c = ms == -INFINITY ? 0.0f : __expf(ms - mm);
+      ll += __ldcg(ps + 1) * c;
+      aa += __ldcg(ps + 2 + dd) * c;
+    }
+    out[(int64_t)(g * rep + r) * D + dd] = f2h(aa / ll);
+  }
+  if (threadIdx.x == 0) tickets[g] = 0u;  // re-armed for the next call
+}
+
+__global__ void k_pos_advance(int* pos) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x == 0 && blockIdx.x == 0) *pos += 1;
+}
+
+}  // namespace otf
+
+using otf::check_device;
+using otf::set_cuda_error;
+
+extern "C" OTF_API int otf_rope_kv(void* q, void* k, const void* v, const void* cos_sin, const int32_t* pos,
+                                   void* k_cache, void* v_cache, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                   int64_t max_pos, void* stream) {
+  if (!q || !k || !v || !cos_sin || !pos || !k_cache || !v_cache) return OTF_ERR_INVALID;
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 || head_dim % 2 || max_pos <= 0)
+    return OTF_ERR_INVALID;
+  int st = check_device();
+  if (st != OTF_OK) return st;
+  const int nvec = (int)((heads + kv_heads) * head_dim / 2);
+  const int blocks = std::max(1, std::min(otf::ceil_div(std::max(nvec, (int)(kv_heads * head_dim)), 256), 148));
+  return set_cuda_error(otf::launch_pdl(otf::k_rope_kv, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                                        1u, static_cast<uint16_t*>(q), static_cast<uint16_t*>(k),
+                                        static_cast<const uint16_t*>(v), static_cast<const uint16_t*>(cos_sin),
+                                        reinterpret_cast<const int*>(pos), static_cast<uint16_t*>(k_cache),
+                                        static_cast<uint16_t*>(v_cache), (int)heads, (int)kv_heads, (int)head_dim,
+                                        (int)max_pos));
+}
+
+extern "C" OTF_API int64_t otf_attn_workspace_bytes(int64_t kv_heads, int64_t head_dim, int64_t max_pos) {
+  if (kv_heads <= 0 || head_dim <= 0 || max_pos <= 0) return -1;
+  const int64_t max_split = (max_pos + otf::kAttnSplitPos - 1) / otf::kAttnSplitPos;
+  return otf::align_up(kv_heads * 4, 256) + kv_heads * max_split * otf::kAttnMaxRep * (head_dim + 2) * 4;
+}
+
+extern "C" OTF_API int otf_attn_decode(const void* q, const void* k_cache, const void* v_cache, const int32_t* pos,
+                                       void* out, float scale, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                       int64_t max_pos, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!q || !k_cache || !v_cache || !pos || !out || !workspace) return OTF_ERR_INVALID;
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || heads / kv_heads > otf::kAttnMaxRep || max_pos <= 0)
+    return OTF_ERR_INVALID;
+  if (head_dim != 64 && head_dim != 128) return OTF_ERR_UNSUPPORTED;
+  if (workspace_bytes < otf_attn_workspace_bytes(kv_heads, head_dim, max_pos)) return OTF_ERR_INVALID;
+  int st = check_device();
+  if (st != OTF_OK) return st;
+  const int max_split = (int)((max_pos + otf::kAttnSplitPos - 1) / otf::kAttnSplitPos);
+  unsigned* tickets = static_cast<unsigned*>(workspace);
+  float* ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + otf::align_up(kv_heads * 4, 256));
+  const dim3 grid((unsigned)kv_heads, (unsigned)max_split);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto* qq = static_cast<const uint16_t*>(q);
+  const auto* kc = static_cast<const uint16_t*>(k_cache);
+  const auto* vc = static_cast<const uint16_t*>(v_cache);
+  auto* o = static_cast<uint16_t*>(out);
+  const int* pp = reinterpret_cast<const int*>(pos);
+  cudaError_t e = head_dim == 128
+                      ? otf::launch_pdl(otf::k_attn_decode<128>, grid, dim3(otf::kAttnThreads), 0, s, 1u, qq, kc, vc, pp, o,
+                                        scale, (int)heads, (int)kv_heads, (int)max_pos, ws, tickets, max_split)
+                      : otf::launch_pdl(otf::k_attn_decode<64>, grid, dim3(otf::kAttnThreads), 0, s, 1u, qq, kc, vc, pp, o,
+                                        scale, (int)heads, (int)kv_heads, (int)max_pos, ws, tickets, max_split);
+  return set_cuda_error(e);
+}
+
+extern "C" OTF_API int otf_pos_advance(int32_t* pos, void* stream) {
+  if (!pos) return OTF_ERR_INVALID;
+  int st = check_device();
+  if (st != OTF_OK) return st;
+  return set_cuda_error(otf::launch_pdl(otf::k_pos_advance, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), 1u,
+                                        reinterpret_cast<int*>(pos)));
+}

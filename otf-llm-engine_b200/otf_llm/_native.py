@@ -100,6 +100,10 @@ EXPORTS = (
     "otf2b_decode_workspace_bytes",
     "otf2b_decode_prepare",
     "otf2b_decode_step",
+    "otf_rope_kv",
+    "otf_attn_workspace_bytes",
+    "otf_attn_decode",
+    "otf_pos_advance",
 )
 
 
@@ -159,6 +163,14 @@ def lib() -> ctypes.CDLL:
     L.otf2b_decode_prepare.restype = i32
     L.otf2b_decode_step.argtypes = [ctypes.POINTER(DecodeDims), vp, vp, vp]
     L.otf2b_decode_step.restype = i32
+    L.otf_rope_kv.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, vp]
+    L.otf_rope_kv.restype = i32
+    L.otf_attn_workspace_bytes.argtypes = [i64, i64, i64]
+    L.otf_attn_workspace_bytes.restype = i64
+    L.otf_attn_decode.argtypes = [vp, vp, vp, vp, vp, ctypes.c_float, i64, i64, i64, i64, vp, i64, vp]
+    L.otf_attn_decode.restype = i32
+    L.otf_pos_advance.argtypes = [vp, vp]
+    L.otf_pos_advance.restype = i32
     _lib = L
     return L
 

@@ -1,0 +1,175 @@
+"""Greedy batch-1 decoding of a whole 2-bit Llama-shaped model on the native kernels.
+
+Per token: INT8 embedding row -> per layer [RMSNorm + q/k/v] -> RoPE + KV-cache write ->
+decode attention over the cache -> [o + residual] -> [RMSNorm + gate/up] -> [SiLU gate +
+down + residual] -> final RMSNorm -> INT8 head with fused argmax -> position + 1.  The token
+id, the position and the KV caches live in device memory, so one token step is one CUDA
+graph replay (prompt tokens are fed by overwriting the id before a replay).
+
+This is what the reference's runner does for one generated token with HF's
+LlamaForCausalLM around the injected modules (otf_llm/run_symmetric_2bit.py:150-215):
+the projections are SymmetricOTF2BitLinear, the embedding / head QuantizedEmbedding /
+QuantizedLinearHead, attention and norms HF's.  Here every step is a native kernel.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _native
+from .symmetric_2bit_engine import QuantizedEmbedding, QuantizedLinearHead, SymmetricOTF2BitLinear
+
+PROJ = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+
+
+@dataclass
+class ModelConfig:
+    layers: int
+    hidden: int
+    intermediate: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    vocab: int
+    rope_theta: float = 500000.0
+    rms_eps: float = 1e-5
+    max_pos: int = 2048
+
+
+LLAMA32_3B = ModelConfig(layers=28, hidden=3072, intermediate=8192, heads=24, kv_heads=8, head_dim=128,
+                         vocab=128256, rope_theta=500000.0)
+
+
+def rope_table(cfg: ModelConfig, device) -> torch.Tensor:
+    """fp16 [max_pos, 2, head_dim]: HF's default rotary cos and sin rows (fp32 angles
+    pos * theta^(-2i/d), both halves duplicated, rounded to fp16 as HF casts them)."""
+    d = cfg.head_dim
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, dtype=torch.int64, device=device).float() / d))
+    pos = torch.arange(cfg.max_pos, device=device, dtype=torch.float32)
+    freqs = pos[:, None] * inv[None, :]
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return torch.stack((emb.cos(), emb.sin()), dim=1).to(torch.float16).contiguous()
+
+
+class GreedyDecoder:
+    """Batch-1 greedy decoding through native kernels (see module docstring)."""
+
+    def __init__(self, cfg: ModelConfig, layers: Sequence[Dict[str, SymmetricOTF2BitLinear]],
+                 norms: Sequence[Tuple[torch.Tensor, torch.Tensor]], embed: QuantizedEmbedding,
+                 head: QuantizedLinearHead, final_norm: Optional[torch.Tensor], device):
+        dev = torch.device(device)
+        self.cfg, self.device = cfg, dev
+        self.layers = [dict(l) for l in layers]
+        for l in self.layers:
+            missing = [n for n in PROJ if n not in l]
+            if missing:
+                raise ValueError(f"decoder layer lacks {missing}")
+        f16 = dict(dtype=torch.float16, device=dev)
+        self.in_norms = [a.to(**f16).contiguous() for a, _ in norms]
+        self.post_norms = [b.to(**f16).contiguous() for _, b in norms]
+        self.embed, self.head = embed, head
+        self.final_norm = (final_norm if final_norm is not None else torch.ones(cfg.hidden)).to(**f16).contiguous()
+        qd, kvd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+        self.kc = [torch.zeros(cfg.max_pos, kvd, **f16) for _ in self.layers]
+        self.vc = [torch.zeros(cfg.max_pos, kvd, **f16) for _ in self.layers]
+        self.cos_sin = rope_table(cfg, dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ids = torch.zeros(1, dtype=torch.int64, device=dev)
+        n = _native.lib().otf_attn_workspace_bytes(cfg.kv_heads, cfg.head_dim, cfg.max_pos)
+        self.attn_ws = torch.zeros(int(n), dtype=torch.uint8, device=dev)
+        self.b = {"h": torch.zeros(1, cfg.hidden, **f16), "h1": torch.zeros(1, cfg.hidden, **f16),
+                  "h2": torch.zeros(1, cfg.hidden, **f16), "q": torch.zeros(1, qd, **f16),
+                  "k": torch.zeros(1, kvd, **f16), "v": torch.zeros(1, kvd, **f16),
+                  "attn": torch.zeros(1, qd, **f16), "g": torch.zeros(1, cfg.intermediate, **f16),
+                  "u": torch.zeros(1, cfg.intermediate, **f16), "xn": torch.zeros(1, cfg.hidden, **f16)}
+        self.logits = torch.zeros(1, cfg.vocab, dtype=torch.float32, device=dev)
+        self.graph = None
+
+    # -- one token step (capturable) ----------------------------------------------------
+    def _step(self) -> None:
+        cfg, b, L = self.cfg, self.b, _native.lib()
+        G = _native.GroupItem
+        st = _native._stream(self.device)
+        h = self.embed(self.ids.view(1)).view(1, -1)
+        b["h"].copy_(h)
+        cur = b["h"]
+        scale = 1.0 / math.sqrt(cfg.head_dim)
+        for li, layer in enumerate(self.layers):
+            _native.linear_group([G(layer[n], cur, b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.in_norms[li],
+                                    eps=cfg.rms_eps) for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"))])
+            _native._check(L.otf_rope_kv(b["q"].data_ptr(), b["k"].data_ptr(), b["v"].data_ptr(),
+                                         self.cos_sin.data_ptr(), self.pos.data_ptr(), self.kc[li].data_ptr(),
+                                         self.vc[li].data_ptr(), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                         cfg.max_pos, st), "otf_rope_kv")
+            _native._check(L.otf_attn_decode(b["q"].data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
+                                             self.pos.data_ptr(), b["attn"].data_ptr(), scale, cfg.heads,
+                                             cfg.kv_heads, cfg.head_dim, cfg.max_pos, self.attn_ws.data_ptr(),
+                                             self.attn_ws.numel(), st), "otf_attn_decode")
+            _native.linear_group([G(layer["o_proj"], b["attn"], b["h1"], residual=cur)])
+            _native.linear_group([G(layer[n], b["h1"], b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.post_norms[li],
+                                    eps=cfg.rms_eps) for n, o in (("gate_proj", "g"), ("up_proj", "u"))])
+            # down writes the residual stream in place: o (its only other reader) already ran
+            _native.linear_group([G(layer["down_proj"], b["g"], b["h"], residual=b["h1"],
+                                    x_op=_native.OTF_XOP_SILU_MUL, x_aux=b["u"])])
+            cur = b["h"]
+        xn = _native.rmsnorm(cur, self.final_norm, cfg.rms_eps, out=b["xn"])
+        self._argmax(xn)
+        _native._check(L.otf_pos_advance(self.pos.data_ptr(), st), "otf_pos_advance")
+
+    def _argmax(self, xn: torch.Tensor) -> None:
+        hd = self.head
+        w, s = hd.weight_int8, hd.scales.reshape(-1)
+        L = _native.lib()
+        with torch.cuda.device(self.device):
+            _native._check(L.otf_i8_head_argmax(xn.data_ptr(), xn.shape[1], w.data_ptr(), w.stride(0), s.data_ptr(),
+                                                self.logits.data_ptr(), self.logits.shape[1], self.ids.data_ptr(), 1,
+                                                w.shape[0], w.shape[1], _native._stream(self.device)),
+                           "otf_i8_head_argmax")
+
+    def capture(self) -> None:
+        """Record one token step as a CUDA graph (warm-up steps run eagerly first, then the
+        position is reset)."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+        self.reset()
+
+    def reset(self) -> None:
+        self.pos.zero_()
+        torch.cuda.synchronize(self.device)
+
+    def step(self) -> None:
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._step()
+
+    def generate(self, prompt: torch.Tensor, new_tokens: int, logits_out: Optional[List[torch.Tensor]] = None
+                 ) -> torch.Tensor:
+        """Greedy continuation of prompt (int64 ids on the device) by new_tokens tokens."""
+        self.reset()
+        out = torch.empty(new_tokens, dtype=torch.int64, device=self.device)
+        n = prompt.numel()
+        for i in range(n):
+            self.ids.copy_(prompt[i:i + 1])
+            self.step()
+            if logits_out is not None:
+                logits_out.append(self.logits.clone())
+        for i in range(new_tokens):
+            out[i:i + 1].copy_(self.ids)
+            if i + 1 < new_tokens:
+                self.step()
+                if logits_out is not None:
+                    logits_out.append(self.logits.clone())
+        return out
