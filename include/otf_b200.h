@@ -341,6 +341,22 @@ OTF_API int otf_attn_decode(const void* q, const void* k_cache, const void* v_ca
                             void* workspace, int64_t workspace_bytes, void* stream);
 OTF_API int otf_pos_advance(int32_t* pos, void* stream);
 
+/*
+ * otf_attn_decode without a workspace argument, for callers that cannot allocate device
+ * memory (a plugin host that passes only the op's own tensors, an allocator frozen after
+ * warm-up, code that must not call cudaMalloc).  No counterpart in the reference.
+ * The split-KV scratch is one fixed array of OTF_ATTN_SCRATCH_BYTES that the library keeps on
+ * every GPU that loads it until the process exits; otf_attn_workspace_bytes(kv_heads,
+ * head_dim, max_pos) must not exceed it (OTF_ERR_UNSUPPORTED otherwise; e.g. 8 KV heads of
+ * 128 fit up to max_pos 4032).  Nothing is allocated.  The first call on each device looks up
+ * the array's device address: make that call before any stream capture.  All calls share the
+ * array, so calls that can run at the same time on one GPU (other streams) race.
+ */
+#define OTF_ATTN_SCRATCH_BYTES (2 * 1024 * 1024)
+OTF_API int otf_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const int32_t* pos,
+                                    void* out, float scale, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                    int64_t max_pos, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,6 +12,7 @@
 // softmax(q k^T / sqrt(d)) v.  Here the dot products and the softmax run in fp32 (as the
 // fused SDPA kernels do); RoPE rounds like HF's fp16 elementwise ops.
 #include <algorithm>
+#include <mutex>
 
 #include "otf_common.cuh"
 
@@ -248,4 +249,73 @@ extern "C" OTF_API int otf_pos_advance(int32_t* pos, void* stream) {
   if (st != OTF_OK) return st;
   return set_cuda_error(otf::launch_pdl(otf::k_pos_advance, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), 1u,
                                         reinterpret_cast<int*>(pos)));
+}
+
+// ---------------------------------------------------------------------------------------
+// Decode attention without a caller-provided workspace.
+//
+// Some callers cannot allocate device memory for the split-KV partials: runtimes that
+// hand a plugin only the tensors of the op (no allocator handle), code running under an
+// allocator that forbids new allocations after warm-up, and hosts that must not call
+// cudaMalloc at all.  For them the scratch lives in one fixed array that the library holds
+// on every GPU that loads it, for as long as the process runs.
+
+namespace otf {
+constexpr int64_t kAttnScratchBytes = OTF_ATTN_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_attn_scratch[kAttnScratchBytes];
+}  // namespace otf
+
+// Device address of the scratch array on the current device, looked up once per device
+// (the array's host-side name is not a device address).
+static int attn_scratch_ptr(unsigned char** out) {
+  static std::mutex mu;
+  static unsigned char* ptr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  if (dev < 0 || dev >= 64) return OTF_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, otf::g_attn_scratch);
+    if (e != cudaSuccess) return set_cuda_error(e);
+    ptr[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = ptr[dev];
+  return OTF_OK;
+}
+
+extern "C" OTF_API int otf_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                               const int32_t* pos, void* out, float scale, int64_t heads,
+                                               int64_t kv_heads, int64_t head_dim, int64_t max_pos, void* stream) {
+  if (!q || !k_cache || !v_cache || !pos || !out) return OTF_ERR_INVALID;
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || heads / kv_heads > otf::kAttnMaxRep || max_pos <= 0)
+    return OTF_ERR_INVALID;
+  if (head_dim != 64 && head_dim != 128) return OTF_ERR_UNSUPPORTED;
+  if (otf_attn_workspace_bytes(kv_heads, head_dim, max_pos) > otf::kAttnScratchBytes) return OTF_ERR_UNSUPPORTED;
+  int st = check_device();
+  if (st != OTF_OK) return st;
+  unsigned char* scratch = nullptr;
+  st = attn_scratch_ptr(&scratch);
+  if (st != OTF_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The per-head tickets must start at zero (a completed call leaves them there; clearing
+  // them here keeps a call independent of how an earlier one ended).
+  const int64_t tbytes = otf::align_up(kv_heads * 4, 256);
+  cudaError_t e = cudaMemsetAsync(scratch, 0, (size_t)(kv_heads * 4), s);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  const int max_split = (int)((max_pos + otf::kAttnSplitPos - 1) / otf::kAttnSplitPos);
+  unsigned* tickets = reinterpret_cast<unsigned*>(scratch);
+  float* ws = reinterpret_cast<float*>(scratch + tbytes);
+  const dim3 grid((unsigned)kv_heads, (unsigned)max_split);
+  const auto* qq = static_cast<const uint16_t*>(q);
+  const auto* kc = static_cast<const uint16_t*>(k_cache);
+  const auto* vc = static_cast<const uint16_t*>(v_cache);
+  auto* o = static_cast<uint16_t*>(out);
+  const int* pp = reinterpret_cast<const int*>(pos);
+  e = head_dim == 128 ? otf::launch_pdl(otf::k_attn_decode<128>, grid, dim3(otf::kAttnThreads), 0, s, 1u, qq, kc, vc,
+                                        pp, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws, tickets, max_split)
+                      : otf::launch_pdl(otf::k_attn_decode<64>, grid, dim3(otf::kAttnThreads), 0, s, 1u, qq, kc, vc,
+                                        pp, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws, tickets, max_split);
+  return set_cuda_error(e);
 }

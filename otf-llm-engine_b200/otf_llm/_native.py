@@ -104,6 +104,7 @@ EXPORTS = (
     "otf_attn_workspace_bytes",
     "otf_attn_decode",
     "otf_pos_advance",
+    "otf_attn_decode_noalloc",
 )
 
 
@@ -171,6 +172,8 @@ def lib() -> ctypes.CDLL:
     L.otf_attn_decode.restype = i32
     L.otf_pos_advance.argtypes = [vp, vp]
     L.otf_pos_advance.restype = i32
+    L.otf_attn_decode_noalloc.argtypes = [vp, vp, vp, vp, vp, ctypes.c_float, i64, i64, i64, i64, vp]
+    L.otf_attn_decode_noalloc.restype = i32
     _lib = L
     return L
 
