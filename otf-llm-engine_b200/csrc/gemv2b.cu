@@ -477,6 +477,20 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
       }
     }
     named_barrier_sync(1, kCThreads);
+    // Anchor dot products of the rows this CTA finishes, one row per thread, from the
+    // weights the bulk copy brought in (or from global memory when they did not fit).
+    if (a.n_out > 0 && tid < nfin) {
+      float d = 0.0f;
+      if (ov_smem) {
+        if (!mbar_wait(ov_bar, 0u)) report_wait_failure();
+        const uint16_t* ovr = reinterpret_cast<const uint16_t*>(smem + L.ov + ov_skew) + (int64_t)tid * a.ldo;
+        for (int j = 0; j < a.n_out; ++j) d = fmaf(xo[j], h2f(ovr[j]), d);
+      } else {
+        const uint16_t* ovr = a.ovals + (int64_t)(frow0 + tid) * a.ldo;
+        for (int j = 0; j < a.n_out; ++j) d = fmaf(xo[j], h2f(ldg_u16(ovr + j)), d);
+      }
+      afin_sum[tid] = d;
+    }
 
     // Main loop: my tiles tl = warp + 8*i, their chunks in order, one stage each.  The MMA
     // accumulators run across a tile's stages; each set's contribution is the difference of
@@ -600,21 +614,6 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
       }
     }
     cp_async_wait<0>();
-    // Anchor dot products of the rows this CTA finishes, one row per thread, from the
-    // weights the bulk copy brought in at entry (or from global memory when they did not
-    // fit) -- after the main loop, so they overlap the other warps' last stages.
-    if (a.n_out > 0 && tid < nfin) {
-      float d = 0.0f;
-      if (ov_smem) {
-        if (!mbar_wait(ov_bar, 0u)) report_wait_failure();
-        const uint16_t* ovr = reinterpret_cast<const uint16_t*>(smem + L.ov + ov_skew) + (int64_t)tid * a.ldo;
-        for (int j = 0; j < a.n_out; ++j) d = fmaf(xo[j], h2f(ovr[j]), d);
-      } else {
-        const uint16_t* ovr = a.ovals + (int64_t)(frow0 + tid) * a.ldo;
-        for (int j = 0; j < a.n_out; ++j) d = fmaf(xo[j], h2f(ldg_u16(ovr + j)), d);
-      }
-      afin_sum[tid] = d;
-    }
     // One cluster barrier below: every partial has landed in its finisher's shared memory.
     cluster_sync_all();
     const bool ar_prod = a.ar_mode == OTF_AR_PRODUCE;
