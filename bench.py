@@ -505,7 +505,7 @@ def run_e2e(args):
             "config": {"workload": "Llama-3.2-3B 2-bit greedy decode", "layers": cfg.layers, "hidden": cfg.hidden,
                        "intermediate": cfg.intermediate, "heads": cfg.heads, "kv_heads": cfg.kv_heads,
                        "vocab": cfg.vocab, "rope": "default, theta 5e5", "group_size": 64, "outlier_ratio": 0.005},
-            "gpu_launches_per_token": 6 * cfg.layers + 5, "device_error": _native.device_error(),
+            "gpu_launches_per_token": 5 * cfg.layers + 5, "device_error": _native.device_error(),
             "first_tokens": [int(t) for t in out[:8].cpu()]}
     print(json.dumps(line), flush=True)
 

@@ -340,6 +340,15 @@ OTF_API int otf_attn_decode(const void* q, const void* k_cache, const void* v_ca
                             float scale, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t max_pos,
                             void* workspace, int64_t workspace_bytes, void* stream);
 OTF_API int otf_pos_advance(int32_t* pos, void* stream);
+/*
+ * otf_rope_kv followed by otf_attn_decode in one launch: q, k, v as the q/k/v projections
+ * wrote them (unrotated), the caches get row pos (rotated k, v), out as otf_attn_decode.
+ * Same workspace (otf_attn_workspace_bytes) and the same results.
+ */
+OTF_API int otf_attn_rope_decode(const void* q, const void* k, const void* v, const void* cos_sin, const int32_t* pos,
+                                 void* k_cache, void* v_cache, void* out, float scale, int64_t heads,
+                                 int64_t kv_heads, int64_t head_dim, int64_t max_pos, void* workspace,
+                                 int64_t workspace_bytes, void* stream);
 
 /*
  * otf_attn_decode without a workspace argument, for callers that cannot allocate device

@@ -180,6 +180,173 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const uint16_t* q,
   if (threadIdx.x == 0) tickets[g] = 0u;  // re-armed for the next call
 }
 
+// RoPE, KV-cache write and split-KV attention in one launch.  Same split of the cached
+// positions and the same partial/ticket merge as k_attn_decode, with three changes:
+//  * every CTA rotates the query heads it needs in registers (the partner half of a head's
+//    vector is 16 lanes away: one shuffle), so q is read unrotated;
+//  * the CTA whose split holds the new position rotates that position's k, writes k and v to
+//    the cache rows and makes them visible to its own warps with a CTA barrier (no other CTA
+//    reads that row in this call);
+//  * 8 warps per CTA, each issuing the loads of up to 4 cached positions before using them.
+constexpr int kAttn2Warps = 8;
+constexpr int kAttn2Threads = kAttn2Warps * 32;
+constexpr int kAttn2Batch = 4;
+
+template <int PL>
+__device__ __forceinline__ void rope_lane(const uint16_t* x, const uint16_t* cs, int D, int lane, __half (&o)[PL]) {
+  __half xv[PL];
+#pragma unroll
+  for (int i = 0; i < PL; ++i) xv[i] = __ushort_as_half(x[lane * PL + i]);
+#pragma unroll
+  for (int i = 0; i < PL; ++i) {
+    const __half pv = __ushort_as_half((uint16_t)__shfl_xor_sync(0xffffffffu, (int)__half_as_ushort(xv[i]), 16));
+    const int dim = lane * PL + i;
+    const __half c = __ushort_as_half(cs[dim]), sn = __ushort_as_half(cs[D + dim]);
+    const __half t = lane < 16 ? __hmul_rn(__hneg(pv), sn) : __hmul_rn(pv, sn);
+    o[i] = __hadd_rn(__hmul_rn(xv[i], c), t);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
+    const uint16_t* q, const uint16_t* knew, const uint16_t* vnew, const uint16_t* cos_sin, const int* pos,
+    uint16_t* kc, uint16_t* vc, uint16_t* out, float scale, int heads, int kv_heads, int max_pos, float* ws,
+    unsigned* tickets, int max_split) {
+  constexpr int PL = D / 32;
+  pdl_trigger();
+  pdl_wait();
+  const int p = *pos;
+  if (p < 0 || p >= max_pos) return;  // the host sized the cache; out of range writes nothing
+  const int rep = heads / kv_heads;
+  const int g = blockIdx.x, sp = blockIdx.y;
+  const int L = p + 1;
+  const int nsplit = min((L + kAttnSplitPos - 1) / kAttnSplitPos, max_split);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float sm_m[kAttn2Warps][kAttnMaxRep], sm_l[kAttn2Warps][kAttnMaxRep];
+  __shared__ float sm_acc[kAttn2Warps][kAttnMaxRep][D];
+  __shared__ unsigned s_last;
+  if (sp >= nsplit) return;  // uniform per CTA
+  const int per = (L + nsplit - 1) / nsplit;
+  const int p0 = sp * per, p1 = min(L, p0 + per);
+  const uint16_t* cs = cos_sin + (int64_t)p * 2 * D;
+  const int64_t stride = (int64_t)kv_heads * D;
+  if (p1 == L && warp == 0) {
+    __half kr[PL];
+    rope_lane<PL>(knew + (int64_t)g * D, cs, D, lane, kr);
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      kc[p * stride + (int64_t)g * D + lane * PL + i] = __half_as_ushort(kr[i]);
+      vc[p * stride + (int64_t)g * D + lane * PL + i] = vnew[(int64_t)g * D + lane * PL + i];
+    }
+  }
+  __syncthreads();  // the new cache row is visible to this CTA's warps
+  float qv[kAttnMaxRep][PL];
+#pragma unroll
+  for (int r = 0; r < kAttnMaxRep; ++r) {
+    if (r < rep) {
+      __half qr[PL];
+      rope_lane<PL>(q + (int64_t)(g * rep + r) * D, cs, D, lane, qr);
+#pragma unroll
+      for (int i = 0; i < PL; ++i) qv[r][i] = __half2float(qr[i]) * scale;
+    } else {
+#pragma unroll
+      for (int i = 0; i < PL; ++i) qv[r][i] = 0.0f;
+    }
+  }
+  float m[kAttnMaxRep], l[kAttnMaxRep], acc[kAttnMaxRep][PL];
+#pragma unroll
+  for (int r = 0; r < kAttnMaxRep; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) acc[r][i] = 0.0f;
+  }
+  for (int base = p0 + warp; base < p1; base += kAttn2Warps * kAttn2Batch) {
+    float kf[kAttn2Batch][PL], vf[kAttn2Batch][PL];
+#pragma unroll
+    for (int j = 0; j < kAttn2Batch; ++j) {
+      const int pp = base + j * kAttn2Warps;
+      const int pc = pp < p1 ? pp : p0;  // a valid row; its values are not used
+      const uint16_t* kr = kc + pc * stride + (int64_t)g * D + lane * PL;
+      const uint16_t* vr = vc + pc * stride + (int64_t)g * D + lane * PL;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) {
+        kf[j][i] = h2f(kr[i]);
+        vf[j][i] = h2f(vr[i]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kAttn2Batch; ++j) {
+      if (base + j * kAttn2Warps >= p1) break;
+#pragma unroll
+      for (int r = 0; r < kAttnMaxRep; ++r) {
+        if (r >= rep) break;
+        float d = 0.0f;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) d = fmaf(qv[r][i], kf[j][i], d);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        const float mn = fmaxf(m[r], d);
+        const float corr = __expf(m[r] - mn), w = __expf(d - mn);
+        l[r] = l[r] * corr + w;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) acc[r][i] = fmaf(acc[r][i], corr, w * vf[j][i]);
+        m[r] = mn;
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kAttnMaxRep; ++r) {
+    if (r >= rep) break;
+    if (lane == 0) {
+      sm_m[warp][r] = m[r];
+      sm_l[warp][r] = l[r];
+    }
+#pragma unroll
+    for (int i = 0; i < PL; ++i) sm_acc[warp][r][lane * PL + i] = acc[r][i];
+  }
+  __syncthreads();
+  float* part = ws + ((int64_t)g * max_split + sp) * kAttnMaxRep * (D + 2);
+  for (int e = threadIdx.x; e < rep * D; e += kAttn2Threads) {
+    const int r = e / D, dd = e - r * D;
+    float mm = -INFINITY;
+    for (int w = 0; w < kAttn2Warps; ++w) mm = fmaxf(mm, sm_m[w][r]);
+    float ll = 0.0f, aa = 0.0f;
+    for (int w = 0; w < kAttn2Warps; ++w) {
+      const float c = sm_m[w][r] == -INFINITY ? 0.0f : __expf(sm_m[w][r] - mm);
+      ll += sm_l[w][r] * c;
+      aa += sm_acc[w][r][dd] * c;
+    }
+    part[r * (D + 2) + 2 + dd] = aa;
+    if (dd == 0) {
+      part[r * (D + 2)] = mm;
+      part[r * (D + 2) + 1] = ll;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(tickets + g, 1u) == (unsigned)nsplit - 1u) ? 1u : 0u;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < rep * D; e += kAttn2Threads) {
+    const int r = e / D, dd = e - r * D;
+    const float* pb = ws + (int64_t)g * max_split * kAttnMaxRep * (D + 2) + r * (D + 2);
+    float mm = -INFINITY;
+    for (int s2 = 0; s2 < nsplit; ++s2) mm = fmaxf(mm, __ldcg(pb + (int64_t)s2 * kAttnMaxRep * (D + 2)));
+    float ll = 0.0f, aa = 0.0f;
+    for (int s2 = 0; s2 < nsplit; ++s2) {
+      const float* ps = pb + (int64_t)s2 * kAttnMaxRep * (D + 2);
+      const float ms = __ldcg(ps);
+      const float c = ms == -INFINITY ? 0.0f : __expf(ms - mm);
+      ll += __ldcg(ps + 1) * c;
+      aa += __ldcg(ps + 2 + dd) * c;
+    }
+    out[(int64_t)(g * rep + r) * D + dd] = f2h(aa / ll);
+  }
+  if (threadIdx.x == 0) tickets[g] = 0u;  // re-armed for the next call
+}
+
 __global__ void k_pos_advance(int* pos) {
   pdl_trigger();
   pdl_wait();
@@ -240,6 +407,40 @@ extern "C" OTF_API int otf_attn_decode(const void* q, const void* k_cache, const
                                         scale, (int)heads, (int)kv_heads, (int)max_pos, ws, tickets, max_split)
                       : otf::launch_pdl(otf::k_attn_decode<64>, grid, dim3(otf::kAttnThreads), 0, s, 1u, qq, kc, vc, pp, o,
                                         scale, (int)heads, (int)kv_heads, (int)max_pos, ws, tickets, max_split);
+  return set_cuda_error(e);
+}
+
+extern "C" OTF_API int otf_attn_rope_decode(const void* q, const void* k, const void* v, const void* cos_sin,
+                                            const int32_t* pos, void* k_cache, void* v_cache, void* out, float scale,
+                                            int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t max_pos,
+                                            void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !cos_sin || !pos || !k_cache || !v_cache || !out || !workspace) return OTF_ERR_INVALID;
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || heads / kv_heads > otf::kAttnMaxRep || max_pos <= 0)
+    return OTF_ERR_INVALID;
+  if (head_dim != 64 && head_dim != 128) return OTF_ERR_UNSUPPORTED;
+  if (workspace_bytes < otf_attn_workspace_bytes(kv_heads, head_dim, max_pos)) return OTF_ERR_INVALID;
+  int st = check_device();
+  if (st != OTF_OK) return st;
+  const int max_split = (int)((max_pos + otf::kAttnSplitPos - 1) / otf::kAttnSplitPos);
+  unsigned* tickets = static_cast<unsigned*>(workspace);
+  float* ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + otf::align_up(kv_heads * 4, 256));
+  const dim3 grid((unsigned)kv_heads, (unsigned)max_split);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto* qq = static_cast<const uint16_t*>(q);
+  const auto* kn = static_cast<const uint16_t*>(k);
+  const auto* vn = static_cast<const uint16_t*>(v);
+  const auto* cs = static_cast<const uint16_t*>(cos_sin);
+  const int* pp = reinterpret_cast<const int*>(pos);
+  auto* kc = static_cast<uint16_t*>(k_cache);
+  auto* vc = static_cast<uint16_t*>(v_cache);
+  auto* o = static_cast<uint16_t*>(out);
+  cudaError_t e = head_dim == 128
+                      ? otf::launch_pdl(otf::k_attn_rope_decode<128>, grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
+                                        vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
+                                        tickets, max_split)
+                      : otf::launch_pdl(otf::k_attn_rope_decode<64>, grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
+                                        vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
+                                        tickets, max_split);
   return set_cuda_error(e);
 }
 

@@ -105,6 +105,7 @@ EXPORTS = (
     "otf_attn_decode",
     "otf_pos_advance",
     "otf_attn_decode_noalloc",
+    "otf_attn_rope_decode",
 )
 
 
@@ -174,6 +175,8 @@ def lib() -> ctypes.CDLL:
     L.otf_pos_advance.restype = i32
     L.otf_attn_decode_noalloc.argtypes = [vp, vp, vp, vp, vp, ctypes.c_float, i64, i64, i64, i64, vp]
     L.otf_attn_decode_noalloc.restype = i32
+    L.otf_attn_rope_decode.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, i64, i64, i64, i64, vp, i64, vp]
+    L.otf_attn_rope_decode.restype = i32
     _lib = L
     return L
 

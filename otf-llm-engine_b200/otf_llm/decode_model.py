@@ -1,7 +1,7 @@
 """Greedy batch-1 decoding of a whole 2-bit Llama-shaped model on the native kernels.
 
-Per token: INT8 embedding row -> per layer [RMSNorm + q/k/v] -> RoPE + KV-cache write ->
-decode attention over the cache -> [o + residual] -> [RMSNorm + gate/up] -> [SiLU gate +
+Per token: INT8 embedding row -> per layer [RMSNorm + q/k/v] -> [RoPE + KV-cache write +
+decode attention over the cache] -> [o + residual] -> [RMSNorm + gate/up] -> [SiLU gate +
 down + residual] -> final RMSNorm -> INT8 head with fused argmax -> position + 1.  The token
 id, the position and the KV caches live in device memory, so one token step is one CUDA
 graph replay (prompt tokens are fed by overwriting the id before a replay).
@@ -101,14 +101,12 @@ class GreedyDecoder:
         for li, layer in enumerate(self.layers):
             _native.linear_group([G(layer[n], cur, b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.in_norms[li],
                                     eps=cfg.rms_eps) for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"))])
-            _native._check(L.otf_rope_kv(b["q"].data_ptr(), b["k"].data_ptr(), b["v"].data_ptr(),
-                                         self.cos_sin.data_ptr(), self.pos.data_ptr(), self.kc[li].data_ptr(),
-                                         self.vc[li].data_ptr(), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                         cfg.max_pos, st), "otf_rope_kv")
-            _native._check(L.otf_attn_decode(b["q"].data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
-                                             self.pos.data_ptr(), b["attn"].data_ptr(), scale, cfg.heads,
-                                             cfg.kv_heads, cfg.head_dim, cfg.max_pos, self.attn_ws.data_ptr(),
-                                             self.attn_ws.numel(), st), "otf_attn_decode")
+            # RoPE, KV-cache write and attention in one launch
+            _native._check(L.otf_attn_rope_decode(b["q"].data_ptr(), b["k"].data_ptr(), b["v"].data_ptr(),
+                                                  self.cos_sin.data_ptr(), self.pos.data_ptr(), self.kc[li].data_ptr(),
+                                                  self.vc[li].data_ptr(), b["attn"].data_ptr(), scale, cfg.heads,
+                                                  cfg.kv_heads, cfg.head_dim, cfg.max_pos, self.attn_ws.data_ptr(),
+                                                  self.attn_ws.numel(), st), "otf_attn_rope_decode")
             _native.linear_group([G(layer["o_proj"], b["attn"], b["h1"], residual=cur)])
             _native.linear_group([G(layer[n], b["h1"], b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.post_norms[li],
                                     eps=cfg.rms_eps) for n, o in (("gate_proj", "g"), ("up_proj", "u"))])

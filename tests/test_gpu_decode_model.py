@@ -150,3 +150,45 @@ def test_greedy_decoder_matches_hf_model(graph, cuda_dev):
     clear = (top2[:, 0] - top2[:, 1]) > 0.05 * ref.abs().max()
     assert bool((got.argmax(-1) == ref.argmax(-1))[clear].all())
     assert _lib().device_error() == 0
+
+
+@pytest.mark.parametrize("hd,heads,kv", [(128, 24, 8), (64, 8, 2)])
+def test_fused_rope_attention_matches_two_launches(hd, heads, kv, cuda_dev):
+    """otf_attn_rope_decode against otf_rope_kv + otf_attn_decode: the same cache rows and
+    the same attention output, over a run of consecutive positions (splits of 64 crossed)."""
+    from otf_llm.decode_model import ModelConfig, rope_table
+    N = _lib()
+    L_ = N.lib()
+    cfg = ModelConfig(layers=1, hidden=heads * hd, intermediate=64, heads=heads, kv_heads=kv, head_dim=hd, vocab=16,
+                      max_pos=160)
+    cs = rope_table(cfg, cuda_dev)
+    g = torch.Generator(device=cuda_dev).manual_seed(hd)
+    f16 = dict(dtype=torch.float16, device=cuda_dev)
+    kc_a, vc_a = torch.zeros(cfg.max_pos, kv * hd, **f16), torch.zeros(cfg.max_pos, kv * hd, **f16)
+    kc_b, vc_b = kc_a.clone(), vc_a.clone()
+    nb = int(L_.otf_attn_workspace_bytes(kv, hd, cfg.max_pos))
+    ws_a = torch.zeros(nb, dtype=torch.uint8, device=cuda_dev)
+    ws_b = torch.zeros_like(ws_a)
+    scale = 1.0 / math.sqrt(hd)
+    st = N._stream(cuda_dev)
+    worst = 0.0
+    for p in list(range(0, 70)) + [127, 128, 150]:
+        q = torch.randn(heads * hd, generator=g, device=cuda_dev).half()
+        k = torch.randn(kv * hd, generator=g, device=cuda_dev).half()
+        v = torch.randn(kv * hd, generator=g, device=cuda_dev).half()
+        pos = torch.tensor([p], dtype=torch.int32, device=cuda_dev)
+        out_a = torch.empty(heads * hd, **f16)
+        out_b = torch.empty_like(out_a)
+        qa, ka = q.clone(), k.clone()
+        N._check(L_.otf_rope_kv(qa.data_ptr(), ka.data_ptr(), v.data_ptr(), cs.data_ptr(), pos.data_ptr(),
+                                kc_a.data_ptr(), vc_a.data_ptr(), heads, kv, hd, cfg.max_pos, st), "otf_rope_kv")
+        N._check(L_.otf_attn_decode(qa.data_ptr(), kc_a.data_ptr(), vc_a.data_ptr(), pos.data_ptr(), out_a.data_ptr(),
+                                    scale, heads, kv, hd, cfg.max_pos, ws_a.data_ptr(), nb, st), "otf_attn_decode")
+        N._check(L_.otf_attn_rope_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), cs.data_ptr(), pos.data_ptr(),
+                                         kc_b.data_ptr(), vc_b.data_ptr(), out_b.data_ptr(), scale, heads, kv, hd,
+                                         cfg.max_pos, ws_b.data_ptr(), nb, st), "otf_attn_rope_decode")
+        torch.cuda.synchronize()
+        assert torch.equal(kc_a[p], kc_b[p]) and torch.equal(vc_a[p], vc_b[p])
+        worst = max(worst, rel_err(out_b.float().cpu().numpy(), out_a.float().cpu().numpy()))
+    assert worst < 2e-3
+    assert _lib().device_error() == 0
