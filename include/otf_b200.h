@@ -189,6 +189,31 @@ typedef struct otf2b_layer {
 OTF_API int otf2b_linear_group(const otf2b_layer* layers, int n_layers, void* stream);
 
 /*
+ * Symmetric 2-bit quantizer (replaces Symmetric2BitQuantizer.quantize_tensor,
+ * otf_llm/symmetric_2bit_engine.py:109-169; packing as pack_2bit_uint8, :100-107).
+ * w: [N, ldw] of w_dtype (OTF_DTYPE_*), ldw a multiple of 4, w aligned to 4 elements.
+ * Column impact ||w[:, c]||_2 (* act[c] when act, fp32 [K], is not NULL); the n_outliers
+ * largest columns (descending, ties to the lower index) go to outlier_idx (int64 [n_outliers])
+ * and outliers (fp16 [N, ldo], column j = fp16(w[:, outlier_idx[j]])), and count as zero in
+ * the fit.  Per group of group_size (16, 32, 64, 128 or 256) columns: RMS start and five
+ * rounds of nearest-centroid codes + least-squares scale over codebook (4 fp32 values in host
+ * memory; NULL = the reference's -1.52, -0.45, 0.45, 1.52).  packed: uint8 [N, ldp] (four
+ * codes per byte, code j at bits 2*(j%4)); scales: fp16 [N, lds].  n_outliers = 0 needs no
+ * workspace; otherwise workspace (256-byte aligned) of otf2b_quantize_workspace_bytes(N, K).
+ * Sums run in a fixed order, so a scale can differ from the torch reference by one fp16 ulp
+ * where its fp32 value lies next to an fp16 rounding boundary; codes, indices and anchor
+ * values follow the reference.
+ */
+#define OTF_DTYPE_F16 0
+#define OTF_DTYPE_BF16 1
+#define OTF_DTYPE_F32 2
+OTF_API int64_t otf2b_quantize_workspace_bytes(int64_t N, int64_t K);
+OTF_API int otf2b_quantize(const void* w, int w_dtype, int64_t ldw, int64_t N, int64_t K, int64_t group_size,
+                           const float* act, int64_t n_outliers, const float* codebook, void* workspace,
+                           int64_t workspace_bytes, uint8_t* packed, int64_t ldp, void* scales, int64_t lds,
+                           void* outliers, int64_t ldo, int64_t* outlier_idx, void* stream);
+
+/*
  * Unpack 2-bit codes to one byte per code: codes[n,k] = q[n,k] in {0..3}.
  * The inverse of pack_2bit_uint8 (otf_llm/symmetric_2bit_engine.py:100-107) and the
  * code-extraction step of unpack_2bit_uint8 (otf_llm/otf_2bit_quantizer.py:58-63).

@@ -48,6 +48,7 @@ def lib() -> ctypes.CDLL:
         _LIB.orc_i8_embed.argtypes = [vp, i64, vp, i64, vp, vp, i64, i64, i64]
         _LIB.orc_i8_embed.restype = i64
         _LIB.orc_i8_quantize.argtypes = [vp, i64, i64, i64, vp, vp]
+        _LIB.orc_quantize_2b.argtypes = [vp, i64, i64, i64, i64, vp, i64, vp, vp, vp, vp, vp]
         _LIB.orc_num_threads.restype = ctypes.c_int
         _LIB.orc_set_num_threads.argtypes = [ctypes.c_int]
     return _LIB
@@ -177,3 +178,31 @@ def i8_quantize(w_f16):
     s = np.empty(V, dtype=np.float16)
     lib().orc_i8_quantize(_p(w), D, V, D, _p(q), _p(s))
     return q, s.reshape(V, 1)
+
+
+def n_outliers(K: int, ratio: float) -> int:
+    """Anchor column count of quantize_tensor: max(1, int(K * ratio)) when ratio > 0, else 0
+    (otf_llm/symmetric_2bit_engine.py:132)."""
+    return max(1, int(K * ratio)) if ratio > 0.0 else 0
+
+
+def quantize_2b(W, group_size: int, ratio: float, act=None, codebook=CB_F32):
+    """Symmetric2BitQuantizer.quantize_tensor (otf_llm/symmetric_2bit_engine.py:109-169) in
+    the fixed summation order of orc_quantize_2b.  W: float array [N, K] (fp16/bf16 values are
+    exact in fp32).  Returns (packed uint8 [N, K/4], scales fp16 [N, K/G], outliers fp16 [N, k]
+    or None, indices int64 [k] or None)."""
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    N, K = W.shape
+    G = int(group_size)
+    assert K % G == 0 and G % 4 == 0 and G <= 256
+    k = n_outliers(K, ratio)
+    a = None if act is None else _c(act, np.float32)
+    cb = _c(codebook, np.float32)
+    packed = np.empty((N, K // 4), np.uint8)
+    scales = np.empty((N, K // G), np.float16)
+    ov = np.empty((N, max(k, 1)), np.float16)
+    idx = np.empty(max(k, 1), np.int64)
+    lib().orc_quantize_2b(_p(W), K, N, K, G, _p(a), k, _p(cb), _p(packed), _p(scales), _p(ov), _p(idx))
+    if k == 0:
+        return packed, scales, None, None
+    return packed, scales, ov, idx

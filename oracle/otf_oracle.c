@@ -234,6 +234,137 @@ void orc_i8_quantize(const h16* wf, int64_t ldw, int64_t V, int64_t D, int8_t* q
   }
 }
 
+/* Symmetric 2-bit quantizer, Symmetric2BitQuantizer.quantize_tensor
+ * (otf_llm/symmetric_2bit_engine.py:109-169, packing :100-107), in fp32 with every product
+ * and sum rounded on its own (no fused multiply-add) and the sums in this fixed order:
+ *   column sums of squares over row chunks of QUANT_IMPACT_ROWS rows (row order inside a
+ *   chunk, then chunk order), sqrt, times act[c];
+ *   group sums: TL = min(32, G/4) partial sums, partial l taking elements 4l..4l+3 of each
+ *   slab of 4*TL elements in slab order, then combined pairwise (l + TL/2, ..., l + 1).
+ * Anchors: the k columns of largest impact, descending, ties to the lower index, NaN above
+ * everything.  The torch reference sums in an order that depends on the device and vector
+ * width; the two agree except for scales next to an fp16 rounding boundary (one ulp apart). */
+#define QUANT_IMPACT_ROWS 256
+
+static inline uint32_t order_key(float f) {
+  uint32_t b;
+  memcpy(&b, &f, 4);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+static const float* g_sort_keys;
+static int cmp_impact(const void* a, const void* b) {
+  const int64_t i = *(const int64_t*)a, j = *(const int64_t*)b;
+  const uint32_t ki = order_key(g_sort_keys[i]), kj = order_key(g_sort_keys[j]);
+  if (ki != kj) return ki > kj ? -1 : 1;
+  return i < j ? -1 : (i > j);
+}
+
+__attribute__((optimize("fp-contract=off")))
+static float team_sum(const float* v, int G, float* lanes) {
+  const int TL = G / 4 < 32 ? G / 4 : 32, S = G / (4 * TL);
+  for (int l = 0; l < TL; ++l) {
+    float acc = 0.0f;
+    int first = 1;
+    for (int s = 0; s < S; ++s)
+      for (int e = 0; e < 4; ++e) {
+        const float p = v[s * 4 * TL + 4 * l + e];
+        acc = first ? p : acc + p;
+        first = 0;
+      }
+    lanes[l] = acc;
+  }
+  for (int o = TL / 2; o > 0; o >>= 1)
+    for (int l = 0; l < o; ++l) lanes[l] = lanes[l] + lanes[l + o];
+  return lanes[0];
+}
+
+__attribute__((optimize("fp-contract=off")))
+void orc_quantize_2b(const float* W, int64_t ldw, int64_t N, int64_t K, int64_t G, const float* act, int64_t k,
+                     const float* cb, uint8_t* packed, h16* scales, h16* outliers, int64_t* idx) {
+  uint8_t* keep = (uint8_t*)malloc((size_t)K);
+  memset(keep, 1, (size_t)K);
+  if (k > 0) {
+    const int64_t nch = (N + QUANT_IMPACT_ROWS - 1) / QUANT_IMPACT_ROWS;
+    float* imp = (float*)malloc((size_t)K * sizeof(float));
+    #pragma omp parallel for schedule(static)
+    for (int64_t c = 0; c < K; ++c) {
+      float tot = 0.0f;
+      for (int64_t ch = 0; ch < nch; ++ch) {
+        float acc = 0.0f;
+        const int64_t r1 = (ch + 1) * QUANT_IMPACT_ROWS < N ? (ch + 1) * QUANT_IMPACT_ROWS : N;
+        for (int64_t r = ch * QUANT_IMPACT_ROWS; r < r1; ++r) {
+          const float v = W[r * ldw + c];
+          const float p = v * v;
+          acc = acc + p;
+        }
+        tot = ch == 0 ? acc : tot + acc;
+      }
+      float v = sqrtf(tot);
+      if (act) v = v * act[c];
+      imp[c] = v;
+    }
+    int64_t* order = (int64_t*)malloc((size_t)K * sizeof(int64_t));
+    for (int64_t c = 0; c < K; ++c) order[c] = c;
+    g_sort_keys = imp;
+    qsort(order, (size_t)K, sizeof(int64_t), cmp_impact);
+    for (int64_t j = 0; j < k; ++j) {
+      idx[j] = order[j];
+      keep[order[j]] = 0;
+    }
+    for (int64_t n = 0; n < N; ++n)
+      for (int64_t j = 0; j < k; ++j) outliers[n * k + j] = f2h(W[n * ldw + idx[j]]);
+    free(order);
+    free(imp);
+  }
+  const int64_t ng = K / G;
+  #pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < N; ++n) {
+    float w[256], kp[256], t[256], lanes[32];
+    uint8_t q[256];
+    for (int64_t g = 0; g < ng; ++g) {
+      int cnt = 0;
+      for (int64_t i = 0; i < G; ++i) {
+        const int64_t c = g * G + i;
+        kp[i] = keep[c] ? 1.0f : 0.0f;
+        w[i] = keep[c] ? W[n * ldw + c] : 0.0f;
+        cnt += keep[c];
+      }
+      for (int64_t i = 0; i < G; ++i) t[i] = w[i] * w[i];
+      const float ss = team_sum(t, (int)G, lanes);
+      const float nact = cnt > 1 ? (float)cnt : 1.0f;
+      float s = sqrtf(ss / nact + 1e-8f) / 0.95f;
+      s = s > 1e-8f ? s : 1e-8f;
+      for (int it = 0; it < 5; ++it) {
+        const float d = s > 1e-8f ? s : 1e-8f;
+        float cq[256];
+        for (int64_t i = 0; i < G; ++i) {
+          const float z = w[i] / d;
+          float best = fabsf(z - cb[0]);
+          int b = 0;
+          for (int j = 1; j < 4; ++j) {
+            const float dj = fabsf(z - cb[j]);
+            if (dj < best) { best = dj; b = j; }
+          }
+          q[i] = (uint8_t)b;
+          cq[i] = cb[b] * kp[i];
+        }
+        for (int64_t i = 0; i < G; ++i) t[i] = w[i] * cq[i];
+        const float num = team_sum(t, (int)G, lanes);
+        for (int64_t i = 0; i < G; ++i) t[i] = cq[i] * cq[i];
+        const float den = team_sum(t, (int)G, lanes);
+        s = num / (den > 1e-8f ? den : 1e-8f);
+        s = s > 1e-8f ? s : 1e-8f;
+      }
+      for (int64_t i = 0; i < G; i += 4)
+        packed[n * (K / 4) + (g * G + i) / 4] =
+            (uint8_t)(q[i] | (q[i + 1] << 2) | (q[i + 2] << 4) | (q[i + 3] << 6));
+      scales[n * ng + g] = f2h(s);
+    }
+  }
+  free(keep);
+}
+
 /* fp16 <-> fp32 helpers exported for the Python side of the oracle. */
 void orc_h2f(const h16* in, float* out, int64_t n) { for (int64_t i = 0; i < n; ++i) out[i] = h2f(in[i]); }
 void orc_f2h(const float* in, h16* out, int64_t n) { for (int64_t i = 0; i < n; ++i) out[i] = f2h(in[i]); }

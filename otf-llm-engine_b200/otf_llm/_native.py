@@ -106,6 +106,8 @@ EXPORTS = (
     "otf_pos_advance",
     "otf_attn_decode_noalloc",
     "otf_attn_rope_decode",
+    "otf2b_quantize_workspace_bytes",
+    "otf2b_quantize",
 )
 
 
@@ -177,6 +179,11 @@ def lib() -> ctypes.CDLL:
     L.otf_attn_decode_noalloc.restype = i32
     L.otf_attn_rope_decode.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, i64, i64, i64, i64, vp, i64, vp]
     L.otf_attn_rope_decode.restype = i32
+    L.otf2b_quantize_workspace_bytes.argtypes = [i64, i64]
+    L.otf2b_quantize_workspace_bytes.restype = i64
+    L.otf2b_quantize.argtypes = [vp, i32, i64, i64, i64, i64, vp, i64, vp, vp, i64, vp, i64, vp, i64, vp, i64, vp,
+                                 vp]
+    L.otf2b_quantize.restype = i32
     _lib = L
     return L
 
@@ -329,6 +336,53 @@ def unpack_codes(packed: torch.Tensor, K: int) -> torch.Tensor:
         st = lib().otf2b_unpack_codes(_ptr(packed), ldp, N, K, _ptr(codes), K, _stream(packed.device))
     _check(st, "otf2b_unpack_codes")
     return codes
+
+
+_QUANT_DTYPES = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
+
+
+def quantize_2b(W: torch.Tensor, group_size: int, n_outliers: int, act: Optional[torch.Tensor] = None,
+                codebook: Optional[Sequence[float]] = None):
+    """Symmetric 2-bit quantisation of W [N, K] on its GPU (otf2b_quantize).
+
+    Returns (packed uint8 [N, K/4], scales fp16 [N, K/G], outliers fp16 [N, k] or None,
+    outlier indices int64 [k] or None), as Symmetric2BitQuantizer.quantize_tensor does.
+    W may be fp16, bf16 or fp32 (other float types are converted to fp32 first)."""
+    _need_cuda(W, "W")
+    if W.dim() != 2:
+        raise ValueError(f"W must be 2-D, got shape {tuple(W.shape)}")
+    if W.dtype not in _QUANT_DTYPES:
+        W = W.float()
+    N, K = W.shape
+    esize = W.element_size()
+    if W.stride(1) != 1 or (W.stride(0) % 4 if N > 1 else 0) or W.data_ptr() % (4 * esize):
+        W = W.contiguous()
+    ldw = W.stride(0) if N > 1 else K
+    G, k = int(group_size), int(n_outliers)
+    if K % G or K % 4:
+        raise ValueError(f"d_in={K} must be a multiple of group_size={G} and of 4")
+    dev = W.device
+    packed = torch.empty((N, K // 4), dtype=torch.uint8, device=dev)
+    scales = torch.empty((N, K // G), dtype=torch.float16, device=dev)
+    ov = idx = ws = a = None
+    nws = 0
+    if k > 0:
+        ov = torch.empty((N, k), dtype=torch.float16, device=dev)
+        idx = torch.empty(k, dtype=torch.int64, device=dev)
+        nws = int(lib().otf2b_quantize_workspace_bytes(N, K))
+        ws = torch.empty(nws, dtype=torch.uint8, device=dev)
+        if act is not None:
+            a = act.detach().to(device=dev, dtype=torch.float32).contiguous()
+            if a.numel() != K:
+                raise ValueError(f"activation profile has {a.numel()} entries, expected {K}")
+    cb = None
+    if codebook is not None:
+        cb = (ctypes.c_float * 4)(*[float(v) for v in codebook])
+    with torch.cuda.device(dev):
+        st = lib().otf2b_quantize(_ptr(W), _QUANT_DTYPES[W.dtype], ldw, N, K, G, _ptr(a), k, cb, _ptr(ws), nws,
+                                  _ptr(packed), K // 4, _ptr(scales), K // G, _ptr(ov), k, _ptr(idx), _stream(dev))
+    _check(st, "otf2b_quantize")
+    return packed, scales, ov, idx
 
 
 def i8_head(x2d: torch.Tensor, w_i8: torch.Tensor, scales: torch.Tensor,

@@ -129,6 +129,14 @@ class Symmetric2BitQuantizer:
     @torch.no_grad()
     def quantize_tensor(self, W: torch.Tensor, activation_profile: Optional[torch.Tensor] = None,
                         row_chunk: int = 2048):
+        """Quantise W on its device.  CUDA tensors go through one native launch sequence
+        (otf2b_quantize: column impact, anchor ranking, anchor gather, group fit; no [N, K/G, G, 4]
+        temporaries); CPU tensors run the reference's torch ops, row-chunked."""
+        if W.is_cuda:
+            from . import _native
+            k = max(1, int(W.shape[1] * self.outlier_ratio)) if self.outlier_ratio > 0.0 else 0
+            return _native.quantize_2b(W.detach(), self.group_size, k, activation_profile,
+                                       [float(v) for v in self.codebook.tolist()])
         dev = W.device
         Wf = W.detach().to(torch.float32)
         d_out, d_in = Wf.shape
