@@ -185,6 +185,50 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+class GemvLaunches:
+    """One otf2b_linear launch per projection of a stack (its weights, a fixed fp16 input of
+    the projection's width, the o/down residual), captured as one CUDA graph: the 2-bit GEMV
+    kernel's own launch duration over the stack's shapes."""
+
+    def __init__(self, stack):
+        import torch
+        from otf_llm import _native
+        dev = stack.norm_w.device
+        gen = torch.Generator(device=dev).manual_seed(17)
+        self.calls = []
+        keep = []
+        for layer in stack.layers:
+            for name, m in layer.items():
+                x = torch.randn(1, m.d_in, generator=gen, device=dev).half()
+                y = torch.empty(1, m.out_features, dtype=torch.float16, device=dev)
+                r = torch.randn(1, m.out_features, generator=gen, device=dev).half() if name in ("o_proj",
+                                                                                                "down_proj") else None
+                keep += [x, y, r]
+                self.calls.append((m, x, y, r))
+        self._keep = keep
+
+        def run():
+            for m, x, y, r in self.calls:
+                _native.linear_2bit(x, m.packed_uint8, m.scales, m.group_size, m.codebook,
+                                    mask=m.outlier_mask_vector if m.has_outliers else None,
+                                    outlier_idx=m.outlier_indices if m.has_outliers else None,
+                                    outlier_vals=m.outliers_fp16 if m.has_outliers else None,
+                                    bias=m.bias if m.has_bias else None, residual=r, clamp=True, out=y)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            run()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            run()
+        torch.cuda.synchronize(dev)
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+
 def run_b200(args, cfg):
     import torch
     import torch.distributed as dist
@@ -208,8 +252,9 @@ def run_b200(args, cfg):
     stack = Llama2BitLinearStack(cfg, device=dev, seed=1, rank=rank, world=world, process_group=pg,
                                  peer_ar=peer_ar, persistent=args.decode == "persistent")
     graph = DecodeGraph(stack)
-    # The 2-bit projections alone (no norm/SiLU, no all-reduce): per-rank kernel time for the roofline.
-    lin_graph = DecodeGraph(stack, linears_only=True, collectives=False)
+    # The dominant kernel timed on its own: every projection of this rank's stack as one 2-bit
+    # GEMV launch, back to back in a graph (the roofline's per-launch duration).
+    lin_graph = GemvLaunches(stack)
     torch.cuda.synchronize()
 
     bytes_tok_rank = stack.bytes_per_token()
@@ -254,7 +299,7 @@ def run_b200(args, cfg):
         graph.step_host(xh, yh)
     ms_e2e = timed(lambda: graph.step_host(xh, yh), args.steps)
 
-    # Dominant kernel: the 2-bit GEMV launches alone (norm/SiLU removed), same weights.
+    # Dominant kernel: the 2-bit GEMV, one launch per projection over the same weights.
     roofline = None
     if lin_graph is not None:
         for _ in range(2):

@@ -342,33 +342,30 @@ class Llama2BitLinearStack(nn.Module):
             cur = b["h2"]
         return cur
 
-    def forward(self, h: torch.Tensor, linears_only: bool = False, collectives: bool = True) -> torch.Tensor:
-        """One decode step for h [1, hidden] fp16; returns the new residual stream.
-
-        linears_only drops RMSNorm and SiLU (the 2-bit projections alone, for the roofline);
-        collectives=False also drops the tensor-parallel all-reduces (per-rank kernel time)."""
-        if self.mk is not None and not linears_only:
+    def forward(self, h: torch.Tensor) -> torch.Tensor:
+        """One decode step for h [1, hidden] fp16; returns the new residual stream."""
+        if self.mk is not None:
             return self.mk(h)
-        if self.fused and not linears_only:
+        if self.fused:
             return self._forward_fused(h)
         b = self._buf
         cur = h
         for li, layer in enumerate(self.layers):
-            xn = cur if linears_only else _native.rmsnorm(cur, self.in_norms[li], self.cfg.rms_eps, out=b["xn"])
+            xn = _native.rmsnorm(cur, self.in_norms[li], self.cfg.rms_eps, out=b["xn"])
             self._lin(layer["q_proj"], xn, b["q"])
             self._lin(layer["k_proj"], xn, b["k"])
             v = self._lin(layer["v_proj"], xn, b["v"])
             attn = self._attn_passthrough(v, b["attn"])
             tp = self.world > 1
             h1 = self._lin(layer["o_proj"], attn, b["h1"], residual=None if (tp and self.rank) else cur)
-            if tp and collectives:
+            if tp:
                 torch.distributed.all_reduce(h1, group=self.pg)
-            xn = h1 if linears_only else _native.rmsnorm(h1, self.post_norms[li], self.cfg.rms_eps, out=b["xn"])
+            xn = _native.rmsnorm(h1, self.post_norms[li], self.cfg.rms_eps, out=b["xn"])
             g = self._lin(layer["gate_proj"], xn, b["g"])
             u = self._lin(layer["up_proj"], xn, b["u"])
-            a = g if linears_only else _native.silu_mul(g, u, out=b["a"])
+            a = _native.silu_mul(g, u, out=b["a"])
             h2 = self._lin(layer["down_proj"], a, b["h2"], residual=None if (tp and self.rank) else h1)
-            if tp and collectives:
+            if tp:
                 torch.distributed.all_reduce(h2, group=self.pg)
             cur = h2
         return cur
@@ -377,7 +374,7 @@ class Llama2BitLinearStack(nn.Module):
 class DecodeGraph:
     """One decode step of a stack captured as a CUDA graph with static input/output."""
 
-    def __init__(self, stack: Llama2BitLinearStack, linears_only: bool = False, collectives: bool = True):
+    def __init__(self, stack: Llama2BitLinearStack):
         dev = stack.norm_w.device
         self.stack = stack
         self.x = torch.zeros(1, stack.cfg.hidden, dtype=torch.float16, device=dev)
@@ -386,12 +383,12 @@ class DecodeGraph:
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
             for _ in range(2):
-                self.y.copy_(stack(self.x, linears_only, collectives))
+                self.y.copy_(stack(self.x))
         torch.cuda.current_stream(dev).wait_stream(s)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self.y.copy_(stack(self.x, linears_only, collectives))
+            self.y.copy_(stack(self.x))
         torch.cuda.synchronize(dev)
 
     def replay(self) -> None:
