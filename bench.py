@@ -473,31 +473,52 @@ def run_sweep(args):
 
 
 def run_e2e(args):
-    """Greedy batch-1 decode of a random-init Llama-3.2-3B-architecture 2-bit model
-    (28 layers, hidden 3072, intermediate 8192, 24 q / 8 KV heads of 128, RoPE theta 5e5,
-    vocabulary 128256 with a tied INT8 embedding / head): P prompt tokens, then T generated
-    tokens, every token step one CUDA graph of native kernels (otf_llm.decode_model)."""
+    """Greedy batch-1 decode of a random-init 2-bit model, every token step one CUDA graph of
+    native kernels (otf_llm.decode_model): Llama-3.2-3B architecture (28 layers, hidden 3072,
+    intermediate 8192, 24 q / 8 KV heads of 128) or Llama-3-70B (80 layers, hidden 8192,
+    intermediate 28672, 64 q / 8 KV heads), RoPE theta 5e5, vocabulary 128256 with a tied INT8
+    embedding / head.  P prompt tokens, then T generated tokens.  Under torchrun the model is
+    tensor-parallel over the ranks (heads, MLP rows and vocabulary split; o/down exchanged by
+    the fused peer stores or NCCL) and times are the max over ranks."""
     import torch
+    import torch.distributed as dist
     from otf_llm import _native
-    from otf_llm.decode_model import LLAMA32_3B, GreedyDecoder, ModelConfig
-    from otf_llm.decoder_stack import StackConfig, random_quantized_linear
+    from otf_llm.decode_model import LLAMA3_70B, LLAMA32_3B, GreedyDecoder, ModelConfig, shard_layers
+    from otf_llm.decoder_stack import StackConfig, random_quantized_linear, split_bounds
     from otf_llm.symmetric_2bit_engine import QuantizedEmbedding, QuantizedLinearHead
     P, T = args.e2e_prompt, args.e2e_tokens
-    base = LLAMA32_3B
+    base = LLAMA3_70B if args.e2e_model == "llama3-70b" else LLAMA32_3B
+    name = "Llama-3-70B" if base is LLAMA3_70B else "Llama-3.2-3B"
     cfg = ModelConfig(layers=base.layers, hidden=base.hidden, intermediate=base.intermediate, heads=base.heads,
                       kv_heads=base.kv_heads, head_dim=base.head_dim, vocab=base.vocab, rope_theta=base.rope_theta,
                       max_pos=P + T + 8)
-    dev = torch.device("cuda", 0)
+    world = args.gpus
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    qcfg = StackConfig(group_size=64, outlier_ratio=0.005, weight_std=0.02)
+    pg = None
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        pg = dist.group.WORLD
+    peer_ar = None
+    if world > 1 and args.tp_exchange == "peer":
+        from otf_llm.tp_allreduce import PeerAllReduce
+        peer_ar = PeerAllReduce(cfg.hidden, group=pg, device=dev)
+    std = 0.015 if base is LLAMA3_70B else 0.02
+    qcfg = StackConfig(group_size=64, outlier_ratio=0.005, weight_std=std)
     shapes = {"q_proj": (cfg.heads * cfg.head_dim, cfg.hidden), "k_proj": (cfg.kv_heads * cfg.head_dim, cfg.hidden),
               "v_proj": (cfg.kv_heads * cfg.head_dim, cfg.hidden), "o_proj": (cfg.hidden, cfg.heads * cfg.head_dim),
               "gate_proj": (cfg.intermediate, cfg.hidden), "up_proj": (cfg.intermediate, cfg.hidden),
               "down_proj": (cfg.hidden, cfg.intermediate)}
     layers = []
     for li in range(cfg.layers):
-        layers.append({n: random_quantized_linear(N, K, qcfg, 7000 + li * 7 + pi, dev)
-                       for pi, (n, (N, K)) in enumerate(shapes.items())})
+        full = {n: random_quantized_linear(N, K, qcfg, 7000 + li * 7 + pi, dev)
+                for pi, (n, (N, K)) in enumerate(shapes.items())}
+        layers.append(shard_layers([full], cfg, rank, world)[0] if world > 1 else full)
+        del full
+    torch.cuda.synchronize()
     ones = torch.ones(cfg.hidden, dtype=torch.float16, device=dev)
     # tied INT8 embedding / head from W_emb ~ N(0, 0.02^2): row absmax / 127 on the device
     gen = torch.Generator(device=dev).manual_seed(11)
@@ -509,50 +530,74 @@ def run_e2e(args):
         step = w.abs().amax(dim=1, keepdim=True).div(127.0).clamp_min(1e-8)
         w8[lo:hi] = w.div(step).round().clamp(-127, 127).to(torch.int8)
         sc[lo:hi] = step.half()
+    r0, r1 = split_bounds(cfg.vocab, rank, world) if world > 1 else (0, cfg.vocab)
     with torch.device("meta"):
         emb = QuantizedEmbedding(cfg.vocab, cfg.hidden)
-        head = QuantizedLinearHead(cfg.hidden, cfg.vocab)
+        head = QuantizedLinearHead(cfg.hidden, r1 - r0)
     emb.weight_int8, emb.scales = w8, sc
-    head.weight_int8, head.scales = w8, sc
-    dec = GreedyDecoder(cfg, layers, [(ones, ones)] * cfg.layers, emb, head, ones, dev)
+    head.weight_int8, head.scales = w8[r0:r1], sc[r0:r1]
+    dec = GreedyDecoder(cfg, layers, [(ones, ones)] * cfg.layers, emb, head, ones, dev, rank=rank, world=world,
+                        process_group=pg, peer_ar=peer_ar, head_row0=r0)
     dec.capture()
     prompt = torch.randint(0, cfg.vocab, (P,), generator=torch.Generator().manual_seed(5)).to(dev)
     for _ in range(max(1, args.warmup // 2)):
         dec.generate(prompt[:16], 8)
     torch.cuda.synchronize()
     dec.reset()
+    if world > 1:
+        dist.barrier(device_ids=[local])
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-    e0.record()
-    for i in range(P):
-        dec.ids.copy_(prompt[i:i + 1])
-        dec.graph.replay()
-    e1.record()
-    out = torch.empty(T, dtype=torch.int64, device=dev)
-    for i in range(T):
-        out[i:i + 1].copy_(dec.ids)
-        dec.graph.replay()
-    e2.record()
-    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0.record()
+        for i in range(P):
+            dec.ids.copy_(prompt[i:i + 1])
+            dec.graph.replay()
+        e1.record()
+        out = torch.empty(T, dtype=torch.int64, device=dev)
+        for i in range(T):
+            out[i:i + 1].copy_(dec.ids)
+            dec.graph.replay()
+        e2.record()
+        torch.cuda.synchronize()
     t_pre = e0.elapsed_time(e1) / 1e3
     t_dec = e1.elapsed_time(e2) / 1e3
     lin_bytes = sum(m.packed_uint8.numel() + m.scales.shape[0] * m.scales.shape[1] * 2 +
                     (m.outliers_fp16.numel() * 2 + m.outlier_indices.numel() * 8 if m.has_outliers else 0)
                     for l in layers for m in l.values())
-    head_bytes = cfg.vocab * cfg.hidden + cfg.vocab * 2
-    line = {"metric": "decode tokens/s, Llama-3.2-3B architecture 2-bit (random init), batch 1",
-            "value": round(T / t_dec, 1), "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True,
+    head_bytes = (r1 - r0) * cfg.hidden + (r1 - r0) * 2
+    if world > 1:
+        t = torch.tensor([t_pre, t_dec], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_pre, t_dec = float(t[0]), float(t[1])
+    peak, peak_kind = measured_peak()
+    rank_gbs = (lin_bytes + head_bytes) * T / t_dec / 1e9
+    line = {"metric": f"decode tokens/s, {name} architecture 2-bit (random init), batch 1",
+            "value": round(T / t_dec, 1), "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
             "prompt_tokens": P, "new_tokens": T, "ms_per_token": round(t_dec / T * 1e3, 4),
             "prefill_tokens_per_s": round(P / t_pre, 1),
-            "hbm_gbs": round((lin_bytes + head_bytes) * T / t_dec / 1e9, 1),
-            "bytes_per_token": {"linears": lin_bytes, "int8_head": head_bytes,
-                                "kv_cache_at_end": 2 * cfg.layers * (P + T) * cfg.kv_heads * cfg.head_dim * 2},
+            "hbm_gbs_per_gpu": round(rank_gbs, 1), "frac_of_peak_per_gpu": round(rank_gbs / peak, 4),
+            "peak_gbs": peak, "peak_kind": peak_kind,
+            "bytes_per_token_per_gpu": {"linears": lin_bytes, "int8_head": head_bytes,
+                                        "kv_cache_at_end": 2 * cfg.layers * (P + T) * dec.kv_heads * cfg.head_dim * 2},
             "data": "synthetic (random-init weights quantised on device; prompt = seeded uniform ids)",
-            "config": {"workload": "Llama-3.2-3B 2-bit greedy decode", "layers": cfg.layers, "hidden": cfg.hidden,
+            "config": {"workload": f"{name} 2-bit greedy decode", "layers": cfg.layers, "hidden": cfg.hidden,
                        "intermediate": cfg.intermediate, "heads": cfg.heads, "kv_heads": cfg.kv_heads,
-                       "vocab": cfg.vocab, "rope": "default, theta 5e5", "group_size": 64, "outlier_ratio": 0.005},
-            "gpu_launches_per_token": 5 * cfg.layers + 5, "device_error": _native.device_error(),
+                       "vocab": cfg.vocab, "rope": "default, theta 5e5", "group_size": 64, "outlier_ratio": 0.005,
+                       "parallelism": f"tp{world}" if world > 1 else "single",
+                       "tp_exchange": args.tp_exchange if world > 1 else None},
+            "gpu_launches_per_token": 5 * cfg.layers + 5 + (1 if peer_ar is not None else 0),
+            "clocks": clk.summary(), "device_error": _native.device_error(),
             "first_tokens": [int(t) for t in out[:8].cpu()]}
-    print(json.dumps(line), flush=True)
+    dec.graph = None
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local])
+        if peer_ar is not None:
+            peer_ar.close()
+            dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 def run_quantize(args):
@@ -623,6 +668,7 @@ def main():
                     help="tensor-parallel exchange after o/down: fused NVLink peer stores, or NCCL all_reduce")
     ap.add_argument("--sweep", action="store_true", help="batch sweep at Llama-3-70B MLP shapes (JSON lines)")
     ap.add_argument("--e2e", action="store_true", help="greedy decode of a Llama-3.2-3B-architecture 2-bit model")
+    ap.add_argument("--e2e-model", choices=("llama3.2-3b", "llama3-70b"), default="llama3.2-3b")
     ap.add_argument("--e2e-prompt", type=int, default=512)
     ap.add_argument("--e2e-tokens", type=int, default=256)
     ap.add_argument("--quantize", action="store_true", help="GPU quantizer on a Llama-3-70B gate_proj matrix")

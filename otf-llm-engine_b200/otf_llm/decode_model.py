@@ -10,6 +10,13 @@ This is what the reference's runner does for one generated token with HF's
 LlamaForCausalLM around the injected modules (otf_llm/run_symmetric_2bit.py:150-215):
 the projections are SymmetricOTF2BitLinear, the embedding / head QuantizedEmbedding /
 QuantizedLinearHead, attention and norms HF's.  Here every step is a native kernel.
+
+Tensor parallelism (world > 1, one process per GPU): q/k/v/gate/up are column shards (whole
+heads; gate/up cut at down_proj's group boundaries), o/down row shards, so each rank attends
+over its own heads with its own KV cache; the partial sums of o and down are exchanged either
+inside the GEMV launches (peer stores over NVLink, ``peer_ar``) or by NCCL all-reduce; the
+embedding is replicated and the INT8 head vocabulary-parallel, with one (max, index) pair per
+rank exchanged for the greedy pick.  ``shard_layers`` cuts a full model into one rank's part.
 """
 from __future__ import annotations
 
@@ -21,6 +28,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import torch
 
 from . import _native
+from .decoder_stack import shard_linear
 from .symmetric_2bit_engine import QuantizedEmbedding, QuantizedLinearHead, SymmetricOTF2BitLinear
 
 PROJ = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
@@ -44,6 +52,30 @@ LLAMA32_3B = ModelConfig(layers=28, hidden=3072, intermediate=8192, heads=24, kv
                          vocab=128256, rope_theta=500000.0)
 
 
+LLAMA3_70B = ModelConfig(layers=80, hidden=8192, intermediate=28672, heads=64, kv_heads=8, head_dim=128,
+                         vocab=128256, rope_theta=500000.0)
+
+
+def shard_layers(layers: Sequence[Dict[str, SymmetricOTF2BitLinear]], cfg: ModelConfig, rank: int, world: int
+                 ) -> List[Dict[str, SymmetricOTF2BitLinear]]:
+    """Rank ``rank``'s tensor-parallel part of full decoder layers: q/k/v by whole query / KV
+    heads (the head counts must divide by world), gate/up by rows at multiples of down_proj's
+    group size, o/down by input columns at group boundaries (anchors re-based, bias on rank 0)."""
+    if cfg.heads % world or cfg.kv_heads % world:
+        raise ValueError(f"{cfg.heads} query / {cfg.kv_heads} KV heads do not split over {world} ranks")
+    out = []
+    for l in layers:
+        G = l["down_proj"].group_size
+        out.append({"q_proj": shard_linear(l["q_proj"], rank, world, "out", cfg.head_dim),
+                    "k_proj": shard_linear(l["k_proj"], rank, world, "out", cfg.head_dim),
+                    "v_proj": shard_linear(l["v_proj"], rank, world, "out", cfg.head_dim),
+                    "o_proj": shard_linear(l["o_proj"], rank, world, "in"),
+                    "gate_proj": shard_linear(l["gate_proj"], rank, world, "out", G),
+                    "up_proj": shard_linear(l["up_proj"], rank, world, "out", G),
+                    "down_proj": shard_linear(l["down_proj"], rank, world, "in")})
+    return out
+
+
 def rope_table(cfg: ModelConfig, device) -> torch.Tensor:
     """fp16 [max_pos, 2, head_dim]: HF's default rotary cos and sin rows (fp32 angles
     pos * theta^(-2i/d), both halves duplicated, rounded to fp16 as HF casts them)."""
@@ -60,53 +92,130 @@ class GreedyDecoder:
 
     def __init__(self, cfg: ModelConfig, layers: Sequence[Dict[str, SymmetricOTF2BitLinear]],
                  norms: Sequence[Tuple[torch.Tensor, torch.Tensor]], embed: QuantizedEmbedding,
-                 head: QuantizedLinearHead, final_norm: Optional[torch.Tensor], device):
+                 head: QuantizedLinearHead, final_norm: Optional[torch.Tensor], device, *, rank: int = 0,
+                 world: int = 1, process_group=None, peer_ar=None, head_row0: int = 0):
+        """``layers``: this rank's modules (``shard_layers`` under tensor parallelism);
+        ``head``: this rank's rows of the INT8 head, which start at vocabulary row
+        ``head_row0``; ``peer_ar``: an otf_llm.tp_allreduce.PeerAllReduce for the exchange fused
+        into the o/down launches (else NCCL all-reduce over ``process_group``)."""
         dev = torch.device(device)
         self.cfg, self.device = cfg, dev
+        self.rank, self.world, self.pg, self.ar = rank, world, process_group, peer_ar
+        self.head_row0 = int(head_row0)
         self.layers = [dict(l) for l in layers]
         for l in self.layers:
             missing = [n for n in PROJ if n not in l]
             if missing:
                 raise ValueError(f"decoder layer lacks {missing}")
+        l0 = self.layers[0]
+        self.heads = l0["q_proj"].out_features // cfg.head_dim      # this rank's query / KV heads
+        self.kv_heads = l0["k_proj"].out_features // cfg.head_dim
+        if world == 1 and (self.heads, self.kv_heads) != (cfg.heads, cfg.kv_heads):
+            raise ValueError("q/k projections do not match the configured head counts")
+        if peer_ar is not None and world > 1:
+            if not all(_native.tensor_pipe_shape_ok(m) for l in self.layers for m in l.values()):
+                raise ValueError("the fused peer exchange needs every projection on the tensor-pipe GEMV")
         f16 = dict(dtype=torch.float16, device=dev)
         self.in_norms = [a.to(**f16).contiguous() for a, _ in norms]
         self.post_norms = [b.to(**f16).contiguous() for _, b in norms]
         self.embed, self.head = embed, head
         self.final_norm = (final_norm if final_norm is not None else torch.ones(cfg.hidden)).to(**f16).contiguous()
-        qd, kvd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+        qd, kvd = self.heads * cfg.head_dim, self.kv_heads * cfg.head_dim
+        inter = l0["gate_proj"].out_features
         self.kc = [torch.zeros(cfg.max_pos, kvd, **f16) for _ in self.layers]
         self.vc = [torch.zeros(cfg.max_pos, kvd, **f16) for _ in self.layers]
         self.cos_sin = rope_table(cfg, dev)
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.ids = torch.zeros(1, dtype=torch.int64, device=dev)
-        n = _native.lib().otf_attn_workspace_bytes(cfg.kv_heads, cfg.head_dim, cfg.max_pos)
+        n = _native.lib().otf_attn_workspace_bytes(self.kv_heads, cfg.head_dim, cfg.max_pos)
         self.attn_ws = torch.zeros(int(n), dtype=torch.uint8, device=dev)
         self.b = {"h": torch.zeros(1, cfg.hidden, **f16), "h1": torch.zeros(1, cfg.hidden, **f16),
                   "h2": torch.zeros(1, cfg.hidden, **f16), "q": torch.zeros(1, qd, **f16),
                   "k": torch.zeros(1, kvd, **f16), "v": torch.zeros(1, kvd, **f16),
-                  "attn": torch.zeros(1, qd, **f16), "g": torch.zeros(1, cfg.intermediate, **f16),
-                  "u": torch.zeros(1, cfg.intermediate, **f16), "xn": torch.zeros(1, cfg.hidden, **f16)}
-        self.logits = torch.zeros(1, cfg.vocab, dtype=torch.float32, device=dev)
+                  "attn": torch.zeros(1, qd, **f16), "g": torch.zeros(1, inter, **f16),
+                  "u": torch.zeros(1, inter, **f16), "xn": torch.zeros(1, cfg.hidden, **f16)}
+        self.logits = torch.zeros(1, head.weight_int8.shape[0], dtype=torch.float32, device=dev)
+        if world > 1:
+            self.loc_idx = torch.zeros(1, dtype=torch.int64, device=dev)
+            self.pairs = torch.zeros(world, 2, dtype=torch.float64, device=dev)
         self.graph = None
 
     # -- one token step (capturable) ----------------------------------------------------
+    def _attention(self, li: int) -> None:
+        """RoPE, KV-cache write and attention over this rank's heads in one launch."""
+        cfg, b = self.cfg, self.b
+        _native._check(_native.lib().otf_attn_rope_decode(
+            b["q"].data_ptr(), b["k"].data_ptr(), b["v"].data_ptr(), self.cos_sin.data_ptr(), self.pos.data_ptr(),
+            self.kc[li].data_ptr(), self.vc[li].data_ptr(), b["attn"].data_ptr(), 1.0 / math.sqrt(cfg.head_dim),
+            self.heads, self.kv_heads, cfg.head_dim, cfg.max_pos, self.attn_ws.data_ptr(), self.attn_ws.numel(),
+            _native._stream(self.device)), "otf_attn_rope_decode")
+
+    def _layers_tp(self, cur: torch.Tensor) -> torch.Tensor:
+        """The decoder layers under tensor parallelism; returns the reduced residual stream.
+        NCCL: o / down write partial sums (rank 0 adds the residual), all-reduced in place.
+        Peer: o / down store their partials into every rank's receive buffer and the next
+        grouped launch sums them while staging its input (the q or gate item also writes the
+        sum back for the residual path); one standalone finish closes the last layer."""
+        cfg, b, G = self.cfg, self.b, _native.GroupItem
+        lead = self.rank == 0
+        RMS = _native.OTF_XOP_RMSNORM
+        if self.ar is None:
+            for li, layer in enumerate(self.layers):
+                _native.linear_group([G(layer[n], cur, b[o], x_op=RMS, x_aux=self.in_norms[li], eps=cfg.rms_eps)
+                                      for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"))])
+                self._attention(li)
+                _native.linear_group([G(layer["o_proj"], b["attn"], b["h1"], residual=cur if lead else None)])
+                torch.distributed.all_reduce(b["h1"], group=self.pg)
+                _native.linear_group([G(layer[n], b["h1"], b[o], x_op=RMS, x_aux=self.post_norms[li], eps=cfg.rms_eps)
+                                      for n, o in (("gate_proj", "g"), ("up_proj", "u"))])
+                _native.linear_group([G(layer["down_proj"], b["g"], b["h2"], residual=b["h1"] if lead else None,
+                                        x_op=_native.OTF_XOP_SILU_MUL, x_aux=b["u"])])
+                torch.distributed.all_reduce(b["h2"], group=self.pg)
+                cur = b["h2"]
+            return cur
+        ar = self.ar
+        PROD, CONS = _native.OTF_AR_PRODUCE, _native.OTF_AR_CONSUME
+        pending = None
+        for li, layer in enumerate(self.layers):
+            if pending is None:
+                items = [G(layer[n], cur, b[o], x_op=RMS, x_aux=self.in_norms[li], eps=cfg.rms_eps)
+                         for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"))]
+            else:
+                items = [G(layer[n], b["h2"], b[o], x_op=RMS, x_aux=self.in_norms[li], eps=cfg.rms_eps, ar=ar,
+                           ar_mode=CONS, ar_buf=pending, ar_out=b["h2"].view(-1) if n == "q_proj" else None)
+                         for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"))]
+                cur = b["h2"]
+            _native.linear_group(items)
+            self._attention(li)
+            ob = ar.next_buffer()
+            _native.linear_group([G(layer["o_proj"], b["attn"], b["h1"], residual=cur if lead else None, ar=ar,
+                                    ar_mode=PROD, ar_buf=ob)])
+            _native.linear_group([G(layer[n], b["h1"], b[o], x_op=RMS, x_aux=self.post_norms[li], eps=cfg.rms_eps,
+                                    ar=ar, ar_mode=CONS, ar_buf=ob, ar_out=b["h1"].view(-1) if n == "gate_proj" else None)
+                                  for n, o in (("gate_proj", "g"), ("up_proj", "u"))])
+            pending = ar.next_buffer()
+            _native.linear_group([G(layer["down_proj"], b["g"], b["h2"], residual=b["h1"] if lead else None,
+                                    x_op=_native.OTF_XOP_SILU_MUL, x_aux=b["u"], ar=ar, ar_mode=PROD, ar_buf=pending)])
+        ar.finish(b["h2"].view(-1), pending)
+        return b["h2"]
+
     def _step(self) -> None:
         cfg, b, L = self.cfg, self.b, _native.lib()
         G = _native.GroupItem
         st = _native._stream(self.device)
         h = self.embed(self.ids.view(1)).view(1, -1)
         b["h"].copy_(h)
+        if self.world > 1:
+            cur = self._layers_tp(b["h"])
+            xn = _native.rmsnorm(cur, self.final_norm, cfg.rms_eps, out=b["xn"])
+            self._argmax(xn)
+            _native._check(L.otf_pos_advance(self.pos.data_ptr(), st), "otf_pos_advance")
+            return
         cur = b["h"]
-        scale = 1.0 / math.sqrt(cfg.head_dim)
         for li, layer in enumerate(self.layers):
             _native.linear_group([G(layer[n], cur, b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.in_norms[li],
                                     eps=cfg.rms_eps) for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"))])
-            # RoPE, KV-cache write and attention in one launch
-            _native._check(L.otf_attn_rope_decode(b["q"].data_ptr(), b["k"].data_ptr(), b["v"].data_ptr(),
-                                                  self.cos_sin.data_ptr(), self.pos.data_ptr(), self.kc[li].data_ptr(),
-                                                  self.vc[li].data_ptr(), b["attn"].data_ptr(), scale, cfg.heads,
-                                                  cfg.kv_heads, cfg.head_dim, cfg.max_pos, self.attn_ws.data_ptr(),
-                                                  self.attn_ws.numel(), st), "otf_attn_rope_decode")
+            self._attention(li)
             _native.linear_group([G(layer["o_proj"], b["attn"], b["h1"], residual=cur)])
             _native.linear_group([G(layer[n], b["h1"], b[o], x_op=_native.OTF_XOP_RMSNORM, x_aux=self.post_norms[li],
                                     eps=cfg.rms_eps) for n, o in (("gate_proj", "g"), ("up_proj", "u"))])
@@ -119,14 +228,25 @@ class GreedyDecoder:
         _native._check(L.otf_pos_advance(self.pos.data_ptr(), st), "otf_pos_advance")
 
     def _argmax(self, xn: torch.Tensor) -> None:
+        """Greedy id into self.ids: the fused INT8 head + argmax over this rank's rows; under
+        tensor parallelism every rank's (max logit, global row) pair is all-gathered and the
+        first rank holding the maximum wins (rows ascend with rank, so ties go to the lowest
+        vocabulary index, as torch.argmax)."""
         hd = self.head
         w, s = hd.weight_int8, hd.scales.reshape(-1)
         L = _native.lib()
+        dst = self.ids if self.world == 1 else self.loc_idx
         with torch.cuda.device(self.device):
             _native._check(L.otf_i8_head_argmax(xn.data_ptr(), xn.shape[1], w.data_ptr(), w.stride(0), s.data_ptr(),
-                                                self.logits.data_ptr(), self.logits.shape[1], self.ids.data_ptr(), 1,
+                                                self.logits.data_ptr(), self.logits.shape[1], dst.data_ptr(), 1,
                                                 w.shape[0], w.shape[1], _native._stream(self.device)),
                            "otf_i8_head_argmax")
+        if self.world > 1:
+            vmax = self.logits.gather(1, self.loc_idx.view(1, 1)).view(1).to(torch.float64)
+            pair = torch.cat([vmax, (self.loc_idx + self.head_row0).to(torch.float64)]).view(1, 2)
+            torch.distributed.all_gather_into_tensor(self.pairs, pair, group=self.pg)
+            best = torch.argmax(self.pairs[:, 0]).view(1)
+            self.ids.copy_(self.pairs.index_select(0, best)[:, 1].to(torch.int64))
 
     def capture(self) -> None:
         """Record one token step as a CUDA graph (warm-up steps run eagerly first, then the

@@ -167,3 +167,38 @@ def test_llama7b_shards_cover_every_group(world):
     assert all(s % cfg.group_size == 0 for s in sizes) and max(sizes) - min(sizes) <= cfg.group_size
     heads = [split_bounds(cfg.heads * cfg.head_dim, r, world, cfg.head_dim) for r in range(world)]
     assert {hi - lo for lo, hi in heads} == {cfg.heads * cfg.head_dim // world}
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_decoder_shards_split_whole_heads(world):
+    """shard_layers (tensor-parallel GreedyDecoder): q/k/v rows are whole heads, every rank
+    gets heads/world query and kv_heads/world KV heads, gate/up rows line up with down_proj's
+    K slice at group boundaries, and the shards put back together give the full layer."""
+    from otf_llm.decode_model import ModelConfig, shard_layers
+    from otf_llm.symmetric_2bit_engine import Symmetric2BitQuantizer, SymmetricOTF2BitLinear
+    cfg = ModelConfig(layers=1, hidden=256, intermediate=1024, heads=8, kv_heads=8, head_dim=32, vocab=64)
+    g = torch.Generator().manual_seed(0)
+    qz = Symmetric2BitQuantizer(group_size=32, outlier_ratio=0.02)
+    shapes = {"q_proj": (256, 256), "k_proj": (256, 256), "v_proj": (256, 256), "o_proj": (256, 256),
+              "gate_proj": (1024, 256), "up_proj": (1024, 256), "down_proj": (256, 1024)}
+    full = {}
+    for n, (o, i) in shapes.items():
+        p, s, ov, oi = qz.quantize_tensor(torch.randn(o, i, generator=g) * 0.02, torch.randn(i, generator=g).abs())
+        full[n] = SymmetricOTF2BitLinear(p, s, i, 32, ov, oi)
+    parts = [shard_layers([full], cfg, r, world)[0] for r in range(world)]
+    for n in ("q_proj", "k_proj", "v_proj"):
+        rows = [p[n].out_features for p in parts]
+        assert all(r % cfg.head_dim == 0 for r in rows) and sum(rows) == 256
+        assert torch.equal(torch.cat([p[n].packed_uint8 for p in parts]), full[n].packed_uint8)
+    assert [p["q_proj"].out_features // 32 for p in parts] == [8 // world] * world
+    for p in parts:
+        assert p["gate_proj"].out_features == p["down_proj"].d_in == p["up_proj"].out_features
+        assert p["o_proj"].d_in == p["q_proj"].out_features
+    for n in ("o_proj", "down_proj"):
+        assert torch.equal(torch.cat([p[n].packed_uint8 for p in parts], dim=1), full[n].packed_uint8)
+        got = sorted(int(i) + sum(q[n].d_in for q in parts[:r]) for r, p in enumerate(parts) if p[n].has_outliers
+                     for i in p[n].outlier_indices)
+        assert got == sorted(full[n].outlier_indices.tolist())
+    with pytest.raises(ValueError):
+        shard_layers([full], ModelConfig(layers=1, hidden=256, intermediate=1024, heads=8, kv_heads=3,
+                                         head_dim=32, vocab=64), 0, 2)
