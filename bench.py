@@ -536,12 +536,19 @@ def run_e2e(args):
         head = QuantizedLinearHead(cfg.hidden, r1 - r0)
     emb.weight_int8, emb.scales = w8, sc
     head.weight_int8, head.scales = w8[r0:r1], sc[r0:r1]
-    dec = GreedyDecoder(cfg, layers, [(ones, ones)] * cfg.layers, emb, head, ones, dev, rank=rank, world=world,
-                        process_group=pg, peer_ar=peer_ar, head_row0=r0)
+    Bt = args.e2e_batch
+    if Bt > 1:
+        if world > 1:
+            raise SystemExit("--e2e-batch > 1 runs on one GPU")
+        from otf_llm.decode_model import BatchedGreedyDecoder
+        dec = BatchedGreedyDecoder(cfg, layers, [(ones, ones)] * cfg.layers, emb, head, ones, dev, Bt)
+    else:
+        dec = GreedyDecoder(cfg, layers, [(ones, ones)] * cfg.layers, emb, head, ones, dev, rank=rank, world=world,
+                            process_group=pg, peer_ar=peer_ar, head_row0=r0)
     dec.capture()
-    prompt = torch.randint(0, cfg.vocab, (P,), generator=torch.Generator().manual_seed(5)).to(dev)
+    prompt = torch.randint(0, cfg.vocab, (Bt, P), generator=torch.Generator().manual_seed(5)).to(dev)
     for _ in range(max(1, args.warmup // 2)):
-        dec.generate(prompt[:16], 8)
+        dec.generate(prompt[:, :16] if Bt > 1 else prompt[0, :16], 8)
     torch.cuda.synchronize()
     dec.reset()
     if world > 1:
@@ -550,12 +557,12 @@ def run_e2e(args):
     with ClockSampler(local) as clk:
         e0.record()
         for i in range(P):
-            dec.ids.copy_(prompt[i:i + 1])
+            dec.ids.copy_(prompt[:, i])
             dec.graph.replay()
         e1.record()
-        out = torch.empty(T, dtype=torch.int64, device=dev)
+        out = torch.empty(T, Bt, dtype=torch.int64, device=dev)
         for i in range(T):
-            out[i:i + 1].copy_(dec.ids)
+            out[i].copy_(dec.ids)
             dec.graph.replay()
         e2.record()
         torch.cuda.synchronize()
@@ -571,23 +578,24 @@ def run_e2e(args):
         t_pre, t_dec = float(t[0]), float(t[1])
     peak, peak_kind = measured_peak()
     rank_gbs = (lin_bytes + head_bytes) * T / t_dec / 1e9
-    line = {"metric": f"decode tokens/s, {name} architecture 2-bit (random init), batch 1",
-            "value": round(T / t_dec, 1), "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
-            "prompt_tokens": P, "new_tokens": T, "ms_per_token": round(t_dec / T * 1e3, 4),
-            "prefill_tokens_per_s": round(P / t_pre, 1),
+    line = {"metric": f"decode tokens/s, {name} architecture 2-bit (random init), batch {Bt}",
+            "value": round(Bt * T / t_dec, 1), "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
+            "batch": Bt, "prompt_tokens": P, "new_tokens": T, "ms_per_step": round(t_dec / T * 1e3, 4),
+            "prefill_tokens_per_s": round(Bt * P / t_pre, 1),
             "hbm_gbs_per_gpu": round(rank_gbs, 1), "frac_of_peak_per_gpu": round(rank_gbs / peak, 4),
             "peak_gbs": peak, "peak_kind": peak_kind,
             "bytes_per_token_per_gpu": {"linears": lin_bytes, "int8_head": head_bytes,
-                                        "kv_cache_at_end": 2 * cfg.layers * (P + T) * dec.kv_heads * cfg.head_dim * 2},
+                                        "kv_cache_at_end": Bt * 2 * cfg.layers * (P + T) * (cfg.kv_heads // world) *
+                                        cfg.head_dim * 2},
             "data": "synthetic (random-init weights quantised on device; prompt = seeded uniform ids)",
             "config": {"workload": f"{name} 2-bit greedy decode", "layers": cfg.layers, "hidden": cfg.hidden,
                        "intermediate": cfg.intermediate, "heads": cfg.heads, "kv_heads": cfg.kv_heads,
                        "vocab": cfg.vocab, "rope": "default, theta 5e5", "group_size": 64, "outlier_ratio": 0.005,
                        "parallelism": f"tp{world}" if world > 1 else "single",
                        "tp_exchange": args.tp_exchange if world > 1 else None},
-            "gpu_launches_per_token": 5 * cfg.layers + 5 + (1 if peer_ar is not None else 0),
+            "gpu_launches_per_step": (11 * cfg.layers + 4) if Bt > 1 else (5 * cfg.layers + 5 + (1 if peer_ar is not None else 0)),
             "clocks": clk.summary(), "device_error": _native.device_error(),
-            "first_tokens": [int(t) for t in out[:8].cpu()]}
+            "first_tokens": [int(t) for t in out[:8, 0].cpu()]}
     dec.graph = None
     if world > 1:
         torch.cuda.synchronize()
@@ -670,6 +678,7 @@ def main():
     ap.add_argument("--e2e", action="store_true", help="greedy decode of a Llama-3.2-3B-architecture 2-bit model")
     ap.add_argument("--e2e-model", choices=("llama3.2-3b", "llama3-70b"), default="llama3.2-3b")
     ap.add_argument("--e2e-prompt", type=int, default=512)
+    ap.add_argument("--e2e-batch", type=int, default=1, help="sequences decoded in lockstep (one GPU)")
     ap.add_argument("--e2e-tokens", type=int, default=256)
     ap.add_argument("--quantize", action="store_true", help="GPU quantizer on a Llama-3-70B gate_proj matrix")
     args = ap.parse_args()

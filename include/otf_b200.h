@@ -376,6 +376,21 @@ OTF_API int otf_attn_rope_decode(const void* q, const void* k, const void* v, co
                                  int64_t workspace_bytes, void* stream);
 
 /*
+ * otf_attn_rope_decode for `batch` independent sequences in one launch (batched greedy decoding):
+ * sequence b reads q + b*ldq, k + b*ldkv, v + b*ldkv, position pos[b], its caches at
+ * k_cache/v_cache + b*cache_stride elements (cache_stride >= max_pos * kv_heads * head_dim), and
+ * writes out + b*ldo.  workspace: caller-owned, zeroed once, otf_attn_workspace_bytes_batch(...).
+ * otf_pos_advance_batch: pos[i] += 1 for i < n.
+ */
+OTF_API int64_t otf_attn_workspace_bytes_batch(int64_t kv_heads, int64_t head_dim, int64_t max_pos, int64_t batch);
+OTF_API int otf_attn_rope_decode_batch(const void* q, int64_t ldq, const void* k, const void* v, int64_t ldkv,
+                                       const void* cos_sin, const int32_t* pos, void* k_cache, void* v_cache,
+                                       int64_t cache_stride, void* out, int64_t ldo, float scale, int64_t heads,
+                                       int64_t kv_heads, int64_t head_dim, int64_t max_pos, int64_t batch,
+                                       void* workspace, int64_t workspace_bytes, void* stream);
+OTF_API int otf_pos_advance_batch(int32_t* pos, int64_t n, void* stream);
+
+/*
  * otf_attn_decode without a workspace argument, for callers that cannot allocate device
  * memory (a plugin host that passes only the op's own tensors, an allocator frozen after
  * warm-up, code that must not call cudaMalloc).  No counterpart in the reference.

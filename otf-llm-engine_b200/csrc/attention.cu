@@ -207,14 +207,29 @@ __device__ __forceinline__ void rope_lane(const uint16_t* x, const uint16_t* cs,
   }
 }
 
+// Batched form: blockIdx.z is the sequence; each has its own q/k/v rows (row strides ldq /
+// ldkv), caches (cache_stride elements apart), position pos[b], output row and workspace slice.
 template <int D>
 __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
     const uint16_t* q, const uint16_t* knew, const uint16_t* vnew, const uint16_t* cos_sin, const int* pos,
     uint16_t* kc, uint16_t* vc, uint16_t* out, float scale, int heads, int kv_heads, int max_pos, float* ws,
-    unsigned* tickets, int max_split) {
+    unsigned* tickets, int max_split, int64_t ldq, int64_t ldkv, int64_t cache_stride, int64_t ldo,
+    int64_t ws_stride) {
   constexpr int PL = D / 32;
   pdl_trigger();
   pdl_wait();
+  {
+    const int b = blockIdx.z;
+    q += b * ldq;
+    knew += b * ldkv;
+    vnew += b * ldkv;
+    kc += b * cache_stride;
+    vc += b * cache_stride;
+    out += b * ldo;
+    ws += b * ws_stride;
+    tickets += b * kv_heads;
+    pos += b;
+  }
   const int p = *pos;
   if (p < 0 || p >= max_pos) return;  // the host sized the cache; out of range writes nothing
   const int rep = heads / kv_heads;
@@ -347,10 +362,10 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
   if (threadIdx.x == 0) tickets[g] = 0u;  // re-armed for the next call
 }
 
-__global__ void k_pos_advance(int* pos) {
+__global__ void k_pos_advance(int* pos, int n) {
   pdl_trigger();
   pdl_wait();
-  if (threadIdx.x == 0 && blockIdx.x == 0) *pos += 1;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) pos[i] += 1;
 }
 
 }  // namespace otf
@@ -434,13 +449,63 @@ extern "C" OTF_API int otf_attn_rope_decode(const void* q, const void* k, const 
   auto* kc = static_cast<uint16_t*>(k_cache);
   auto* vc = static_cast<uint16_t*>(v_cache);
   auto* o = static_cast<uint16_t*>(out);
+  const int64_t z = 0;
   cudaError_t e = head_dim == 128
                       ? otf::launch_pdl(otf::k_attn_rope_decode<128>, grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
                                         vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
-                                        tickets, max_split)
+                                        tickets, max_split, z, z, z, z, z)
                       : otf::launch_pdl(otf::k_attn_rope_decode<64>, grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
                                         vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
-                                        tickets, max_split);
+                                        tickets, max_split, z, z, z, z, z);
+  return set_cuda_error(e);
+}
+
+extern "C" OTF_API int64_t otf_attn_workspace_bytes_batch(int64_t kv_heads, int64_t head_dim, int64_t max_pos,
+                                                          int64_t batch) {
+  if (kv_heads <= 0 || head_dim <= 0 || max_pos <= 0 || batch <= 0) return -1;
+  const int64_t max_split = (max_pos + otf::kAttnSplitPos - 1) / otf::kAttnSplitPos;
+  return otf::align_up(batch * kv_heads * 4, 256) +
+         batch * kv_heads * max_split * otf::kAttnMaxRep * (head_dim + 2) * 4;
+}
+
+extern "C" OTF_API int otf_attn_rope_decode_batch(const void* q, int64_t ldq, const void* k, const void* v,
+                                                  int64_t ldkv, const void* cos_sin, const int32_t* pos,
+                                                  void* k_cache, void* v_cache, int64_t cache_stride, void* out,
+                                                  int64_t ldo, float scale, int64_t heads, int64_t kv_heads,
+                                                  int64_t head_dim, int64_t max_pos, int64_t batch, void* workspace,
+                                                  int64_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !cos_sin || !pos || !k_cache || !v_cache || !out || !workspace) return OTF_ERR_INVALID;
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || heads / kv_heads > otf::kAttnMaxRep || max_pos <= 0)
+    return OTF_ERR_INVALID;
+  if (batch <= 0 || batch > 65535) return OTF_ERR_INVALID;
+  if (head_dim != 64 && head_dim != 128) return OTF_ERR_UNSUPPORTED;
+  if (ldq < heads * head_dim || ldo < heads * head_dim || ldkv < kv_heads * head_dim ||
+      cache_stride < max_pos * kv_heads * head_dim)
+    return OTF_ERR_INVALID;
+  if (workspace_bytes < otf_attn_workspace_bytes_batch(kv_heads, head_dim, max_pos, batch)) return OTF_ERR_INVALID;
+  int st = check_device();
+  if (st != OTF_OK) return st;
+  const int max_split = (int)((max_pos + otf::kAttnSplitPos - 1) / otf::kAttnSplitPos);
+  unsigned* tickets = static_cast<unsigned*>(workspace);
+  float* ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + otf::align_up(batch * kv_heads * 4, 256));
+  const int64_t ws_stride = kv_heads * max_split * otf::kAttnMaxRep * (head_dim + 2);
+  const dim3 grid((unsigned)kv_heads, (unsigned)max_split, (unsigned)batch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto* qq = static_cast<const uint16_t*>(q);
+  const auto* kn = static_cast<const uint16_t*>(k);
+  const auto* vn = static_cast<const uint16_t*>(v);
+  const auto* cs = static_cast<const uint16_t*>(cos_sin);
+  const int* pp = reinterpret_cast<const int*>(pos);
+  auto* kc = static_cast<uint16_t*>(k_cache);
+  auto* vc = static_cast<uint16_t*>(v_cache);
+  auto* o = static_cast<uint16_t*>(out);
+  cudaError_t e = head_dim == 128
+                      ? otf::launch_pdl(otf::k_attn_rope_decode<128>, grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
+                                        vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
+                                        tickets, max_split, ldq, ldkv, cache_stride, ldo, ws_stride)
+                      : otf::launch_pdl(otf::k_attn_rope_decode<64>, grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
+                                        vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
+                                        tickets, max_split, ldq, ldkv, cache_stride, ldo, ws_stride);
   return set_cuda_error(e);
 }
 
@@ -449,7 +514,16 @@ extern "C" OTF_API int otf_pos_advance(int32_t* pos, void* stream) {
   int st = check_device();
   if (st != OTF_OK) return st;
   return set_cuda_error(otf::launch_pdl(otf::k_pos_advance, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), 1u,
-                                        reinterpret_cast<int*>(pos)));
+                                        reinterpret_cast<int*>(pos), 1));
+}
+
+extern "C" OTF_API int otf_pos_advance_batch(int32_t* pos, int64_t n, void* stream) {
+  if (!pos || n <= 0 || n > (1 << 20)) return OTF_ERR_INVALID;
+  int st = check_device();
+  if (st != OTF_OK) return st;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148);
+  return set_cuda_error(otf::launch_pdl(otf::k_pos_advance, dim3(blocks), dim3(256), 0,
+                                        static_cast<cudaStream_t>(stream), 1u, reinterpret_cast<int*>(pos), (int)n));
 }
 
 // ---------------------------------------------------------------------------------------

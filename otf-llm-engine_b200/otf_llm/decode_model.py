@@ -291,3 +291,126 @@ class GreedyDecoder:
                 if logits_out is not None:
                     logits_out.append(self.logits.clone())
         return out
+
+
+class BatchedGreedyDecoder:
+    """Greedy decoding of ``batch`` independent sequences in lockstep on one GPU: one token step
+    moves every sequence by one position.  Per layer: RMSNorm, q/k/v, batched RoPE + KV-cache
+    write + attention (each sequence its own caches and position), o + residual, RMSNorm,
+    gate/up, SiLU gate, down + residual; the 2-bit projections run with M = batch rows (the
+    batched integer-MMA kernel up to 8 rows per weight pass, the tcgen05 GEMM from 32).  The
+    reference has no batched decoder; HF's generate with a padded batch does the same math."""
+
+    def __init__(self, cfg: ModelConfig, layers: Sequence[Dict[str, SymmetricOTF2BitLinear]],
+                 norms: Sequence[Tuple[torch.Tensor, torch.Tensor]], embed: QuantizedEmbedding,
+                 head: QuantizedLinearHead, final_norm: Optional[torch.Tensor], device, batch: int):
+        dev = torch.device(device)
+        B = int(batch)
+        if B < 1:
+            raise ValueError("batch must be >= 1")
+        self.cfg, self.device, self.batch = cfg, dev, B
+        self.layers = [dict(l) for l in layers]
+        for l in self.layers:
+            missing = [n for n in PROJ if n not in l]
+            if missing:
+                raise ValueError(f"decoder layer lacks {missing}")
+        f16 = dict(dtype=torch.float16, device=dev)
+        self.in_norms = [a.to(**f16).contiguous() for a, _ in norms]
+        self.post_norms = [b.to(**f16).contiguous() for _, b in norms]
+        self.embed, self.head = embed, head
+        self.final_norm = (final_norm if final_norm is not None else torch.ones(cfg.hidden)).to(**f16).contiguous()
+        qd, kvd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+        self.kc = [torch.zeros(B, cfg.max_pos, kvd, **f16) for _ in self.layers]
+        self.vc = [torch.zeros(B, cfg.max_pos, kvd, **f16) for _ in self.layers]
+        self.cos_sin = rope_table(cfg, dev)
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.ids = torch.zeros(B, dtype=torch.int64, device=dev)
+        n = _native.lib().otf_attn_workspace_bytes_batch(cfg.kv_heads, cfg.head_dim, cfg.max_pos, B)
+        self.attn_ws = torch.zeros(int(n), dtype=torch.uint8, device=dev)
+        inter = self.layers[0]["gate_proj"].out_features
+        self.b = {n_: torch.zeros(B, w, **f16) for n_, w in (("h", cfg.hidden), ("h1", cfg.hidden), ("xn", cfg.hidden),
+                                                               ("q", qd), ("k", kvd), ("v", kvd), ("attn", qd),
+                                                               ("g", inter), ("u", inter), ("a", inter))}
+        self.logits = torch.zeros(B, head.weight_int8.shape[0], dtype=torch.float32, device=dev)
+        self.graph = None
+
+    @staticmethod
+    def _lin(m: SymmetricOTF2BitLinear, x: torch.Tensor, out: torch.Tensor, residual=None) -> None:
+        _native.linear_2bit(x, m.packed_uint8, m.scales, m.group_size, m.codebook,
+                            mask=m.outlier_mask_vector if m.has_outliers else None,
+                            outlier_idx=m.outlier_indices if m.has_outliers else None,
+                            outlier_vals=m.outliers_fp16 if m.has_outliers else None,
+                            bias=m.bias if m.has_bias else None, residual=residual, clamp=True, out=out)
+
+    def _step(self) -> None:
+        cfg, b, L, B = self.cfg, self.b, _native.lib(), self.batch
+        st = _native._stream(self.device)
+        b["h"].copy_(self.embed(self.ids).view(B, -1))
+        kvd = cfg.kv_heads * cfg.head_dim
+        for li, layer in enumerate(self.layers):
+            _native.rmsnorm(b["h"], self.in_norms[li], cfg.rms_eps, out=b["xn"])
+            for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v")):
+                self._lin(layer[n], b["xn"], b[o])
+            _native._check(L.otf_attn_rope_decode_batch(
+                b["q"].data_ptr(), b["q"].stride(0), b["k"].data_ptr(), b["v"].data_ptr(), b["k"].stride(0),
+                self.cos_sin.data_ptr(), self.pos.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
+                cfg.max_pos * kvd, b["attn"].data_ptr(), b["attn"].stride(0), 1.0 / math.sqrt(cfg.head_dim), cfg.heads,
+                cfg.kv_heads, cfg.head_dim, cfg.max_pos, B, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
+                "otf_attn_rope_decode_batch")
+            self._lin(layer["o_proj"], b["attn"], b["h1"], residual=b["h"])
+            _native.rmsnorm(b["h1"], self.post_norms[li], cfg.rms_eps, out=b["xn"])
+            self._lin(layer["gate_proj"], b["xn"], b["g"])
+            self._lin(layer["up_proj"], b["xn"], b["u"])
+            _native.silu_mul(b["g"], b["u"], out=b["a"])
+            self._lin(layer["down_proj"], b["a"], b["h"], residual=b["h1"])
+        _native.rmsnorm(b["h"], self.final_norm, cfg.rms_eps, out=b["xn"])
+        w, s = self.head.weight_int8, self.head.scales.reshape(-1)
+        _native._check(L.otf_i8_head_argmax(b["xn"].data_ptr(), b["xn"].stride(0), w.data_ptr(), w.stride(0),
+                                            s.data_ptr(), self.logits.data_ptr(), self.logits.shape[1],
+                                            self.ids.data_ptr(), B, w.shape[0], w.shape[1], st), "otf_i8_head_argmax")
+        _native._check(L.otf_pos_advance_batch(self.pos.data_ptr(), B, st), "otf_pos_advance_batch")
+
+    def capture(self) -> None:
+        """Record one token step (all sequences) as a CUDA graph; positions reset afterwards."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+        self.reset()
+
+    def reset(self) -> None:
+        self.pos.zero_()
+        torch.cuda.synchronize(self.device)
+
+    def step(self) -> None:
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._step()
+
+    def generate(self, prompts: torch.Tensor, new_tokens: int, logits_out: Optional[List[torch.Tensor]] = None
+                 ) -> torch.Tensor:
+        """Greedy continuation of prompts (int64 [batch, P] on the device, equal lengths) by
+        new_tokens tokens per sequence; returns int64 [batch, new_tokens]."""
+        if prompts.dim() != 2 or prompts.shape[0] != self.batch:
+            raise ValueError(f"prompts must be [{self.batch}, P]")
+        self.reset()
+        out = torch.empty(self.batch, new_tokens, dtype=torch.int64, device=self.device)
+        for i in range(prompts.shape[1]):
+            self.ids.copy_(prompts[:, i])
+            self.step()
+            if logits_out is not None:
+                logits_out.append(self.logits.clone())
+        for i in range(new_tokens):
+            out[:, i].copy_(self.ids)
+            if i + 1 < new_tokens:
+                self.step()
+                if logits_out is not None:
+                    logits_out.append(self.logits.clone())
+        return out
