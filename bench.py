@@ -489,9 +489,9 @@ def run_e2e(args):
     P, T = args.e2e_prompt, args.e2e_tokens
     base = LLAMA3_70B if args.e2e_model == "llama3-70b" else LLAMA32_3B
     name = "Llama-3-70B" if base is LLAMA3_70B else "Llama-3.2-3B"
-    cfg = ModelConfig(layers=base.layers, hidden=base.hidden, intermediate=base.intermediate, heads=base.heads,
-                      kv_heads=base.kv_heads, head_dim=base.head_dim, vocab=base.vocab, rope_theta=base.rope_theta,
-                      max_pos=P + T + 8)
+    cfg = ModelConfig(layers=args.e2e_layers or base.layers, hidden=base.hidden, intermediate=base.intermediate,
+                      heads=base.heads, kv_heads=base.kv_heads, head_dim=base.head_dim, vocab=base.vocab,
+                      rope_theta=base.rope_theta, max_pos=P + T + 8)
     world = args.gpus
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -679,6 +679,8 @@ def main():
     ap.add_argument("--e2e-model", choices=("llama3.2-3b", "llama3-70b"), default="llama3.2-3b")
     ap.add_argument("--e2e-prompt", type=int, default=512)
     ap.add_argument("--e2e-batch", type=int, default=1, help="sequences decoded in lockstep (one GPU)")
+    ap.add_argument("--e2e-layers", type=int, default=0,
+                    help="decoder layers of the e2e model (default: the architecture's; fewer for a profiling case)")
     ap.add_argument("--e2e-tokens", type=int, default=256)
     ap.add_argument("--quantize", action="store_true", help="GPU quantizer on a Llama-3-70B gate_proj matrix")
     args = ap.parse_args()
