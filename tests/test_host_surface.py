@@ -97,3 +97,37 @@ def test_pack_matches_reference_packing():
     w32 = torch.from_numpy(gd["packed"]).view(torch.int32).numpy().astype(np.int64) & 0xFFFFFFFF
     k = np.arange(gd["codes"].shape[1])
     assert np.array_equal((w32[:, k // 16] >> (2 * (k % 16))) & 3, gd["codes"])
+
+
+def test_gpu_quantizer_refuses_cpu_tensors():
+    """The native quantizer entry point has no CPU path (the module-level quantize_tensor keeps
+    the reference's torch ops for CPU tensors, checked against the fixtures above)."""
+    from otf_llm import _native
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _native.quantize_2b(torch.zeros(8, 64), 32, 1)
+
+
+def test_quantize_abi_rejects_bad_arguments():
+    """otf2b_quantize validates sizes, group sizes, strides and outlier counts before touching
+    the device (no GPU needed for these checks)."""
+    import ctypes
+
+    from otf_llm import _native
+    L = _native.lib()
+    i64 = ctypes.c_int64
+    nul = None
+    OTF_ERR_INVALID, OTF_ERR_UNSUPPORTED = 1, 2
+
+    def call(w, dtype, ldw, N, K, G, k, packed, ldp, scales, lds, ov=None, ldo=0, idx=None, ws=None, nws=0):
+        return L.otf2b_quantize(w, dtype, ldw, N, K, G, nul, k, nul, ws, nws, packed, ldp, scales, lds, ov, ldo, idx,
+                                nul)
+
+    fake = ctypes.c_void_p(1 << 20)   # never dereferenced: every case fails validation first
+    assert call(nul, 0, 64, 8, 64, 32, 0, fake, 16, fake, 2) == OTF_ERR_INVALID          # no weights
+    assert call(fake, 0, 64, 8, 64, 48, 0, fake, 16, fake, 2) == OTF_ERR_UNSUPPORTED     # group size 48
+    assert call(fake, 0, 64, 8, 96, 64, 0, fake, 24, fake, 2) == OTF_ERR_INVALID         # K % G
+    assert call(fake, 0, 62, 8, 64, 32, 0, fake, 16, fake, 2) == OTF_ERR_INVALID         # ldw < K
+    assert call(fake, 7, 64, 8, 64, 32, 0, fake, 16, fake, 2) == OTF_ERR_INVALID         # dtype
+    assert call(fake, 0, 64, 8, 64, 32, 65, fake, 16, fake, 2) == OTF_ERR_INVALID        # k > K
+    assert call(fake, 0, 64, 8, 64, 32, 2, fake, 16, fake, 2) == OTF_ERR_INVALID         # anchors, no buffers
+    assert L.otf2b_quantize_workspace_bytes(300, 1024) == (2 * 1024 * 4) + 1024 * 4 + 256   # 2 row chunks
