@@ -376,7 +376,8 @@ OTF_API int otf_attn_rope_decode(const void* q, const void* k, const void* v, co
                                  int64_t workspace_bytes, void* stream);
 
 /*
- * otf_attn_rope_decode for `batch` independent sequences in one launch (batched greedy decoding):
+ * otf_attn_rope_decode for `batch` independent sequences in one launch (batched greedy decoding;
+ * no counterpart in the reference, whose runner decodes one sequence with HF attention):
  * sequence b reads q + b*ldq, k + b*ldkv, v + b*ldkv, position pos[b], its caches at
  * k_cache/v_cache + b*cache_stride elements (cache_stride >= max_pos * kv_heads * head_dim), and
  * writes out + b*ldo.  workspace: caller-owned, zeroed once, otf_attn_workspace_bytes_batch(...).
