@@ -121,8 +121,10 @@ class OTF2BitLinear(nn.Module):
                 raise ValueError("outlier_indices must lie in [0, d_in)")
             self.register_buffer("outliers_fp16", outliers_fp16.to(dtype=torch.float16))
             self.register_buffer("outlier_indices", idx)
-            keep = torch.ones(d_in, dtype=torch.float16)
-            keep[idx.cpu()] = 0.0
+            # on the packed codes' device (the reference builds it on the CPU), so a module made
+            # from CUDA tensors runs without a .to()
+            keep = torch.ones(d_in, dtype=torch.float16, device=packed_uint8.device)
+            keep[idx.to(keep.device)] = 0.0
             self.register_buffer("outlier_mask_vector", keep)
             self.has_outliers = True
         else:
