@@ -332,32 +332,77 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
       ll += sm_l[w][r] * c;
       aa += sm_acc[w][r][dd] * c;
     }
+    if (nsplit == 1) {              // the whole cache in this CTA: no partials, no merge
+      out[(int64_t)(g * rep + r) * D + dd] = f2h(aa / ll);
+      continue;
+    }
     part[r * (D + 2) + 2 + dd] = aa;
     if (dd == 0) {
       part[r * (D + 2)] = mm;
       part[r * (D + 2) + 1] = ll;
     }
   }
+  if (nsplit == 1) return;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = (atomicAdd(tickets + g, 1u) == (unsigned)nsplit - 1u) ? 1u : 0u;
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  for (int e = threadIdx.x; e < rep * D; e += kAttn2Threads) {
-    const int r = e / D, dd = e - r * D;
-    const float* pb = ws + (int64_t)g * max_split * kAttnMaxRep * (D + 2) + r * (D + 2);
-    float mm = -INFINITY;
-    for (int s2 = 0; s2 < nsplit; ++s2) mm = fmaxf(mm, __ldcg(pb + (int64_t)s2 * kAttnMaxRep * (D + 2)));
-    float ll = 0.0f, aa = 0.0f;
-    for (int s2 = 0; s2 < nsplit; ++s2) {
-      const float* ps = pb + (int64_t)s2 * kAttnMaxRep * (D + 2);
-      const float ms = __ldcg(ps);
-      const float c = ms == -INFINITY ? 0.0f : __expf(ms - mm);
-      ll += __ldcg(ps + 1) * c;
-      aa += __ldcg(ps + 2 + dd) * c;
+  const float* pbase = ws + (int64_t)g * max_split * kAttnMaxRep * (D + 2);
+  constexpr int kSmFloats = kAttn2Warps * kAttnMaxRep * D;
+  if (2 * nsplit * rep + 2 * rep <= kSmFloats) {
+    // The split maxima and sums of every head, loaded in parallel into shared memory (sm_acc
+    // is free now); one thread per head forms the weights exp(m_s - max) and the total sum in
+    // split order; every output element then loads its splits' partial sums together.
+    float* pm = &sm_acc[0][0][0];   // [nsplit][rep]: maxima, then weights
+    float* pl = pm + nsplit * rep;  // [nsplit][rep]: sums
+    float* hl = pl + nsplit * rep;  // [rep]: total sum per head
+    for (int i = threadIdx.x; i < nsplit * rep; i += kAttn2Threads) {
+      const int s2 = i / rep, r = i - s2 * rep;
+      const float* ps = pbase + ((int64_t)s2 * kAttnMaxRep + r) * (D + 2);
+      pm[i] = __ldcg(ps);
+      pl[i] = __ldcg(ps + 1);
     }
-    out[(int64_t)(g * rep + r) * D + dd] = f2h(aa / ll);
+    __syncthreads();
+    if (threadIdx.x < rep) {
+      const int r = threadIdx.x;
+      float mm = -INFINITY;
+      for (int s2 = 0; s2 < nsplit; ++s2) mm = fmaxf(mm, pm[s2 * rep + r]);
+      float ll = 0.0f;
+      for (int s2 = 0; s2 < nsplit; ++s2) {
+        const float ms = pm[s2 * rep + r];
+        const float c = ms == -INFINITY ? 0.0f : __expf(ms - mm);
+        ll += pl[s2 * rep + r] * c;
+        pm[s2 * rep + r] = c;
+      }
+      hl[r] = ll;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < rep * D; e += kAttn2Threads) {
+      const int r = e / D, dd = e - r * D;
+      const float* pe = pbase + (int64_t)r * (D + 2) + 2 + dd;
+      float aa = 0.0f;
+#pragma unroll 8
+      for (int s2 = 0; s2 < nsplit; ++s2) aa += __ldcg(pe + (int64_t)s2 * kAttnMaxRep * (D + 2)) * pm[s2 * rep + r];
+      out[(int64_t)(g * rep + r) * D + dd] = f2h(aa / hl[r]);
+    }
+  } else {
+    for (int e = threadIdx.x; e < rep * D; e += kAttn2Threads) {
+      const int r = e / D, dd = e - r * D;
+      const float* pb = pbase + r * (D + 2);
+      float mm = -INFINITY;
+      for (int s2 = 0; s2 < nsplit; ++s2) mm = fmaxf(mm, __ldcg(pb + (int64_t)s2 * kAttnMaxRep * (D + 2)));
+      float ll = 0.0f, aa = 0.0f;
+      for (int s2 = 0; s2 < nsplit; ++s2) {
+        const float* ps = pb + (int64_t)s2 * kAttnMaxRep * (D + 2);
+        const float ms = __ldcg(ps);
+        const float c = ms == -INFINITY ? 0.0f : __expf(ms - mm);
+        ll += __ldcg(ps + 1) * c;
+        aa += __ldcg(ps + 2 + dd) * c;
+      }
+      out[(int64_t)(g * rep + r) * D + dd] = f2h(aa / ll);
+    }
   }
   if (threadIdx.x == 0) tickets[g] = 0u;  // re-armed for the next call
 }
