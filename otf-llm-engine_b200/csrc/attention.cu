@@ -209,7 +209,9 @@ __device__ __forceinline__ void rope_lane(const uint16_t* x, const uint16_t* cs,
 
 // Batched form: blockIdx.z is the sequence; each has its own q/k/v rows (row strides ldq /
 // ldkv), caches (cache_stride elements apart), position pos[b], output row and workspace slice.
-template <int D>
+// REP > 0: the query heads per KV head fixed at compile time (the head loops unroll without
+// early exits, so the heads' reductions interleave); REP = 0: any ratio up to kAttnMaxRep.
+template <int D, int REP>
 __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
     const uint16_t* q, const uint16_t* knew, const uint16_t* vnew, const uint16_t* cos_sin, const int* pos,
     uint16_t* kc, uint16_t* vc, uint16_t* out, float scale, int heads, int kv_heads, int max_pos, float* ws,
@@ -232,7 +234,7 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
   }
   const int p = *pos;
   if (p < 0 || p >= max_pos) return;  // the host sized the cache; out of range writes nothing
-  const int rep = heads / kv_heads;
+  const int rep = REP > 0 ? REP : heads / kv_heads;
   const int g = blockIdx.x, sp = blockIdx.y;
   const int L = p + 1;
   const int nsplit = min((L + kAttnSplitPos - 1) / kAttnSplitPos, max_split);
@@ -294,8 +296,8 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
     for (int j = 0; j < kAttn2Batch; ++j) {
       if (base + j * kAttn2Warps >= p1) break;
 #pragma unroll
-      for (int r = 0; r < kAttnMaxRep; ++r) {
-        if (r >= rep) break;
+      for (int r = 0; r < (REP > 0 ? REP : kAttnMaxRep); ++r) {
+        if (REP == 0 && r >= rep) break;
         float d = 0.0f;
 #pragma unroll
         for (int i = 0; i < PL; ++i) d = fmaf(qv[r][i], kf[j][i], d);
@@ -311,8 +313,8 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
     }
   }
 #pragma unroll
-  for (int r = 0; r < kAttnMaxRep; ++r) {
-    if (r >= rep) break;
+  for (int r = 0; r < (REP > 0 ? REP : kAttnMaxRep); ++r) {
+    if (REP == 0 && r >= rep) break;
     if (lane == 0) {
       sm_m[warp][r] = m[r];
       sm_l[warp][r] = l[r];
@@ -415,6 +417,21 @@ __global__ void k_pos_advance(int* pos, int n) {
 
 }  // namespace otf
 
+namespace otf {
+// The fused attention kernel for a query-per-KV-head ratio (compile-time for the common ones).
+template <int D>
+static decltype(&k_attn_rope_decode<D, 0>) attn2_kernel(int64_t rep) {
+  switch (rep) {
+    case 1: return k_attn_rope_decode<D, 1>;
+    case 2: return k_attn_rope_decode<D, 2>;
+    case 3: return k_attn_rope_decode<D, 3>;
+    case 4: return k_attn_rope_decode<D, 4>;
+    case 8: return k_attn_rope_decode<D, 8>;
+    default: return k_attn_rope_decode<D, 0>;
+  }
+}
+}  // namespace otf
+
 using otf::check_device;
 using otf::set_cuda_error;
 
@@ -496,10 +513,10 @@ extern "C" OTF_API int otf_attn_rope_decode(const void* q, const void* k, const 
   auto* o = static_cast<uint16_t*>(out);
   const int64_t z = 0;
   cudaError_t e = head_dim == 128
-                      ? otf::launch_pdl(otf::k_attn_rope_decode<128>, grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
+                      ? otf::launch_pdl(otf::attn2_kernel<128>(heads / kv_heads), grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
                                         vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
                                         tickets, max_split, z, z, z, z, z)
-                      : otf::launch_pdl(otf::k_attn_rope_decode<64>, grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
+                      : otf::launch_pdl(otf::attn2_kernel<64>(heads / kv_heads), grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
                                         vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
                                         tickets, max_split, z, z, z, z, z);
   return set_cuda_error(e);
@@ -545,10 +562,10 @@ extern "C" OTF_API int otf_attn_rope_decode_batch(const void* q, int64_t ldq, co
   auto* vc = static_cast<uint16_t*>(v_cache);
   auto* o = static_cast<uint16_t*>(out);
   cudaError_t e = head_dim == 128
-                      ? otf::launch_pdl(otf::k_attn_rope_decode<128>, grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
+                      ? otf::launch_pdl(otf::attn2_kernel<128>(heads / kv_heads), grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
                                         vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
                                         tickets, max_split, ldq, ldkv, cache_stride, ldo, ws_stride)
-                      : otf::launch_pdl(otf::k_attn_rope_decode<64>, grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
+                      : otf::launch_pdl(otf::attn2_kernel<64>(heads / kv_heads), grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
                                         vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
                                         tickets, max_split, ldq, ldkv, cache_stride, ldo, ws_stride);
   return set_cuda_error(e);
