@@ -67,8 +67,10 @@ OTF_API int otf_last_cuda_error(void);
 /*
  * Device-side failure flag of the pipelined kernels (synchronous).  Every wait inside a
  * kernel is bounded; if one gives up (a pipeline that never completes), the kernel sets
- * this flag instead of hanging.  Returns 1 if set, 0 if not, -1 on a CUDA error; with
- * clear != 0 the flag is reset.  No counterpart in the reference (it has no pipelines).
+ * this flag instead of hanging.  The attention kernels set it too when the device-side
+ * position is outside [0, max_pos) (they then write nothing).  Returns 1 if set, 0 if not,
+ * -1 on a CUDA error; with clear != 0 the flag is reset.  No counterpart in the reference
+ * (it has no pipelines).
  */
 OTF_API int otf_device_error(int clear);
 
@@ -356,6 +358,8 @@ OTF_API int otf2b_decode_step(const otf2b_decode_dims* dims, void* h, void* work
  * 64 positions, fp32 arithmetic.  head_dim 64 or 128.  workspace: caller-owned, zeroed once,
  * otf_attn_workspace_bytes(...) bytes.
  * otf_pos_advance: *pos += 1 (the last launch of a token step).
+ * Every attention entry point reads pos on the device: a position outside [0, max_pos)
+ * writes nothing (no cache row, no output) and raises the otf_device_error flag.
  */
 OTF_API int otf_rope_kv(void* q, void* k, const void* v, const void* cos_sin, const int32_t* pos, void* k_cache,
                         void* v_cache, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t max_pos,
@@ -401,6 +405,10 @@ OTF_API int otf_pos_advance_batch(int32_t* pos, int64_t n, void* stream);
  * 128 fit up to max_pos 4032).  Nothing is allocated.  The first call on each device looks up
  * the array's device address: make that call before any stream capture.  All calls share the
  * array, so calls that can run at the same time on one GPU (other streams) race.
+ * The address is cached per device and context (a context created again after
+ * cudaDeviceReset is looked up afresh); the stream must belong to the current device
+ * (OTF_ERR_INVALID otherwise).  A position outside [0, max_pos) writes nothing and raises
+ * the otf_device_error flag, as otf_attn_decode does.
  */
 #define OTF_ATTN_SCRATCH_BYTES (2 * 1024 * 1024)
 OTF_API int otf_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const int32_t* pos,

@@ -20,11 +20,20 @@ namespace otf {
 
 int set_cuda_error(cudaError_t e);  // capi.cu
 int check_device();                 // capi.cu
+int attn_device_error(int clear);   // read (and optionally clear) the flag below
 
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kAttnMaxRep = 8;       // query heads per KV head
 constexpr int kAttnSplitPos = 64;    // cached positions per CTA (split-KV)
+
+// Set when an attention launch saw a position outside [0, max_pos): such a launch writes
+// nothing (no cache row, no output).  Read and cleared through otf_device_error.
+__device__ int g_attn_device_error;
+
+__device__ __forceinline__ void report_bad_position() {
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicExch(&g_attn_device_error, 1);
+}
 
 // q (heads x D), k (kv_heads x D) rotated in place with cos/sin of position *pos; k and v
 // copied into the caches at row *pos.  HF rotate_half form, fp16 arithmetic:
@@ -36,7 +45,10 @@ __global__ void k_rope_kv(uint16_t* q, uint16_t* k, const uint16_t* v, const uin
   pdl_trigger();
   pdl_wait();
   const int p = *pos;
-  if (p < 0 || p >= max_pos) return;  // the host sized the cache; an out-of-range position writes nothing
+  if (p < 0 || p >= max_pos) {  // the host sized the cache; an out-of-range position writes nothing
+    report_bad_position();
+    return;
+  }
   const int half = D / 2;
   const uint16_t* cs = cos_sin + (int64_t)p * 2 * D;
   const int nvec = (heads + kv_heads) * half;
@@ -78,7 +90,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const uint16_t* q,
   pdl_wait();
   const int rep = heads / kv_heads;
   const int g = blockIdx.x, sp = blockIdx.y;
-  const int L = min(*pos + 1, max_pos);
+  const int p = *pos;
+  if (p < 0 || p >= max_pos) {  // out of range: write nothing, as the fused kernel does
+    report_bad_position();
+    return;
+  }
+  const int L = p + 1;
   const int nsplit = min((L + kAttnSplitPos - 1) / kAttnSplitPos, max_split);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float sm_m[kAttnWarps][kAttnMaxRep], sm_l[kAttnWarps][kAttnMaxRep];
@@ -233,7 +250,10 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
     pos += b;
   }
   const int p = *pos;
-  if (p < 0 || p >= max_pos) return;  // the host sized the cache; out of range writes nothing
+  if (p < 0 || p >= max_pos) {  // the host sized the cache; out of range writes nothing
+    if (blockIdx.z == 0) report_bad_position();
+    return;
+  }
   const int rep = REP > 0 ? REP : heads / kv_heads;
   const int g = blockIdx.x, sp = blockIdx.y;
   const int L = p + 1;
@@ -571,6 +591,19 @@ extern "C" OTF_API int otf_attn_rope_decode_batch(const void* q, int64_t ldq, co
   return set_cuda_error(e);
 }
 
+int otf::attn_device_error(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, otf::g_attn_device_error, sizeof(int)) != cudaSuccess) {
+    set_cuda_error(cudaGetLastError());
+    return -1;
+  }
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(otf::g_attn_device_error, &z, sizeof(int));
+  }
+  return v;
+}
+
 extern "C" OTF_API int otf_pos_advance(int32_t* pos, void* stream) {
   if (!pos) return OTF_ERR_INVALID;
   int st = check_device();
@@ -602,21 +635,43 @@ constexpr int64_t kAttnScratchBytes = OTF_ATTN_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_attn_scratch[kAttnScratchBytes];
 }  // namespace otf
 
-// Device address of the scratch array on the current device, looked up once per device
-// (the array's host-side name is not a device address).
+// The current context, through the driver's cuCtxGetCurrent (looked up once from the runtime,
+// so the library does not link libcuda).  Null if the lookup failed.
+typedef int (*CtxGetCurrentFn)(void**);
+static void* current_context() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  void* c = nullptr;
+  if (fn && fn(&c) != 0) c = nullptr;
+  return c;
+}
+
+// Device address of the scratch array in the current device's context (the array's
+// host-side name is not a device address).  Looked up with cudaGetSymbolAddress on the
+// first call in each context and cached per device together with that context, so a
+// context torn down by cudaDeviceReset and created again is looked up afresh.
 static int attn_scratch_ptr(unsigned char** out) {
   static std::mutex mu;
   static unsigned char* ptr[64] = {};
+  static void* ctx[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_cuda_error(e);
   if (dev < 0 || dev >= 64) return OTF_ERR_UNSUPPORTED;
+  void* c = current_context();
   std::lock_guard<std::mutex> lk(mu);
-  if (!ptr[dev]) {
+  if (!ptr[dev] || c == nullptr || c != ctx[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, otf::g_attn_scratch);
     if (e != cudaSuccess) return set_cuda_error(e);
     ptr[dev] = static_cast<unsigned char*>(p);
+    ctx[dev] = c;
   }
   *out = ptr[dev];
   return OTF_OK;
@@ -632,14 +687,20 @@ extern "C" OTF_API int otf_attn_decode_noalloc(const void* q, const void* k_cach
   if (otf_attn_workspace_bytes(kv_heads, head_dim, max_pos) > otf::kAttnScratchBytes) return OTF_ERR_UNSUPPORTED;
   int st = check_device();
   if (st != OTF_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The scratch address belongs to the current device: the stream must be on that device.
+  int cur = 0, sdev = 0;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e == cudaSuccess) e = cudaStreamGetDevice(s, &sdev);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  if (sdev != cur) return OTF_ERR_INVALID;
   unsigned char* scratch = nullptr;
   st = attn_scratch_ptr(&scratch);
   if (st != OTF_OK) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   // The per-head tickets must start at zero (a completed call leaves them there; clearing
   // them here keeps a call independent of how an earlier one ended).
   const int64_t tbytes = otf::align_up(kv_heads * 4, 256);
-  cudaError_t e = cudaMemsetAsync(scratch, 0, (size_t)(kv_heads * 4), s);
+  e = cudaMemsetAsync(scratch, 0, (size_t)(kv_heads * 4), s);
   if (e != cudaSuccess) return set_cuda_error(e);
   const int max_split = (int)((max_pos + otf::kAttnSplitPos - 1) / otf::kAttnSplitPos);
   unsigned* tickets = reinterpret_cast<unsigned*>(scratch);

@@ -1448,6 +1448,7 @@ const void* ar_device_table(const otf_ar* ar);  // tp_ar.cu
 int64_t ar_max_elems(const otf_ar* ar);         // tp_ar.cu
 int ar_device_error(int clear);                 // tp_ar.cu
 int mk_device_error(int clear);                 // decode_step.cu
+int attn_device_error(int clear);               // attention.cu
 
 static int num_sms() {
   static thread_local int cached[64] = {};
@@ -1971,6 +1972,7 @@ extern "C" OTF_API int otf_device_error(int clear) {
   }
   const int w = ar_device_error(clear);
   const int x = mk_device_error(clear);
-  if (w < 0 || x < 0) return -1;
-  return v | w | x;
+  const int a = attn_device_error(clear);
+  if (w < 0 || x < 0 || a < 0) return -1;
+  return v | w | x | a;
 }

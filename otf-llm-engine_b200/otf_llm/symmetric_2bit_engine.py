@@ -56,7 +56,14 @@ class QuantizedEmbedding(nn.Module):
         dev = input_ids.device
         w = self.weight_int8 if self.weight_int8.device == dev else self.weight_int8.to(dev)
         s = self.scales if self.scales.device == dev else self.scales.to(dev)
-        rows = _native.i8_embed(input_ids, w.contiguous(), s.contiguous())
+        # Ids outside [0, V) raise, as F.embedding does (reference :44).  The kernel flags them
+        # on the device; reading the flag needs a host sync, which a CUDA graph capture cannot
+        # take, so a captured call writes zero rows for them instead.
+        capturing = torch.cuda.is_current_stream_capturing()
+        flag = None if capturing else torch.zeros(1, dtype=torch.int32, device=dev)
+        rows = _native.i8_embed(input_ids, w.contiguous(), s.contiguous(), flag)
+        if flag is not None and int(flag.item()):
+            raise IndexError("index out of range in self")
         return rows.view(*input_ids.shape, self.embedding_dim)
 
 

@@ -11,14 +11,16 @@ The outputs come from running the reference converter itself,
 otf_llm v4.1.0), unmodified, on CPU.  It moves each weight to the GPU with
 ``Tensor.cuda()`` (otf_llm/convert_symmetric_2bit.py:168, :177); this script makes that
 call return the tensor itself, so the same quantizer arithmetic runs on the host.
-Run in a container where the reference is mounted (read-only):
+Run where the reference's source tree is available (read-only), named by --reference or
+the OTF_REFERENCE_DIR environment variable:
 
-    python tests/golden/make_checkpoints.py
+    python tests/golden/make_checkpoints.py --reference /root/reference
 
 The tests never import the reference; they read these files.
 """
 from __future__ import annotations
 
+import argparse
 import json
 import os
 import shutil
@@ -28,7 +30,6 @@ import tempfile
 import torch
 from safetensors.torch import save_file
 
-REF = "/root/reference"
 OUT = os.path.dirname(os.path.abspath(__file__))
 
 # name: (hidden, intermediate, layers, heads, kv_heads, vocab, tied, qkv_bias, group_size, outlier_ratio, seed)
@@ -67,8 +68,14 @@ def source_model(hidden, inter, layers, heads, kv_heads, vocab, tied, qkv_bias, 
     return sd, prof
 
 
-def main() -> None:
-    sys.path.insert(0, REF)
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--reference", default=os.environ.get("OTF_REFERENCE_DIR"),
+                    help="directory holding the reference's otf_llm package (read-only)")
+    ref = ap.parse_args(argv).reference
+    if not ref or not os.path.isdir(os.path.join(ref, "otf_llm")):
+        ap.error("give the reference's source tree with --reference or OTF_REFERENCE_DIR")
+    sys.path.insert(0, ref)
     torch.Tensor.cuda = lambda self, *a, **k: self      # run the converter's quantizer on the host
     from otf_llm.convert_symmetric_2bit import convert_symmetric_model
 

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory from the reference implementation.
 
-Run in a container where the reference package is mounted (it is imported from
-/root/reference, read-only):
+Run where the reference's source tree is available (it is imported read-only from the
+directory given by --reference, or by the OTF_REFERENCE_DIR environment variable):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference /root/reference
 
 Each fixture is an .npz of seeded inputs and the reference's own outputs, produced by
 the reference functions named in its ``source`` entry (GT-Labs-AI/otf-llm-engine,
@@ -12,13 +12,26 @@ these files.
 """
 from __future__ import annotations
 
+import argparse
 import os
 import sys
 
 import numpy as np
 import torch
 
-REF = "/root/reference"
+
+def reference_dir(argv=None) -> str:
+    """The reference's source tree: --reference DIR, else $OTF_REFERENCE_DIR."""
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--reference", default=os.environ.get("OTF_REFERENCE_DIR"),
+                    help="directory holding the reference's otf_llm package")
+    ref = ap.parse_args(argv).reference
+    if not ref or not os.path.isdir(os.path.join(ref, "otf_llm")):
+        ap.error("give the reference's source tree with --reference or OTF_REFERENCE_DIR")
+    return ref
+
+
+REF = reference_dir()
 OUT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REF)
 

@@ -20,6 +20,17 @@ def test_embedding_golden_bit_exact(cuda_dev):
     assert np.array_equal(out.view(np.uint16), gd["emb_out"].view(np.uint16))
 
 
+def test_embedding_module_rejects_out_of_range_ids(cuda_dev):
+    """QuantizedEmbedding.forward raises on ids outside [0, V), as the reference's
+    F.embedding does (otf_llm/symmetric_2bit_engine.py:44)."""
+    from otf_llm.symmetric_2bit_engine import QuantizedEmbedding
+    emb = QuantizedEmbedding(100, 64).to(cuda_dev)
+    emb(torch.tensor([[0, 99]], device=cuda_dev))
+    for bad in ([[0, 100]], [[-1, 3]]):
+        with pytest.raises(IndexError):
+            emb(torch.tensor(bad, device=cuda_dev))
+
+
 def test_embedding_large_vocab_bit_exact(cuda_dev):
     from otf_llm import _native
     V, D = 128256, 3072
