@@ -46,9 +46,9 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def profile_traffic():
-    """dram bytes per GEMV launch from the committed ncu summary, if one exists."""
-    path = os.path.join(ROOT, "profiles", "gemv2b_7b_stack_traffic.txt")
+def profile_traffic(name: str):
+    """dram bytes per GEMV launch from a committed ncu summary, if it exists."""
+    path = os.path.join(ROOT, "profiles", name)
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch="):
@@ -185,44 +185,26 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
-class GemvLaunches:
-    """One otf2b_linear launch per projection of a stack (its weights, a fixed fp16 input of
-    the projection's width, the o/down residual), captured as one CUDA graph: the 2-bit GEMV
-    kernel's own launch duration over the stack's shapes."""
+class StepLaunches:
+    """The decode step's own 2-bit GEMV launches (4 grouped launches per layer: RMSNorm +
+    q/k/v, o + residual, RMSNorm + gate/up, SiLU + down + residual) captured as one CUDA graph
+    without the step's output copy: the dominant kernel's per-launch duration is this
+    graph's time divided by its launch count."""
 
     def __init__(self, stack):
         import torch
-        from otf_llm import _native
         dev = stack.norm_w.device
-        gen = torch.Generator(device=dev).manual_seed(17)
-        self.calls = []
-        keep = []
-        for layer in stack.layers:
-            for name, m in layer.items():
-                x = torch.randn(1, m.d_in, generator=gen, device=dev).half()
-                y = torch.empty(1, m.out_features, dtype=torch.float16, device=dev)
-                r = torch.randn(1, m.out_features, generator=gen, device=dev).half() if name in ("o_proj",
-                                                                                                "down_proj") else None
-                keep += [x, y, r]
-                self.calls.append((m, x, y, r))
-        self._keep = keep
-
-        def run():
-            for m, x, y, r in self.calls:
-                _native.linear_2bit(x, m.packed_uint8, m.scales, m.group_size, m.codebook,
-                                    mask=m.outlier_mask_vector if m.has_outliers else None,
-                                    outlier_idx=m.outlier_indices if m.has_outliers else None,
-                                    outlier_vals=m.outliers_fp16 if m.has_outliers else None,
-                                    bias=m.bias if m.has_bias else None, residual=r, clamp=True, out=y)
+        self.x = torch.randn(1, stack.cfg.hidden, generator=torch.Generator(device=dev).manual_seed(17),
+                             device=dev).half()
         s = torch.cuda.Stream(dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
-            run()
+            stack(self.x)
         torch.cuda.current_stream(dev).wait_stream(s)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            run()
+            stack(self.x)
         torch.cuda.synchronize(dev)
 
     def replay(self) -> None:
@@ -252,9 +234,9 @@ def run_b200(args, cfg):
     stack = Llama2BitLinearStack(cfg, device=dev, seed=1, rank=rank, world=world, process_group=pg,
                                  peer_ar=peer_ar, persistent=args.decode == "persistent")
     graph = DecodeGraph(stack)
-    # The dominant kernel timed on its own: every projection of this rank's stack as one 2-bit
-    # GEMV launch, back to back in a graph (the roofline's per-launch duration).
-    lin_graph = GemvLaunches(stack)
+    # The dominant kernel timed on its own: the step's grouped GEMV launches, back to back in a
+    # graph without the output copy (the roofline's per-launch duration).
+    lin_graph = StepLaunches(stack) if stack.mk is None else None
     torch.cuda.synchronize()
 
     bytes_tok_rank = stack.bytes_per_token()
@@ -299,22 +281,23 @@ def run_b200(args, cfg):
         graph.step_host(xh, yh)
     ms_e2e = timed(lambda: graph.step_host(xh, yh), args.steps)
 
-    # Dominant kernel: the 2-bit GEMV, one launch per projection over the same weights.
+    # Dominant kernel: the step's grouped 2-bit GEMV launches on their own.
     roofline = None
     if lin_graph is not None:
         for _ in range(2):
             lin_graph.replay()
         ms_lin = timed(lin_graph.replay, args.steps)
-        n_lin = len(lin_bytes)
-        avg_s = ms_lin / 1e3 / (args.steps * n_lin)
-        avg_bytes = sum(lin_bytes) / n_lin
+        avg_s = ms_lin / 1e3 / (args.steps * launches)
+        avg_bytes = bytes_tok_rank / launches
         peak, kind = measured_peak()
         achieved = avg_bytes / avg_s / 1e9
-        tr = profile_traffic()
+        tr = profile_traffic("gemv2b_group_7b_step_traffic.txt")
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                     "frac": round(achieved / peak, 4), "traffic": tr, "peak_kind": kind,
-                    "kernel": "k_gemv2b (2-bit GEMV, fused anchors/residual)", "launches_per_step": n_lin,
-                    "avg_launch_us": round(avg_s * 1e6, 3), "algorithmic_bytes_per_launch": round(avg_bytes)}
+                    "kernel": "k_gemv2b_group (grouped 2-bit GEMV: RMSNorm + q/k/v, o + residual, "
+                              "RMSNorm + gate/up, SiLU + down + residual)",
+                    "launches_per_step": launches, "avg_launch_us": round(avg_s * 1e6, 3),
+                    "algorithmic_bytes_per_launch": round(avg_bytes)}
 
     total_bytes = bytes_tok_rank * world  # x/y of column shards counted per rank
     if world > 1:

@@ -163,6 +163,239 @@ __device__ __forceinline__ __half xform_v(__half x, int xop, uint16_t aux_v, boo
 }
 
 
+// Where one CTA's activation side lives in shared memory and which slice of the layer it
+// owns (the batch-1 kernel's single and grouped launches).
+struct XSlice {
+  uint8_t* tbl;          // fixed-point table of the K slice (the MMA's B fragments)
+  __half* xs;            // staged x slice (fp16)
+  float2* sFT;           // per block: (2^-E / 64, c0 * sum x)
+  float* sS;             // per block: sum x (zero-point term)
+  float* xo;             // x at the anchor columns
+  float* afin_sum;       // anchor dot product of each row this CTA finishes
+  float* fin;            // K-partials pushed to this CTA: [parts][fin_rows]
+  uint8_t* zblk;         // zero block read by the lanes without a real B fragment
+  float* nrm;            // RMSNorm partial sums exchanged across the cluster
+  const uint8_t* ov;     // anchor weights of the finished rows in shared memory, or null
+  uint32_t ov_bar;       // mbarrier of their bulk copy
+  int kbeg, nbs, nbs_pad;  // first code of the K slice; real and padded blocks in it
+  int S, rank, group;    // cluster size, rank in it, cluster group of the layer
+  int frow0, nfin, fin_rows;  // rows this CTA finishes: [frow0, frow0 + nfin)
+};
+
+// Everything between the entry and the main loop that depends on the activation, run by the
+// kCThreads threads that compute (thread i < nfin also owns finished row frow0 + i): bias,
+// the PDL wait, residual, the tensor-parallel consumer's sum, the staged x slice with its
+// transform and mask, the RMSNorm statistics over the cluster, the anchor activations, the
+// fixed-point table and the anchor dot products.  Returns the row's bias + residual.
+template <int W>
+__device__ __forceinline__ float gemv_stage_x(const LinearArgs& a, const XSlice& c) {
+  constexpr int BLK = 16 * W, SL = tbl_sl(W), SB = tbl_sb(W);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Epilogue inputs of the rows this CTA finishes: thread i takes row c.frow0 + i.
+  const bool fin_ok = tid < c.nfin;
+  const int frow = c.frow0 + tid;
+  float ep = 0.0f;
+  if (fin_ok && a.bias) ep += h2f(ldg_u16(a.bias + frow));
+  // Anchor columns (independent of the predecessor): thread j < n_out holds column j.
+  int kcol = 0;
+  if (tid < a.n_out) kcol = (int)__ldg(a.oidx + tid);
+  // Weights, scales and bias are in flight; from here on we read the predecessor's output.
+  pdl_wait();
+  if (fin_ok && a.res) ep += h2f(ldg_u16(a.res + frow));
+  // Tensor-parallel consumer: x is the sum of every rank's rows in the receive buffer,
+  // each word polled until it carries this exchange's tag (bounded per thread).
+  const bool ar_cons = a.ar_mode == OTF_AR_CONSUME;
+  const unsigned ar_tg = ar_cons ? ar_tag(a.ar, a.ar_buf) : 0u;
+  uint32_t ar_budget = kArSpinLimit;
+  int ar_err = 0;
+  // x at this thread's anchor column (and the transform's second operand there), issued
+  // together with the staging loads below.
+  uint32_t x_k = 0u, xaux_k = 0u;
+  if (ar_cons) {
+    if (tid < a.n_out) x_k = ar_sum1(a.ar, a.ar_buf, kcol, ar_tg, ar_budget, ar_err);
+  } else {
+    ld_u16_pred(x_k, a.x + kcol, tid < a.n_out);
+  }
+  ld_u16_pred(xaux_k, a.xaux + kcol, tid < a.n_out && a.xaux != nullptr && a.xop != OTF_XOP_NONE);
+  // Stage my slice of x (fp16); padded tail = 0.  The SiLU gate and the mask apply on the
+  // way in; RMSNorm first needs the sum of squares of all K, combined across the cluster
+  // (the K slices partition K) over distributed shared memory, then a second pass.
+  const bool norm = a.xop == OTF_XOP_RMSNORM;
+  float ssq = 0.0f;
+  {
+    const uint4* xsrc = reinterpret_cast<const uint4*>(a.x + c.kbeg);
+    for (int v = tid; v < c.nbs_pad * BLK / 8; v += kCThreads) {
+      uint4 xv = make_uint4(0, 0, 0, 0);
+      if (v < c.nbs * BLK / 8) {
+        if (ar_cons) {
+          xv = ar_sum8(a.ar, a.ar_buf, (int64_t)c.kbeg + 8 * v, ar_tg, ar_budget, ar_err);
+          if (a.ar_out && c.group == 0) reinterpret_cast<uint4*>(a.ar_out + c.kbeg)[v] = xv;
+        } else {
+          xv = __ldg(xsrc + v);
+        }
+        __half2* xh = reinterpret_cast<__half2*>(&xv);
+        if (norm) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(xh[i]);
+            ssq = fmaf(f.x, f.x, fmaf(f.y, f.y, ssq));
+          }
+        } else {
+          if (a.xop == OTF_XOP_SILU_MUL) {
+            const uint4 uv = __ldg(reinterpret_cast<const uint4*>(a.xaux + c.kbeg) + v);
+            const __half* uh = reinterpret_cast<const __half*>(&uv);
+            __half* e = reinterpret_cast<__half*>(&xv);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float gv = __half2float(e[i]);
+              e[i] = __hmul(__float2half_rn(gv / (1.0f + expf(-gv))), uh[i]);
+            }
+          }
+          if (a.mask) {
+            const uint4 mv = __ldg(reinterpret_cast<const uint4*>(a.mask + c.kbeg) + v);
+            const __half2* mh = reinterpret_cast<const __half2*>(&mv);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xh[i] = __hmul2(xh[i], mh[i]);
+          }
+        }
+      }
+      reinterpret_cast<uint4*>(c.xs)[v] = xv;
+    }
+  }
+  cluster_wait();  // every CTA of the cluster is running: peers' shared memory is live
+  float rnorm = 1.0f;
+  if (norm) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
+    if (lane == 0) c.nrm[kMaxCluster + warp] = ssq;
+    named_barrier_sync(1, kCThreads);
+    if (tid == 0) {
+      float part = 0.0f;
+      for (int w = 0; w < kCWarps; ++w) part += c.nrm[kMaxCluster + w];
+      for (int q = 0; q < c.S; ++q) st_cluster_f32_plain(mapa_shared(smem_u32(c.nrm + c.rank), (uint32_t)q), part);
+    }
+    cluster_sync_all();
+    float tot = 0.0f;
+    for (int q = 0; q < c.S; ++q) tot += c.nrm[q];
+    rnorm = rsqrtf(tot / (float)a.K + a.eps);
+    for (int v = tid; v < c.nbs * BLK / 8; v += kCThreads) {
+      uint4 xv = reinterpret_cast<uint4*>(c.xs)[v];
+      __half* e = reinterpret_cast<__half*>(&xv);
+      uint4 wv = make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);  // ones
+      if (a.xaux) wv = __ldg(reinterpret_cast<const uint4*>(a.xaux + c.kbeg) + v);
+      const __half* wh = reinterpret_cast<const __half*>(&wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) e[i] = __hmul(wh[i], __float2half_rn(__half2float(e[i]) * rnorm));
+      if (a.mask) {
+        const uint4 mv = __ldg(reinterpret_cast<const uint4*>(a.mask + c.kbeg) + v);
+        __half2* xh = reinterpret_cast<__half2*>(&xv);
+        const __half2* mh = reinterpret_cast<const __half2*>(&mv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xh[i] = __hmul2(xh[i], mh[i]);
+      }
+      reinterpret_cast<uint4*>(c.xs)[v] = xv;
+    }
+  }
+  // Anchor activations: the transformed, unmasked x at the anchor columns.
+  if (tid < a.n_out)
+    c.xo[tid] = __half2float(xform_v(__ushort_as_half((uint16_t)x_k), a.xop, (uint16_t)xaux_k, a.xaux != nullptr, rnorm));
+  for (int j = tid + kCThreads; j < a.n_out; j += kCThreads) {
+    const int k = (int)__ldg(a.oidx + j);
+    const uint16_t av = (a.xaux && a.xop != OTF_XOP_NONE) ? ldg_u16(a.xaux + k) : (uint16_t)0;
+    c.xo[j] = __half2float(xform_v(__ushort_as_half(ldg_u16(a.x + k)), a.xop, av, a.xaux != nullptr, rnorm));
+  }
+  for (int i = tid; i < 32; i += kCThreads) reinterpret_cast<uint32_t*>(c.zblk)[i] = 0u;
+  named_barrier_sync(1, kCThreads);  // the staged slice of x is complete
+  if (ar_cons) {
+    if (ar_err) report_wait_failure();
+    if (tid == 0) ar_consumed(a.ar, a.ar_buf);  // every read of the buffer is done
+  }
+  // Quantise the table slice: 4W lanes per block, lane (w, j) owns codes 16w+4i+j.
+  {
+    constexpr int LPB = 4 * W;
+    constexpr int BPP = 32 / LPB;
+    const float bl = a.c1 - a.c0, bh = 0.5f * (a.c2 - a.c0);
+    const float cmax = fmaxf(fabsf(bl), fabsf(bh));
+    const int sub = lane / LPB, l = lane % LPB;
+    const int wq = l >> 2, j = l & 3;
+    for (int b0 = 0; b0 < c.nbs_pad; b0 += BPP * kCWarps) {
+      const int bi = b0 + warp * BPP + sub;
+      const bool on = bi < c.nbs_pad;
+      float xv[4];
+      float mx = 0.0f, sx = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float v = on ? __half2float(c.xs[bi * BLK + 16 * wq + 4 * i + j]) : 0.0f;
+        xv[i] = v;
+        mx = fmaxf(mx, fabsf(v));
+        sx += v;
+      }
+#pragma unroll
+      for (int o = LPB / 2; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        sx += __shfl_xor_sync(0xffffffffu, sx, o);
+      }
+      const int E = fixed_point_exp(mx * cmax);
+      const float sc = exp2i(E);
+      const float kl = bl * sc, kh = bh * sc;
+      int hl[4], ll[4], hh[4], lh[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        split_limbs(rint_small(xv[i] * kl), hl[i], ll[i]);
+        split_limbs(rint_small(xv[i] * kh), hh[i], lh[i]);
+      }
+      if (on) {
+        uint8_t* e = c.tbl + bi * SB + (wq * 4 + j) * 8;
+        *reinterpret_cast<uint2*>(e) =
+            make_uint2(pack4(hl[0], hl[1], hl[2], hl[3]), pack4(hh[0], hh[1], hh[2], hh[3]));
+        *reinterpret_cast<uint2*>(e + SL) =
+            make_uint2(pack4(ll[0], ll[1], ll[2], ll[3]), pack4(lh[0], lh[1], lh[2], lh[3]));
+        if (l == 0) {
+          c.sFT[bi] = make_float2(exp2i(-E) * (1.0f / 64.0f), a.c0 * sx);
+          c.sS[bi] = sx;
+        }
+      }
+    }
+  }
+  named_barrier_sync(1, kCThreads);
+  // Anchor dot products of the rows this CTA finishes, one row per thread, from the
+  // weights the bulk copy brought in (or from global memory when they did not fit).
+  if (a.n_out > 0 && tid < c.nfin) {
+    float d = 0.0f;
+    if (c.ov) {
+      if (!mbar_wait_spin(c.ov_bar, 0u)) report_wait_failure();
+      const uint16_t* ovr = reinterpret_cast<const uint16_t*>(c.ov) + (int64_t)tid * a.ldo;
+      for (int j = 0; j < a.n_out; ++j) d = fmaf(c.xo[j], h2f(ovr[j]), d);
+    } else {
+      const uint16_t* ovr = a.ovals + (int64_t)(c.frow0 + tid) * a.ldo;
+      for (int j = 0; j < a.n_out; ++j) d = fmaf(c.xo[j], h2f(ldg_u16(ovr + j)), d);
+    }
+    c.afin_sum[tid] = d;
+  }
+  return ep;
+}
+
+// The finisher: after one cluster barrier (every K-partial has landed in its shared memory)
+// thread i sums the parts of row frow0 + i in a fixed order, adds bias, residual and the
+// anchor term, and stores fp16 (or hands the fp32 row to the tensor-parallel exchange).
+__device__ __forceinline__ void gemv_finish(const LinearArgs& a, const XSlice& c, float ep, int parts) {
+  const int tid = threadIdx.x;
+  cluster_sync_all();
+  const bool ar_prod = a.ar_mode == OTF_AR_PRODUCE;
+  if (tid < c.nfin) {
+    const int frow = c.frow0 + tid;
+    float yv = ep + (a.n_out > 0 ? c.afin_sum[tid] : 0.0f);
+    for (int q = 0; q < parts; ++q) yv += c.fin[q * c.fin_rows + tid];
+    if (ar_prod) {
+      // Tensor-parallel producer: the fp32 row goes to every rank (clamped after the sum).
+      ar_put(a.ar, a.ar_buf, frow, yv, ar_tag(a.ar, a.ar_buf));
+    } else {
+      if (a.clamp) yv = fminf(fmaxf(yv, -65504.0f), 65504.0f);
+      a.y[frow] = f2h(yv);
+    }
+  }
+}
+
 template <int G, bool ZEROS>
 __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) {
   constexpr int W = words_for(G);
@@ -307,191 +540,12 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
     cp_async_commit();
   }
 
+  const XSlice xc{tbl, xs, sFT, sS, xo, afin_sum, fin, zblk, reinterpret_cast<float*>(smem + L.nrm),
+                  ov_smem ? smem + L.ov + ov_skew : nullptr, ov_bar, kbeg, nbs, nbs_pad, S, rank, group, frow0, nfin,
+                  fin_rows};
+  const float ep = gemv_stage_x<W>(a, xc);
   const int g = lane >> 2, t = lane & 3;
   {
-    // Epilogue inputs of the rows this CTA finishes: thread i takes row frow0 + i.
-    const bool fin_ok = tid < nfin;
-    const int frow = frow0 + tid;
-    float ep = 0.0f;
-    if (fin_ok && a.bias) ep += h2f(ldg_u16(a.bias + frow));
-    // Anchor columns (independent of the predecessor): thread j < n_out holds column j.
-    int kcol = 0;
-    if (tid < a.n_out) kcol = (int)__ldg(a.oidx + tid);
-    // Weights, scales and bias are in flight; from here on we read the predecessor's output.
-    pdl_wait();
-    if (fin_ok && a.res) ep += h2f(ldg_u16(a.res + frow));
-    // Tensor-parallel consumer: x is the sum of every rank's rows in the receive buffer,
-    // each word polled until it carries this exchange's tag (bounded per thread).
-    const bool ar_cons = a.ar_mode == OTF_AR_CONSUME;
-    const unsigned ar_tg = ar_cons ? ar_tag(a.ar, a.ar_buf) : 0u;
-    uint32_t ar_budget = kArSpinLimit;
-    int ar_err = 0;
-    // x at this thread's anchor column (and the transform's second operand there), issued
-    // together with the staging loads below.
-    uint32_t x_k = 0u, xaux_k = 0u;
-    if (ar_cons) {
-      if (tid < a.n_out) x_k = ar_sum1(a.ar, a.ar_buf, kcol, ar_tg, ar_budget, ar_err);
-    } else {
-      ld_u16_pred(x_k, a.x + kcol, tid < a.n_out);
-    }
-    ld_u16_pred(xaux_k, a.xaux + kcol, tid < a.n_out && a.xaux != nullptr && a.xop != OTF_XOP_NONE);
-    // Stage my slice of x (fp16); padded tail = 0.  The SiLU gate and the mask apply on the
-    // way in; RMSNorm first needs the sum of squares of all K, combined across the cluster
-    // (the K slices partition K) over distributed shared memory, then a second pass.
-    float* nrm = reinterpret_cast<float*>(smem + L.nrm);
-    const bool norm = a.xop == OTF_XOP_RMSNORM;
-    float ssq = 0.0f;
-    {
-      const uint4* xsrc = reinterpret_cast<const uint4*>(a.x + kbeg);
-      for (int v = tid; v < nbs_pad * BLK / 8; v += kCThreads) {
-        uint4 xv = make_uint4(0, 0, 0, 0);
-        if (v < nbs * BLK / 8) {
-          if (ar_cons) {
-            xv = ar_sum8(a.ar, a.ar_buf, (int64_t)kbeg + 8 * v, ar_tg, ar_budget, ar_err);
-            if (a.ar_out && group == 0) reinterpret_cast<uint4*>(a.ar_out + kbeg)[v] = xv;
-          } else {
-            xv = __ldg(xsrc + v);
-          }
-          __half2* xh = reinterpret_cast<__half2*>(&xv);
-          if (norm) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float2 f = __half22float2(xh[i]);
-              ssq = fmaf(f.x, f.x, fmaf(f.y, f.y, ssq));
-            }
-          } else {
-            if (a.xop == OTF_XOP_SILU_MUL) {
-              const uint4 uv = __ldg(reinterpret_cast<const uint4*>(a.xaux + kbeg) + v);
-              const __half* uh = reinterpret_cast<const __half*>(&uv);
-              __half* e = reinterpret_cast<__half*>(&xv);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float gv = __half2float(e[i]);
-                e[i] = __hmul(__float2half_rn(gv / (1.0f + expf(-gv))), uh[i]);
-              }
-            }
-            if (a.mask) {
-              const uint4 mv = __ldg(reinterpret_cast<const uint4*>(a.mask + kbeg) + v);
-              const __half2* mh = reinterpret_cast<const __half2*>(&mv);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) xh[i] = __hmul2(xh[i], mh[i]);
-            }
-          }
-        }
-        reinterpret_cast<uint4*>(xs)[v] = xv;
-      }
-    }
-    cluster_wait();  // every CTA of the cluster is running: peers' shared memory is live
-    float rnorm = 1.0f;
-    if (norm) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
-      if (lane == 0) nrm[kMaxCluster + warp] = ssq;
-      named_barrier_sync(1, kCThreads);
-      if (tid == 0) {
-        float part = 0.0f;
-        for (int w = 0; w < kCWarps; ++w) part += nrm[kMaxCluster + w];
-        for (int q = 0; q < S; ++q) st_cluster_f32_plain(mapa_shared(smem_u32(nrm + rank), (uint32_t)q), part);
-      }
-      cluster_sync_all();
-      float tot = 0.0f;
-      for (int q = 0; q < S; ++q) tot += nrm[q];
-      rnorm = rsqrtf(tot / (float)K + a.eps);
-      for (int v = tid; v < nbs * BLK / 8; v += kCThreads) {
-        uint4 xv = reinterpret_cast<uint4*>(xs)[v];
-        __half* e = reinterpret_cast<__half*>(&xv);
-        uint4 wv = make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);  // ones
-        if (a.xaux) wv = __ldg(reinterpret_cast<const uint4*>(a.xaux + kbeg) + v);
-        const __half* wh = reinterpret_cast<const __half*>(&wv);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) e[i] = __hmul(wh[i], __float2half_rn(__half2float(e[i]) * rnorm));
-        if (a.mask) {
-          const uint4 mv = __ldg(reinterpret_cast<const uint4*>(a.mask + kbeg) + v);
-          __half2* xh = reinterpret_cast<__half2*>(&xv);
-          const __half2* mh = reinterpret_cast<const __half2*>(&mv);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) xh[i] = __hmul2(xh[i], mh[i]);
-        }
-        reinterpret_cast<uint4*>(xs)[v] = xv;
-      }
-    }
-    // Anchor activations: the transformed, unmasked x at the anchor columns.
-    if (tid < a.n_out)
-      xo[tid] = __half2float(xform_v(__ushort_as_half((uint16_t)x_k), a.xop, (uint16_t)xaux_k, a.xaux != nullptr, rnorm));
-    for (int j = tid + kCThreads; j < a.n_out; j += kCThreads) {
-      const int k = (int)__ldg(a.oidx + j);
-      const uint16_t av = (a.xaux && a.xop != OTF_XOP_NONE) ? ldg_u16(a.xaux + k) : (uint16_t)0;
-      xo[j] = __half2float(xform_v(__ushort_as_half(ldg_u16(a.x + k)), a.xop, av, a.xaux != nullptr, rnorm));
-    }
-    for (int i = tid; i < 32; i += kCThreads) reinterpret_cast<uint32_t*>(zblk)[i] = 0u;
-    named_barrier_sync(1, kCThreads);  // the staged slice of x is complete
-    if (ar_cons) {
-      if (ar_err) report_wait_failure();
-      if (tid == 0) ar_consumed(a.ar, a.ar_buf);  // every read of the buffer is done
-    }
-    // Quantise the table slice: 4W lanes per block, lane (w, j) owns codes 16w+4i+j.
-    {
-      constexpr int LPB = 4 * W;
-      constexpr int BPP = 32 / LPB;
-      const float bl = a.c1 - a.c0, bh = 0.5f * (a.c2 - a.c0);
-      const float cmax = fmaxf(fabsf(bl), fabsf(bh));
-      const int sub = lane / LPB, l = lane % LPB;
-      const int wq = l >> 2, j = l & 3;
-      for (int b0 = 0; b0 < nbs_pad; b0 += BPP * kCWarps) {
-        const int bi = b0 + warp * BPP + sub;
-        const bool on = bi < nbs_pad;
-        float xv[4];
-        float mx = 0.0f, sx = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float v = on ? __half2float(xs[bi * BLK + 16 * wq + 4 * i + j]) : 0.0f;
-          xv[i] = v;
-          mx = fmaxf(mx, fabsf(v));
-          sx += v;
-        }
-#pragma unroll
-        for (int o = LPB / 2; o > 0; o >>= 1) {
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          sx += __shfl_xor_sync(0xffffffffu, sx, o);
-        }
-        const int E = fixed_point_exp(mx * cmax);
-        const float sc = exp2i(E);
-        const float kl = bl * sc, kh = bh * sc;
-        int hl[4], ll[4], hh[4], lh[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          split_limbs(rint_small(xv[i] * kl), hl[i], ll[i]);
-          split_limbs(rint_small(xv[i] * kh), hh[i], lh[i]);
-        }
-        if (on) {
-          uint8_t* e = tbl + bi * SB + (wq * 4 + j) * 8;
-          *reinterpret_cast<uint2*>(e) =
-              make_uint2(pack4(hl[0], hl[1], hl[2], hl[3]), pack4(hh[0], hh[1], hh[2], hh[3]));
-          *reinterpret_cast<uint2*>(e + SL) =
-              make_uint2(pack4(ll[0], ll[1], ll[2], ll[3]), pack4(lh[0], lh[1], lh[2], lh[3]));
-          if (l == 0) {
-            sFT[bi] = make_float2(exp2i(-E) * (1.0f / 64.0f), a.c0 * sx);
-            sS[bi] = sx;
-          }
-        }
-      }
-    }
-    named_barrier_sync(1, kCThreads);
-    // Anchor dot products of the rows this CTA finishes, one row per thread, from the
-    // weights the bulk copy brought in (or from global memory when they did not fit).
-    if (a.n_out > 0 && tid < nfin) {
-      float d = 0.0f;
-      if (ov_smem) {
-        if (!mbar_wait(ov_bar, 0u)) report_wait_failure();
-        const uint16_t* ovr = reinterpret_cast<const uint16_t*>(smem + L.ov + ov_skew) + (int64_t)tid * a.ldo;
-        for (int j = 0; j < a.n_out; ++j) d = fmaf(xo[j], h2f(ovr[j]), d);
-      } else {
-        const uint16_t* ovr = a.ovals + (int64_t)(frow0 + tid) * a.ldo;
-        for (int j = 0; j < a.n_out; ++j) d = fmaf(xo[j], h2f(ldg_u16(ovr + j)), d);
-      }
-      afin_sum[tid] = d;
-    }
-
     // Main loop: my tiles tl = warp + 8*i, their chunks in order, one stage each.  The MMA
     // accumulators run across a tile's stages; each set's contribution is the difference of
     // the folded sums before and after it (uint32 arithmetic), so no MMA starts from zero.
@@ -614,21 +668,8 @@ __device__ __forceinline__ void gemv_body(const LinearArgs& a, const int group) 
       }
     }
     cp_async_wait<0>();
-    // One cluster barrier below: every partial has landed in its finisher's shared memory.
-    cluster_sync_all();
-    const bool ar_prod = a.ar_mode == OTF_AR_PRODUCE;
-    if (fin_ok) {
-      float yv = ep + (a.n_out > 0 ? afin_sum[tid] : 0.0f);
-      for (int q = 0; q < S; ++q) yv += fin[q * fin_rows + tid];
-      if (ar_prod) {
-        // Tensor-parallel producer: the fp32 row goes to every rank (clamped after the sum).
-        ar_put(a.ar, a.ar_buf, frow, yv, ar_tag(a.ar, a.ar_buf));
-      } else {
-        if (a.clamp) yv = fminf(fmaxf(yv, -65504.0f), 65504.0f);
-        a.y[frow] = f2h(yv);
-      }
-    }
-
+    // One cluster barrier: every partial has landed in its finisher's shared memory.
+    gemv_finish(a, xc, ep, S);
   }
 }
 
@@ -1449,6 +1490,7 @@ int64_t ar_max_elems(const otf_ar* ar);         // tp_ar.cu
 int ar_device_error(int clear);                 // tp_ar.cu
 int mk_device_error(int clear);                 // decode_step.cu
 int attn_device_error(int clear);               // attention.cu
+int head_device_error(int clear);               // int8_ops.cu
 
 static int num_sms() {
   static thread_local int cached[64] = {};
@@ -1493,13 +1535,13 @@ static GemvPlan gemv_plan(const LinearArgs& a, int S, int budget) {
 
 // Largest number of co-resident clusters of S CTAs of a kernel for a given dynamic shared
 // memory size (cached: the occupancy query is a host call we do not want per launch).
-static int max_active_clusters_of(const void* kernel, int S, int64_t smem) {
+static int max_active_clusters_of(const void* kernel, int S, int64_t smem, int threads = kThreads) {
   static std::mutex mu;
-  static std::map<std::tuple<int, const void*, int, int64_t>, int> cache;
+  static std::map<std::tuple<int, const void*, int, int64_t, int>, int> cache;
   int dev = 0;
   cudaGetDevice(&dev);
   const int64_t bucket = align_up(smem, 4096);
-  const auto key = std::make_tuple(dev, kernel, S, bucket);
+  const auto key = std::make_tuple(dev, kernel, S, bucket, threads);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -1507,7 +1549,7 @@ static int max_active_clusters_of(const void* kernel, int S, int64_t smem) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)S, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3((unsigned)threads, 1, 1);
   cfg.dynamicSmemBytes = (size_t)bucket;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1749,6 +1791,7 @@ static int fast_variant(const LinearArgs& a, uint32_t flags) {
   return (a.G >= 32) ? a.G : 0;
 }
 
+
 // tcgen05 GEMM variant: the group size (32, 64, 128, 256) when the rows, vectors and strides are
 // aligned for its copies (any codebook: the dequant is a table lookup), else 0.
 static int tc_variant(const LinearArgs& a) {
@@ -1973,6 +2016,7 @@ extern "C" OTF_API int otf_device_error(int clear) {
   const int w = ar_device_error(clear);
   const int x = mk_device_error(clear);
   const int a = attn_device_error(clear);
-  if (w < 0 || x < 0 || a < 0) return -1;
-  return v | w | x | a;
+  const int h = head_device_error(clear);
+  if (w < 0 || x < 0 || a < 0 || h < 0) return -1;
+  return v | w | x | a | h;
 }

@@ -6,6 +6,8 @@
 // MMA columns 2t (hi) and 2t+1 (lo), so each thread's accumulator fragment holds
 // its own block.  Replaces QuantizedLinearHead.forward
 // (otf_llm/symmetric_2bit_engine.py:75-91) and QuantizedEmbedding.forward (:41-47).
+#include <cuda.h>
+
 #include <algorithm>
 
 #include "otf_common.cuh"
@@ -14,6 +16,12 @@ namespace otf {
 
 int set_cuda_error(cudaError_t e);  // capi.cu
 int check_device();                 // capi.cu
+bool encode_tiled_2d(void* map, int elem_bytes, const void* base, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                     uint32_t box_inner, uint32_t box_rows, bool swizzle128);  // capi.cu
+int head_device_error(int clear);   // read (and optionally clear) the flag below
+
+// Set when a bounded wait of the TMA-fed head gives up; read through otf_device_error.
+__device__ int g_head_device_error;
 
 constexpr int kHeadWarps = 8;
 constexpr int kHeadSL = 24;  // bytes per (block, limb): 16 data + 8 pad (conflict-free lane map)
@@ -202,6 +210,167 @@ __global__ void __launch_bounds__(kHeadWarps * 32) k_i8_head_imma(const HeadArgs
   cp_async_wait<0>();
 }
 
+// TMA-fed head: one producer warp streams boxes of 64 vocabulary rows x 128 weight bytes
+// (128-byte swizzle) into two rings, one per team of four consumer warps.  Team k takes the
+// CTA's row quads k, k+2, ... with all their chunks in order; warp w of the team multiplies
+// tile w (16 rows) of each box, both MMA sets, exactly as the copy-stage kernel does.  The
+// producer alternates the teams' boxes and refills a slot once that team's four warps have
+// consumed it.  Every wait is bounded (about a second; then the flag above is raised).
+constexpr int kHTRows = 64;                          // rows per box
+constexpr int kHTBoxBytes = kHTRows * kHeadChunk;    // 8 KB
+constexpr int kHTConsumers = 8;                      // two teams of four
+constexpr int kHTThreads = (kHTConsumers + 1) * 32;
+constexpr int kHTSlots = 4;                          // ring slots per team (a power of two)
+
+struct alignas(64) HeadTmaArgs {
+  CUtensorMap wmap;  // int8 [V, D], 128 x 64 boxes, 128-byte swizzle
+  HeadArgs a;
+};
+
+__host__ __device__ inline int64_t head_tma_smem_bytes(int D) {
+  return 1024 + 2 * kHTSlots * kHTBoxBytes + 128 + head_smem_bytes(D);
+}
+
+__device__ __forceinline__ void head_wait_failed() { atomicExch(&g_head_device_error, 1); }
+
+__global__ void __launch_bounds__(kHTThreads, 2) k_i8_head_tma(const __grid_constant__ HeadTmaArgs p) {
+  const HeadArgs& a = p.a;
+  pdl_trigger();
+  // Dynamic shared memory rounded up to the 1024-byte period of the swizzle (1 KB of slack).
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* const smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* const ring = smem;                                      // [team][slot] boxes
+  const uint32_t full = smem_u32(smem + 2 * kHTSlots * kHTBoxBytes);
+  const uint32_t empty = full + 8 * 2 * kHTSlots;
+  uint8_t* const tbl = smem + 2 * kHTSlots * kHTBoxBytes + 128;
+  const int nb = a.D / 16;
+  float* const metaF = reinterpret_cast<float*>(tbl + align_up((int64_t)nb * kHeadSB, 16));
+  uint8_t* const zblk = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(metaF + nb), 16));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nq = ceil_div(a.V, kHTRows), nch = ceil_div(a.D, kHeadChunk);
+  const int q_beg = (int)((int64_t)blockIdx.x * nq / gridDim.x);
+  const int q_end = (int)((int64_t)(blockIdx.x + 1) * nq / gridDim.x);
+  const int nq0 = (q_end - q_beg + 1) / 2, nq1 = (q_end - q_beg) / 2;  // quads of teams 0 and 1
+  if (tid == 0) {
+    for (int i = 0; i < 2 * kHTSlots; ++i) {
+      mbar_init(full + 8 * i, 1);
+      mbar_init(empty + 8 * i, 4);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == kHTConsumers) {
+    // Producer (weights only: they do not depend on the previous kernel, so no PDL wait).
+    if (lane == 0) {
+      const int nbox[2] = {nq0 * nch, nq1 * nch};
+      int i[2] = {0, 0}, q[2] = {q_beg, q_beg + 1}, c[2] = {0, 0};
+      while (i[0] < nbox[0] || i[1] < nbox[1]) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          if (i[k] >= nbox[k]) continue;
+          const int sl = k * kHTSlots + (i[k] & (kHTSlots - 1));
+          if (i[k] >= kHTSlots && !mbar_wait_sleep(empty + 8 * sl, (uint32_t)((i[k] / kHTSlots) - 1) & 1u))
+            head_wait_failed();
+          mbar_arrive_expect_tx(full + 8 * sl, (uint32_t)kHTBoxBytes);
+          tma_load_2d(smem_u32(ring + sl * kHTBoxBytes), &p.wmap, c[k] * kHeadChunk, q[k] * kHTRows, full + 8 * sl);
+          ++i[k];
+          if (++c[k] == nch) {
+            c[k] = 0;
+            q[k] += 2;
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  pdl_wait();
+  // Activation table for the whole D (every CTA builds its own; its rows amortise it).
+  for (int it = tid; it < 2 * nb; it += kHTConsumers * 32) {
+    const int b = it >> 1, limb = it & 1;
+    float xv[16];
+    float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      xv[i] = h2f(a.x[b * 16 + i]);
+      mx = fmaxf(mx, fabsf(xv[i]));
+    }
+    const int E = fixed_point_exp(mx);
+    const float sc = ldexpf(1.0f, E);
+    uint32_t wd[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      int hi, lo;
+      split_limbs(__float2int_rn(__fmul_rn(xv[i], sc)), hi, lo);
+      wd[i >> 2] |= (uint32_t)((limb == 0 ? hi : lo) & 0xff) << (8 * (i & 3));
+    }
+    uint2* dst = reinterpret_cast<uint2*>(tbl + b * kHeadSB + limb * kHeadSL);
+    dst[0] = make_uint2(wd[0], wd[1]);
+    dst[1] = make_uint2(wd[2], wd[3]);
+    if (limb == 0) metaF[b] = ldexpf(1.0f, -E);
+  }
+  if (tid < 4) reinterpret_cast<uint32_t*>(zblk)[tid] = 0u;
+  named_barrier_sync(1, kHTConsumers * 32);
+
+  const int team = warp >> 2, wt = warp & 3;
+  const int g = lane >> 2, t = lane & 3;
+  const bool breal = (g >> 1) == t;
+  const int r = wt * 16 + g;                        // box row of this thread's first row
+  int i = 0;                                        // this team's box count
+  const int my_nq = team ? nq1 : nq0;
+  for (int qi = 0; qi < my_nq; ++qi) {
+    const int quad = q_beg + team + 2 * qi;
+    float acc0 = 0.0f, acc1 = 0.0f;
+    for (int cc = 0; cc < nch; ++cc, ++i) {
+      const int sl = team * kHTSlots + (i & (kHTSlots - 1));
+      if (!mbar_wait_spin(full + 8 * sl, (uint32_t)(i / kHTSlots) & 1u)) head_wait_failed();
+      const uint8_t* const box = ring + sl * kHTBoxBytes;
+#pragma unroll
+      for (int set = 0; set < 2; ++set) {
+        // 16-byte piece 2t+set of rows r and r+8 (piece j of row r sits at j ^ (r & 7) = j ^ g).
+        const uint8_t* pa = box + r * kHeadChunk + (((2 * t + set) ^ g) << 4);
+        const uint4 cw = *reinterpret_cast<const uint4*>(pa);
+        const uint4 cw8 = *reinterpret_cast<const uint4*>(pa + 8 * kHeadChunk);
+        const int blk = cc * 8 + 2 * t + set;          // my block (this quad's)
+        const int bblk = cc * 8 + 2 * (g >> 1) + set;  // the block whose B rows this lane supplies
+        const uint8_t* bp = (breal && bblk < nb) ? (tbl + bblk * kHeadSB + (g & 1) * kHeadSL) : zblk;
+        const uint2 b01 = *reinterpret_cast<const uint2*>(bp);
+        const uint2 b23 = *reinterpret_cast<const uint2*>(bp + 8);
+        int C[4] = {0, 0, 0, 0};
+        mma_s8s8(C, cw.x, cw8.x, cw.y, cw8.y, b01.x, b01.y);
+        mma_s8s8(C, cw.z, cw8.z, cw.w, cw8.w, b23.x, b23.y);
+        if (blk < nb) {
+          const float F = metaF[blk];
+          acc0 = fmaf((float)(256 * C[0] + C[1]), F, acc0);
+          acc1 = fmaf((float)(256 * C[2] + C[3]), F, acc1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + 8 * sl);
+    }
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+    const int rg = quad * kHTRows + r, rg8 = rg + 8;
+    const float l0 = rg < a.V ? head_finish(acc0, h2f(a.scales[rg])) : 0.0f;
+    const float l1 = rg8 < a.V ? head_finish(acc1, h2f(a.scales[rg8])) : 0.0f;
+    if (t == 0 && a.out) {
+      if (rg < a.V) a.out[rg] = l0;
+      if (rg8 < a.V) a.out[rg8] = l1;
+    }
+    if (a.amax) {
+      unsigned long long key = 0ull;
+      if (rg < a.V) key = argmax_key(l0, rg);
+      if (rg8 < a.V) key = max(key, argmax_key(l1, rg8));
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+      if (lane == 0) atomicMax(a.amax, key);
+    }
+  }
+}
+
 // Portable head for any D / stride: one warp per vocabulary row.
 __global__ void __launch_bounds__(256) k_i8_head_generic(const HeadArgs a) {
   pdl_trigger();
@@ -251,6 +420,46 @@ __global__ void k_i8_embed(const int64_t* ids, int n, const int8_t* w, int64_t l
 
 using namespace otf;
 
+int otf::head_device_error(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, otf::g_head_device_error, sizeof(int)) != cudaSuccess) {
+    set_cuda_error(cudaGetLastError());
+    return -1;
+  }
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(otf::g_head_device_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+// The TMA-fed head for rows of 16-byte aligned int8 weights (D a multiple of 16); false if
+// the layout does not qualify (the caller then runs the copy-stage kernel).
+static bool head_launch_tma(const HeadArgs& a, cudaStream_t s, cudaError_t& err) {
+  const int64_t smem = head_tma_smem_bytes(a.D);
+  if (a.D % 16 || a.ldw % 16 || reinterpret_cast<uintptr_t>(a.w) % 16 || smem > 227 * 1024) return false;
+  static thread_local int configured_dev[64] = {};
+  static thread_local int sms_of[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return false;
+  if (!configured_dev[dev]) {
+    err = cudaFuncSetAttribute(k_i8_head_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (err != cudaSuccess) return true;
+    cudaDeviceGetAttribute(&sms_of[dev], cudaDevAttrMultiProcessorCount, dev);
+    configured_dev[dev] = 1;
+  }
+  static thread_local HeadTmaArgs p;  // 128-byte tensor map + arguments, kept off the stack
+  if (!encode_tiled_2d(&p.wmap, 1, a.w, (uint64_t)a.D, (uint64_t)a.V, (uint64_t)a.ldw, (uint32_t)kHeadChunk,
+                       (uint32_t)kHTRows, true))
+    return false;
+  p.a = a;
+  const int per_sm = smem <= 113 * 1024 ? 2 : 1;
+  const int ctas = std::max(1, std::min(ceil_div(a.V, kHTRows), per_sm * std::max(1, sms_of[dev])));
+  err = launch_pdl(k_i8_head_tma, dim3((unsigned)ctas), dim3(kHTThreads), (size_t)smem, s, 1u, p);
+  return true;
+}
+
 static int head_launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scales, float* logits,
                        int64_t ldl, unsigned long long* keys, int64_t M, int64_t V, int64_t D, cudaStream_t s) {
   const bool fast = D % 16 == 0 && ldw % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
@@ -276,8 +485,13 @@ static int head_launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw,
     a.amax = keys ? keys + m : nullptr;
     a.V = (int)V;
     a.D = (int)D;
+    cudaError_t e = cudaSuccess;
+    if (head_launch_tma(a, s, e)) {
+      if (e != cudaSuccess) return set_cuda_error(e);
+      continue;
+    }
     const int ctas_per_sm = head_pipe_smem_bytes((int)D) <= 110 * 1024 ? 2 : 1;
-    cudaError_t e = fast ? launch_pdl(k_i8_head_imma,
+    e = fast ? launch_pdl(k_i8_head_imma,
                                       dim3(std::max(1, std::min(ceil_div(ceil_div((int)V, 16), kHeadWarps),
                                                                 sms * ctas_per_sm))),
                                       dim3(kHeadWarps * 32), (size_t)head_pipe_smem_bytes((int)D), s, 1u, a)

@@ -115,6 +115,43 @@ __device__ __forceinline__ bool mbar_wait(uint32_t addr, uint32_t parity) {
     if (mbar_try_wait_hint(addr, parity)) return true;
   return false;
 }
+// try_wait without a suspend-time hint (the thread is parked for a short system-defined
+// time at most and released as soon as the phase completes); the wait is bounded by the
+// global timer instead of a poll count: false after about one second.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t addr, uint32_t parity) {
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(addr, parity)) return true;
+    if (global_ns() - t0 > 1000000000ull) return false;
+  }
+}
+// The same wait for a thread that is not on the critical path (a copy producer refilling
+// slots): a short sleep between polls keeps it from taking issue slots from the warps that
+// compute.
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t addr, uint32_t parity) {
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    __nanosleep(64);
+    if (mbar_try_wait(addr, parity)) return true;
+    if (global_ns() - t0 > 1000000000ull) return false;
+  }
+}
 // 2-D tiled bulk tensor load into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int x, int y, uint32_t mbar) {
   asm volatile(

@@ -65,7 +65,8 @@ def test_head_golden(cuda_dev):
         assert rel_err(lg, gd[f"logits_m{M}"]) < 1.5e-3
 
 
-@pytest.mark.parametrize("V,D,M", [(128256, 3072, 1), (128256, 8192, 1), (1000, 200, 2), (4097, 64, 3)])
+@pytest.mark.parametrize("V,D,M", [(128256, 3072, 1), (128256, 8192, 1), (1000, 200, 2), (4097, 64, 3),
+                                   (17, 256, 1), (65, 128, 2), (1000, 4096, 1), (64000, 8192, 4), (300, 2064, 1)])
 def test_head_shapes(V, D, M, cuda_dev):
     from otf_llm import _native
     g = torch.Generator().manual_seed(V + D)
@@ -75,6 +76,32 @@ def test_head_shapes(V, D, M, cuda_dev):
     lg = _native.i8_head(x.to(cuda_dev), w.to(cuda_dev), s.to(cuda_dev)).cpu().numpy()
     ref = oracle.i8_head(x.numpy(), w.numpy(), s.numpy())
     assert rel_err(lg, ref) < 1e-3
+
+
+def test_head_graph_replay(cuda_dev):
+    """The head's launch (its weight tensor map travels in the kernel parameters) replays
+    from a CUDA graph exactly as it ran eagerly."""
+    from otf_llm import _native
+    g = torch.Generator().manual_seed(3)
+    w = torch.randint(-127, 128, (20000, 3072), generator=g, dtype=torch.int32).to(torch.int8).to(cuda_dev)
+    s = (torch.rand(20000, 1, generator=g) * 2e-4 + 1e-5).half().to(cuda_dev)
+    x = torch.randn(1, 3072, generator=g).half().to(cuda_dev)
+    out = torch.empty(1, 20000, dtype=torch.float32, device=cuda_dev)
+    _native.i8_head(x, w, s, out)
+    eager = out.clone()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        _native.i8_head(x, w, s, out)
+    torch.cuda.current_stream().wait_stream(st)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        _native.i8_head(x, w, s, out)
+    out.zero_()
+    gr.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    assert _native.device_error() == 0
 
 
 @pytest.mark.parametrize("V,D,M", [(128256, 3072, 1), (1000, 256, 3), (50000, 4096, 2), (777, 272, 2)])
