@@ -411,7 +411,7 @@ def run_sweep(args):
     for (N, K) in [(28672, 8192), (8192, 28672)]:
         R = 4
         Ls = [layer(N, K) for _ in range(R)]
-        for M in [1, 2, 4, 8, 16, 32, 64]:
+        for M in [1, 2, 4, 8, 9, 16, 32, 64, 128]:
             x = torch.randn(M, K, device=dev, generator=gen).half()
             y = torch.empty(M, N, dtype=torch.float16, device=dev)
 
@@ -444,8 +444,8 @@ def run_sweep(args):
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1e3 / (reps * R)
             nb = linear_bytes(N, K, 64, max(1, int(K * 0.005)), batch=M)
-            kernel = ("k_gemm2b_tc (tcgen05)" if M >= 32 else "k_gemv2b" if M == 1 else
-                      "k_gemv2b_batch (8-row slices)")
+            kernel = ("k_gemm2b_tmem (tcgen05, dequantised weights in tensor memory)" if M >= 9 else
+                      "k_gemv2b" if M == 1 else "k_gemv2b_batch")
             print(json.dumps({"sweep": "70B MLP 2-bit GEMM", "N": N, "K": K, "B": M, "us": round(us, 2),
                               "GBps": round(nb / us / 1e3, 1), "TFLOPs": round(2 * M * N * K / us / 1e6, 1),
                               "kernel": kernel, "data": "synthetic codes/scales, 4 rotating copies",

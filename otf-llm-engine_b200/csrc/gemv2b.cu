@@ -35,6 +35,8 @@
 // Reference behaviour replaced: otf_llm/otf_triton_2bit_kernel.py:164-194 (dispatch,
 // mask multiply, LUT path), :23-113 (warp GEMV), otf_llm/symmetric_2bit_engine.py:
 // 214-235 (bias, outlier anchors, clamp), otf_llm/otf_2bit_quantizer.py:193-221.
+#include <cuda.h>
+
 #include <algorithm>
 #include <map>
 #include <mutex>
@@ -1402,6 +1404,388 @@ __global__ void __launch_bounds__(tc::kThreadsT, 1) k_gemm2b_tc(const __grid_con
 }
 
 
+// ---------------------------------------------------------------------------------------
+// Batched and prefill shapes with the dequantised weights in tensor memory (k_gemm2b_tmem):
+// the weight-only-quantised GEMM in its tcgen05 form, for symmetric layers with G = 32 or 64
+// and 16-byte aligned code, scale and activation rows.
+//
+// CTA = 128 weight rows (MMA M) x NB activation rows (MMA N), eleven warps:
+//  * warp 0 streams 512-code "super-stages" (128 rows x 128 code bytes, 128-byte swizzle, and
+//    the rows' scales) into ring 1 with tensor copies, before the programmatic-dependent-launch
+//    wait (weights do not depend on the previous kernel);
+//  * warp 1 streams the x tile of each 64-code K tile (NB rows x 128 bytes, 128-byte swizzle:
+//    the MMA's B operand as it lands) into ring 2;
+//  * warps 3-10 dequantise: thread (quarter, half) turns 32 codes of row 32*quarter + lane into
+//    fp16 -- W = fp16(c[q] * s) through a byte-permute table, the reference's own fp16 dequant,
+//    times the mask where it is not 1 -- and stores them with tcgen05.st into the K tile's A
+//    buffer in tensor memory (a warp reaches only its own 32 lanes: quarter = warp % 4);
+//  * warp 2 issues the tile's four K=16 tcgen05.mma (A from tensor memory, B from shared
+//    memory) and commits them to the slot's empty barrier, which frees the A buffer and the
+//    x tile together.
+// The fp32 accumulator is in tensor memory as well; the dequant warps read it back for the
+// epilogue (bias, residual, clamp).  The fp16 anchors are extra K tiles of the same
+// accumulation (A = the rows' anchor weights, B = x at the anchor columns).  Split K over a
+// cluster of S CTAs as in k_gemm2b_tc, in whole super-stages.  Every wait is bounded.
+namespace tm {
+constexpr int kRowsW = 128;       // weight rows per CTA = MMA M
+constexpr int kKT = 64;           // codes per K tile
+constexpr int kSS = 8;            // K tiles per super-stage (one 128-byte row of codes)
+constexpr int kNS1 = 3;           // super-stage slots
+constexpr int kNA = 4;            // A buffers in tensor memory (K tiles in flight)
+constexpr int kMaxNX = 16;        // x-tile slots in shared memory (the host sizes the ring)
+constexpr int kWarps = 11;
+constexpr int kThr = kWarps * 32;
+constexpr int kDeq = 8;           // dequant warps 3..10
+}  // namespace tm
+
+struct alignas(64) TmParams {
+  CUtensorMap cmap;  // codes uint8 [N, K/4]: 128 x 128 boxes, 128-byte swizzle
+  CUtensorMap smap;  // scales fp16 [N, K/G]: (512/G) x 128 boxes
+  CUtensorMap xmap;  // x fp16 [M, K]: 64 x NB boxes, 128-byte swizzle
+  LinearArgs a;
+};
+
+// x-tile slots for NB activation rows: a 32 KB ring, between 4 and 16 slots.
+__host__ __device__ constexpr int tm_nx(int nb) {
+  return (32 * 1024) / (nb * 128) < 4 ? 4 : ((32 * 1024) / (nb * 128) > tm::kMaxNX ? tm::kMaxNX : (32 * 1024) / (nb * 128));
+}
+
+struct TmSmem {
+  int64_t codes, xt, scl, sel, amask, bars, tptr, total;
+};
+
+// nkt_max: K tiles of the largest K slice of the cluster.
+__host__ __device__ inline TmSmem tm_smem_layout(int nb, int G, int nkt_max) {
+  TmSmem L;
+  int64_t off = 0;
+  const int nx = tm_nx(nb);
+  L.codes = off; off += (int64_t)tm::kNS1 * tm::kRowsW * 128;                 // 16 KB per slot
+  L.xt = off;    off += (int64_t)(nx > 4 ? nx : 4) * nb * 128;              // nb rows x 128 B per slot
+  L.scl = off;   off = align_up(off + (int64_t)tm::kNS1 * tm::kRowsW * 2 * (tm::kSS * tm::kKT / G), 128);
+  L.sel = off;   off += 256 * 16 * 4;                                        // selectors, 16 copies
+  L.amask = off; off = align_up(off + (int64_t)nkt_max * 8, 16);            // columns whose mask is not 1
+  L.bars = off;  off = align_up(off + (2 * tm::kNS1 + 2 * tm::kMaxNX + 2 * tm::kNA + 1) * 8, 16);
+  L.tptr = off;  off += 16;
+  L.total = off;
+  return L;
+}
+
+template <int G, int NB>
+__global__ void __launch_bounds__(tm::kThr, 2) k_gemm2b_tmem(const __grid_constant__ TmParams p) {
+  using namespace tm;
+  static_assert(G == 32 || G == 64, "group size");
+  static_assert(NB % 16 == 0 && NB >= 16 && NB <= 256, "MMA N");
+  // Independent fp32 accumulators: the MMAs into one accumulator form a dependent chain, so
+  // consecutive K=16 steps go round-robin to NACC of them (summed in the epilogue).
+  constexpr int NACC = NB <= 32 ? 4 : (NB <= 128 ? 2 : 1);
+  constexpr int ACOL = NACC * NB;                             // first A-buffer column
+  constexpr int NCOLS = ACOL + kNA * 32 <= 256 ? 256 : 512;  // accumulators + A buffers (power of two)
+  constexpr int NX = tm_nx(NB);
+  constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(kRowsW >> 4) << 24);
+  constexpr int SROW = 2 * (kSS * kKT / G);                   // scale bytes per row per super-stage
+  const LinearArgs& a = p.a;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // The 128-byte swizzle is keyed to absolute shared-memory address bits (1 KB of slack).
+  uint8_t* const smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int N = a.N, K = a.K, M = a.M;
+  uint32_t csz;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(csz));
+  const int S = (int)csz;
+  const int q = (int)cluster_ctarank();
+  const int row0 = (int)(blockIdx.x / csz) * kRowsW, m0 = blockIdx.y * NB;
+  const int nkt_all = ceil_div(K, kKT), nss_all = ceil_div(nkt_all, kSS);
+  const int ss0 = (q * nss_all) / S, ss1 = ((q + 1) * nss_all) / S;
+  const int kt0 = ss0 * kSS, kt1 = min(ss1 * kSS, nkt_all);
+  const int nkt = max(0, kt1 - kt0), nss = ss1 - ss0;
+  const int nat = (q == S - 1) ? ceil_div(a.n_out, kKT) : 0;  // anchor tiles
+  const int ntiles = nkt + nat;
+  const TmSmem L = tm_smem_layout(NB, G, ceil_div(nss_all, S) * kSS);
+  uint8_t* const codes = smem + L.codes;
+  uint8_t* const xt = smem + L.xt;
+  const uint8_t* const scl = smem + L.scl;
+  uint32_t* const sel = reinterpret_cast<uint32_t*>(smem + L.sel);
+  uint32_t* const amask = reinterpret_cast<uint32_t*>(smem + L.amask);
+  const uint32_t full1 = smem_u32(smem + L.bars), empty1 = full1 + 8 * kNS1;
+  const uint32_t xfull = empty1 + 8 * kNS1, xempty = xfull + 8 * kMaxNX;
+  const uint32_t afull = xempty + 8 * kMaxNX, aempty = afull + 8 * kNA;
+  const uint32_t done = aempty + 8 * kNA;
+
+  pdl_trigger();
+  // Selector table in 16 copies (entry v of copy c at word 16 v + c; lane l reads copy l % 16,
+  // so a warp's lookups meet at most two to a bank): byte v of four codes -> the byte-permute
+  // selectors of their two fp16 pairs.
+  for (int i = tid; i < 256 * 16; i += kThr) {
+    const int v = i >> 4;
+    sel[i] = pair_selector(v & 3, (v >> 2) & 3) | (pair_selector((v >> 4) & 3, (v >> 6) & 3) << 16);
+  }
+  for (int i = tid; i < 2 * nkt; i += kThr) amask[i] = 0u;
+  if (tid == 0) {
+    for (int i = 0; i < kNS1; ++i) {
+      mbar_init(full1 + 8 * i, 1);
+      mbar_init(empty1 + 8 * i, kDeq);
+    }
+    for (int i = 0; i < NX; ++i) {
+      mbar_init(xfull + 8 * i, 1);
+      mbar_init(xempty + 8 * i, 1);
+    }
+    for (int i = 0; i < kNA; ++i) {
+      mbar_init(afull + 8 * i, kDeq);
+      mbar_init(aempty + 8 * i, 1);
+    }
+    mbar_init(done, 1);
+    mbar_fence_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(smem + L.tptr), NCOLS);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  // Columns of my K range whose mask is not 1 (the anchors): their weights get the mask value.
+  if (a.mask)
+    for (int k = kt0 * kKT + tid; k < min(kt1 * kKT, K); k += kThr)
+      if (h2f(ldg_u16(a.mask + k)) != 1.0f) atomicOr(&amask[2 * (k / kKT - kt0) + ((k % kKT) >> 5)], 1u << (k & 31));
+  __syncthreads();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L.tptr);
+
+  if (warp == 0) {
+    // Ring 1: codes and scales of super-stage j into slot j % 2.
+    if (lane == 0) {
+      for (int j = 0; j < nss; ++j) {
+        const int sl = j % kNS1;
+        if (j >= kNS1 && !mbar_wait_sleep(empty1 + 8 * sl, (uint32_t)((j / kNS1) - 1) & 1u)) report_wait_failure();
+        mbar_arrive_expect_tx(full1 + 8 * sl, (uint32_t)(kRowsW * 128 + kRowsW * SROW));
+        tma_load_2d(smem_u32(codes + sl * kRowsW * 128), &p.cmap, (ss0 + j) * 128, row0, full1 + 8 * sl);
+        tma_load_2d(smem_u32(scl + sl * kRowsW * SROW), &p.smap, (ss0 + j) * (kSS * kKT / G), row0, full1 + 8 * sl);
+      }
+    }
+    __syncwarp();  // lanes 1-31 wait here, converged, for lane 0's loop (not at the CTA barrier)
+  } else if (warp == 1) {
+    // Ring 2: the x tile of K tile t into slot t % NX, once the MMAs of tile t - NX are done.
+    if (lane == 0) {
+      pdl_wait();  // x is the previous kernel's output
+      int sl = 0;
+      uint32_t ph = 0;
+      for (int t = 0; t < nkt; ++t) {
+        if (t >= NX && !mbar_wait_spin(xempty + 8 * sl, ph ^ 1u)) report_wait_failure();
+        mbar_arrive_expect_tx(xfull + 8 * sl, (uint32_t)(NB * 128));
+        tma_load_2d(smem_u32(xt + sl * NB * 128), &p.xmap, (kt0 + t) * kKT, m0, xfull + 8 * sl);
+        if (++sl == NX) {
+          sl = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // MMA issue: K tile t = four K=16 steps, A from tensor memory, B from the x tile.
+    if (lane == 0) {
+      int xs = 0;
+      uint32_t xph = 0;
+      for (int t = 0; t < ntiles; ++t) {
+        const int as = t & (kNA - 1);
+        if (t < nkt && !mbar_wait_spin(xfull + 8 * xs, xph)) report_wait_failure();
+        if (!mbar_wait_spin(afull + 8 * as, (uint32_t)(t / kNA) & 1u)) report_wait_failure();
+        tc_fence_after_sync();
+        const uint32_t bbase = smem_u32(xt + xs * NB * 128);
+#pragma unroll
+        for (int kk = 0; kk < kKT / 16; ++kk) {
+          const int step = t * (kKT / 16) + kk;     // K=16 step index; accumulator step % NACC
+          tc_mma_f16_ta(tmem + (uint32_t)((step % NACC) * NB), tmem + (uint32_t)(ACOL + 32 * as + 8 * kk),
+                        tc_desc_sw128(bbase + 32 * kk), kIdesc, step >= NACC ? 1u : 0u);
+        }
+        tc_commit(xempty + 8 * xs);
+        tc_commit(aempty + 8 * as);
+        if (++xs == NX) {
+          xs = 0;
+          xph ^= 1u;
+        }
+      }
+      tc_commit(done);
+    }
+    __syncwarp();
+  } else {
+    // Dequant warps.
+    const int dq = warp - 3, h = dq >> 2, quarter = warp & 3;
+    const int r = 32 * quarter + lane;             // the weight row of this thread
+    const int grow = row0 + r;
+    const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+    const __half2 cb01 = __halves2half2(__float2half_rn(a.c0), __float2half_rn(a.c1));
+    const __half2 cb23 = __halves2half2(__float2half_rn(a.c2), __float2half_rn(a.c3));
+    const uint32_t* const selr = sel + (lane & 15);
+    // Software-pipelined: the tensor-memory store of tile t completes while tile t + 1 is
+    // dequantised; its afull arrival follows the wait.
+    int pend = -1;                                   // tile whose store is in flight
+    auto publish = [&](int tp) {
+      tmem_wait_st();
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(afull + 8 * (tp & (kNA - 1)));
+    };
+    for (int t = 0; t < nkt; ++t) {
+      const int j = t >> 3, kt = t & (kSS - 1);
+      const int s1 = j % kNS1, sl = t & (kNA - 1);
+      if (kt == 0 && !mbar_wait_spin(full1 + 8 * s1, (uint32_t)(j / kNS1) & 1u)) report_wait_failure();
+      // 32 codes: bytes [8h, 8h + 8) of 16-byte piece kt of row r (piece c at c ^ (r & 7)).
+      const uint2 cw = *reinterpret_cast<const uint2*>(codes + s1 * kRowsW * 128 + r * 128 + ((kt ^ (r & 7)) << 4) +
+                                                      8 * h);
+      const int grp = G == 64 ? kt : 2 * kt + h;     // scale group within the super-stage
+      const __half sh = *reinterpret_cast<const __half*>(scl + s1 * kRowsW * SROW + r * SROW + 2 * grp);
+      const __half2 s2 = __halves2half2(sh, sh);
+      const __half2 e01 = __hmul2(cb01, s2), e23 = __hmul2(cb23, s2);
+      const uint32_t lut0 = *reinterpret_cast<const uint32_t*>(&e01), lut1 = *reinterpret_cast<const uint32_t*>(&e23);
+      uint32_t o[16];
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        const uint32_t w = b < 4 ? cw.x : cw.y;
+        const uint32_t sv = selr[((w >> (8 * (b & 3))) & 0xFFu) * 16];
+        o[2 * b] = __byte_perm(lut0, lut1, sv & 0xFFFFu);
+        o[2 * b + 1] = __byte_perm(lut0, lut1, sv >> 16);
+      }
+      const uint32_t mb = amask[2 * t + h];
+      if (mb) {                                      // rare: anchor columns (mask 0) or other masks
+        const uint16_t* mrow = a.mask + (kt0 + t) * kKT + 32 * h;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if ((mb >> (2 * i)) & 3u) {
+            const __half2 m2 = __halves2half2(__ushort_as_half(ldg_u16(mrow + 2 * i)),
+                                              __ushort_as_half(ldg_u16(mrow + 2 * i + 1)));
+            __half2 v = *reinterpret_cast<const __half2*>(&o[i]);
+            v = __hmul2(v, m2);
+            o[i] = *reinterpret_cast<const uint32_t*>(&v);
+          }
+        }
+      }
+      if (kt == kSS - 1 || t == nkt - 1) {           // the super-stage's codes are all read
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty1 + 8 * s1);
+      }
+      if (pend >= 0) publish(pend);
+      if (t >= kNA && !mbar_wait_spin(aempty + 8 * sl, (uint32_t)((t / kNA) - 1) & 1u)) report_wait_failure();
+      tmem_st16(tmem + lane_base + (uint32_t)(ACOL + 32 * sl + 16 * h), o);
+      pend = t;
+    }
+    if (pend >= 0) publish(pend);
+    if (nat > 0) pdl_wait();
+    for (int ta = 0; ta < nat; ++ta) {
+      // Anchor tile: A = anchor weights [64 ta + 32 h, +32) of row r; B = x at those anchors.
+      const int t = nkt + ta, sl = t & (kNA - 1), xs = t % NX;
+      if (t >= kNA && !mbar_wait_spin(aempty + 8 * sl, (uint32_t)((t / kNA) - 1) & 1u)) report_wait_failure();
+      if (t >= NX && !mbar_wait_spin(xempty + 8 * xs, (uint32_t)((t / NX) - 1) & 1u)) report_wait_failure();
+      uint32_t o[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j0 = ta * kKT + 32 * h + 2 * i;
+        const uint32_t lo = (grow < N && j0 < a.n_out) ? ldg_u16(a.ovals + (int64_t)grow * a.ldo + j0) : 0u;
+        const uint32_t hi = (grow < N && j0 + 1 < a.n_out) ? ldg_u16(a.ovals + (int64_t)grow * a.ldo + j0 + 1) : 0u;
+        o[i] = lo | (hi << 16);
+      }
+      tmem_st16(tmem + lane_base + (uint32_t)(ACOL + 32 * sl + 16 * h), o);
+      // x rows n < NB at anchors [64 ta, +64): 8 fp16 per 16-byte piece, 128-byte swizzle.
+      for (int i = tid - 3 * 32; i < NB * 8; i += kDeq * 32) {
+        const int n = i >> 3, c = i & 7;
+        uint32_t v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j0 = ta * kKT + 8 * c + 2 * u;
+          const bool mok = m0 + n < M;
+          const uint32_t lo = (mok && j0 < a.n_out) ? ldg_u16(a.x + (int64_t)(m0 + n) * a.ldx + __ldg(a.oidx + j0)) : 0u;
+          const uint32_t hi =
+              (mok && j0 + 1 < a.n_out) ? ldg_u16(a.x + (int64_t)(m0 + n) * a.ldx + __ldg(a.oidx + j0 + 1)) : 0u;
+          v[u] = lo | (hi << 16);
+        }
+        *reinterpret_cast<uint4*>(xt + xs * NB * 128 + n * 128 + ((c ^ (n & 7)) << 4)) = make_uint4(v[0], v[1], v[2], v[3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tmem_wait_st();
+      tc_fence_before_sync();
+      named_barrier_sync(1, kDeq * 32);              // every x row of the tile is written
+      if (lane == 0) mbar_arrive(afull + 8 * sl);
+    }
+  }
+
+  // Epilogue: the dequant warps read the accumulator (their own 32 lanes, half the columns each).
+  auto finish = [&](int row, int m, float acc) {
+    if (row < N && m < M) {
+      float yv = acc;
+      if (a.bias) yv += h2f(ldg_u16(a.bias + row));
+      if (a.res) yv += h2f(ldg_u16(a.res + (int64_t)m * a.ldr + row));
+      if (a.clamp) yv = fminf(fmaxf(yv, -65504.0f), 65504.0f);
+      a.y[(int64_t)m * a.ldy + row] = f2h(yv);
+    }
+  };
+  const bool deq = warp >= 3;
+  const int h = (warp - 3) >> 2, quarter = warp & 3;
+  const int lrow = 32 * quarter + lane;
+  // Columns c0..c0+7 of this thread's row, summed over the accumulators (0 without MMAs).
+  auto acc_ld8 = [&](int c0, float (&acc)[8]) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+#pragma unroll
+    for (int u = 0; u < NACC; ++u) {
+      uint32_t v[8];
+      tmem_ld8(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(u * NB + c0), v);
+      tmem_wait_ld();
+      if (ntiles > 0)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += __uint_as_float(v[j]);
+    }
+  };
+  pdl_wait();  // every thread that stores y or reads the residual waits for the previous kernel
+  if (deq) {
+    if (ntiles > 0 && !mbar_wait_spin(done, 0u)) report_wait_failure();
+    tc_fence_after_sync();
+  }
+  if (S == 1) {
+    if (deq) {
+#pragma unroll 1
+      for (int c0 = h * (NB / 2); c0 < (h + 1) * (NB / 2); c0 += 8) {
+        float acc[8];
+        acc_ld8(c0, acc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) finish(row0 + lrow, m0 + c0 + j, acc[j]);
+      }
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    if (warp == 2) tmem_dealloc(tmem, NCOLS);
+  } else {
+    // Every CTA of the cluster is past its last MMA before the x area is reused: partials of
+    // row r go to CTA r / (128/S) as recv[source][owned row][column] fp32.
+    cluster_sync_all();
+    const int rows_own = kRowsW / S;
+    float* recv = reinterpret_cast<float*>(xt);
+    if (deq) {
+      const int owner = lrow / rows_own;
+#pragma unroll 1
+      for (int c0 = h * (NB / 2); c0 < (h + 1) * (NB / 2); c0 += 8) {
+        float acc[8];
+        acc_ld8(c0, acc);
+        uint32_t v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __float_as_uint(acc[j]);
+        const uint32_t dst = smem_u32(recv + ((q * rows_own + (lrow - owner * rows_own)) * NB + c0));
+        const uint32_t rdst = mapa_shared(dst, (uint32_t)owner);
+        asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rdst), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+                     "r"(v[3]) : "memory");
+        asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rdst + 16), "r"(v[4]), "r"(v[5]),
+                     "r"(v[6]), "r"(v[7]) : "memory");
+      }
+    }
+    tc_fence_before_sync();
+    cluster_sync_all();
+    if (warp == 2) tmem_dealloc(tmem, NCOLS);
+    for (int i = tid; i < rows_own * NB; i += kThr) {
+      const int rr = i / NB, c = i - rr * NB;
+      float acc = 0.0f;
+      for (int src = 0; src < S; ++src) acc += recv[(src * rows_own + rr) * NB + c];
+      finish(row0 + q * rows_own + rr, m0 + c, acc);
+    }
+  }
+}
+
 // Portable CUDA-core kernel: any M, any G dividing K with G % 4 == 0, any codebook.
 // One warp per output row, lanes stride over packed bytes; MT activation rows per launch.
 template <int MT>
@@ -1711,6 +2095,67 @@ static int launch_gemm_tc(const LinearArgs& a, cudaStream_t st) {
                                    (unsigned)S, a));
 }
 
+bool encode_tiled_2d(void* map, int elem_bytes, const void* base, uint64_t inner, uint64_t rows, uint64_t row_bytes,
+                     uint32_t box_inner, uint32_t box_rows, bool swizzle128);  // capi.cu
+
+// The tensor-memory GEMM (k_gemm2b_tmem) for activation rows 9.. and the layers it takes:
+// symmetric, G = 32 or 64, 16-byte aligned code, scale and activation rows (tensor copies).
+constexpr int kTmMinRows = 9;
+static bool tm_variant(const LinearArgs& a) {
+  const auto al = [](const void* p, int n) { return reinterpret_cast<uintptr_t>(p) % n == 0; };
+  return !a.zeros && (a.G == 32 || a.G == 64) && a.xop == OTF_XOP_NONE && al(a.packed, 16) && a.ldp % 16 == 0 &&
+         al(a.scales, 16) && (a.lds * 2) % 16 == 0 && al(a.x, 16) && (a.ldx * 2) % 16 == 0 &&
+         (!a.mask || al(a.mask, 2)) && a.K % 8 == 0;
+}
+
+template <int G, int NB>
+static int launch_gemm_tmem(const LinearArgs& a, cudaStream_t st) {
+  static thread_local int configured_dev[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured_dev[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm2b_tmem<G, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return set_cuda_error(e);
+    configured_dev[dev] = 1;
+  }
+  // Split K over a cluster of S in {1, 2, 4} CTAs (whole super-stages) while the grid stays
+  // within two CTAs per SM and every CTA keeps at least two super-stages.
+  const int rt = ceil_div(a.N, tm::kRowsW), bt = ceil_div(a.M, NB);
+  const int nss = ceil_div(ceil_div(a.K, tm::kKT), tm::kSS);
+  int S = 1;
+  while (S < 4 && (int64_t)rt * bt * S * 2 <= 2 * num_sms() && nss >= 4 * S) S *= 2;
+  const int64_t smem = tm_smem_layout(NB, G, ceil_div(nss, S) * tm::kSS).total + 1024;
+  if (smem > 227 * 1024) return OTF_ERR_UNSUPPORTED;
+  static thread_local TmParams p;  // three tensor maps + arguments, kept off the stack
+  if (!encode_tiled_2d(&p.cmap, 1, a.packed, (uint64_t)(a.K / 4), (uint64_t)a.N, (uint64_t)a.ldp, 128u,
+                       (uint32_t)tm::kRowsW, true) ||
+      !encode_tiled_2d(&p.smap, 2, a.scales, (uint64_t)(a.K / G), (uint64_t)a.N, (uint64_t)(a.lds * 2),
+                       (uint32_t)(tm::kSS * tm::kKT / G), (uint32_t)tm::kRowsW, false) ||
+      !encode_tiled_2d(&p.xmap, 2, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)(a.ldx * 2), (uint32_t)tm::kKT,
+                       (uint32_t)NB, true))
+    return OTF_ERR_UNSUPPORTED;
+  p.a = a;
+  const dim3 grid((unsigned)(rt * S), (unsigned)bt);
+  return set_cuda_error(launch_pdl(k_gemm2b_tmem<G, NB>, grid, dim3(tm::kThr), (size_t)smem, st, (unsigned)S, p));
+}
+
+template <int G>
+static int launch_tmem_g(const LinearArgs& a, cudaStream_t s) {
+  if (a.M <= 16) return launch_gemm_tmem<G, 16>(a, s);
+  if (a.M <= 32) return launch_gemm_tmem<G, 32>(a, s);
+  if (a.M <= 64) return launch_gemm_tmem<G, 64>(a, s);
+  if (a.M <= 128) return launch_gemm_tmem<G, 128>(a, s);
+  return launch_gemm_tmem<G, 256>(a, s);
+}
+
+static int launch_tmem(const LinearArgs& a, cudaStream_t s) {
+  switch (a.G) {
+    case 32: return launch_tmem_g<32>(a, s);
+    case 64: return launch_tmem_g<64>(a, s);
+    default: return OTF_ERR_UNSUPPORTED;
+  }
+}
+
 static int launch_generic(const LinearArgs& a, cudaStream_t st) {
   const int ctas = ceil_div(a.N, 8);
   for (int m0 = 0; m0 < a.M; m0 += 4) {
@@ -1879,8 +2324,12 @@ extern "C" OTF_API int otf2b_linear(const void* x, int64_t ldx, const uint8_t* p
   if (st != OTF_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = OTF_ERR_UNSUPPORTED;
+  // Nine rows and more: the tensor-memory tcgen05 GEMM when the layer qualifies.
+  if (a.M >= kTmMinRows && !(flags & OTF_FLAG_FORCE_GENERIC) && tm_variant(a)) rc = launch_tmem(a, s);
   const int Gt = (a.M >= kTcMinRows && !(flags & OTF_FLAG_FORCE_GENERIC)) ? tc_variant(a) : 0;
-  if (Gt != 0) {
+  if (rc != OTF_ERR_UNSUPPORTED) {
+    // done
+  } else if (Gt != 0) {
     rc = launch_tc(a, Gt, s);
   } else if (a.M == 1) {
     rc = launch_fast(a, fast_variant(a, flags), s);
@@ -1919,6 +2368,10 @@ extern "C" OTF_API int otf2b_gemm_mma(const void* x, int64_t ldx, const uint8_t*
   if (st != OTF_OK) return st;
   st = check_device();
   if (st != OTF_OK) return st;
+  if (tm_variant(a) && !(flags & OTF_FLAG_FORCE_GENERIC)) {
+    const int rc = launch_tmem(a, static_cast<cudaStream_t>(stream));
+    if (rc != OTF_ERR_UNSUPPORTED) return rc;
+  }
   const int G = tc_variant(a);
   if (G == 0) return OTF_ERR_UNSUPPORTED;
   return launch_tc(a, G, static_cast<cudaStream_t>(stream));
