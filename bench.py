@@ -159,6 +159,41 @@ def cpu_reference_sample(cfg, target_s: float, threads: int = 0):
     return nbytes / el / 1e9, cores, f"{reps} layer(s) x 7 projections of the stack, CPU LUT-dequant + matmul", el
 
 
+def cpu_decode_sample(dec, layers, cfg, w8, sc, start: int, tokens, target_s: float):
+    """Time the reference engine's decode step restated on the host cores (oracle.decode:
+    LUT dequant + matmul per projection, fp32 attention, INT8 head) on the model the GPU just
+    decoded.  The CPU continues from position ``start`` on a copy of the GPU run's KV cache of
+    the prompt, fed the GPU's first generated token, and decodes greedily until ``target_s``
+    has passed (at most 64 tokens).  Returns the cpu_baseline object."""
+    import numpy as np
+    from oracle import decode, oracle
+    oracle.set_num_threads(os.cpu_count() or 1)
+    cores = oracle.num_threads()
+    ones = np.ones(cfg.hidden, np.float16)
+    cl = [{n: decode.projection_of(m) for n, m in l.items()} for l in layers]
+    w8h, sch = w8.cpu().numpy(), sc.cpu().numpy()
+    cpu = decode.Decoder(cl, [(ones, ones)] * cfg.layers, ones, w8h, sch, w8h, sch, heads=cfg.heads,
+                         kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, rope_theta=cfg.rope_theta,
+                         rms_eps=cfg.rms_eps, max_pos=start + 65)
+    for li in range(cfg.layers):
+        cpu.set_cache(li, dec.kc[li][:start].cpu().numpy(), dec.vc[li][:start].cpu().numpy())
+    tok, picks = int(tokens[0]), []
+    t0 = time.perf_counter()
+    while True:
+        tok = int(oracle.argmax_rows(cpu.step(tok, start + len(picks))[None])[0])
+        picks.append(tok)
+        el = time.perf_counter() - t0
+        if el >= target_s or len(picks) >= 64:
+            break
+    same = sum(1 for i, t in enumerate(picks) if i + 1 < len(tokens) and int(tokens[i + 1]) == t)
+    n = len(picks)
+    return {"value": round(n / el, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{n} greedy decode steps of the same model at positions {start}..{start + n - 1} on a copy of "
+                      f"the GPU run's {start}-position KV cache, the reference engine's step restated on the host "
+                      f"(LUT dequant + matmul per projection, fp32 attention, INT8 head); {el:.1f} s",
+            "picks_equal_to_gpu": f"{same} of {n}"}
+
+
 def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -579,6 +614,9 @@ def run_e2e(args):
             "gpu_launches_per_step": (11 * cfg.layers + 4) if Bt > 1 else (5 * cfg.layers + 5 + (1 if peer_ar is not None else 0)),
             "clocks": clk.summary(), "device_error": _native.device_error(),
             "first_tokens": [int(t) for t in out[:8, 0].cpu()]}
+    if rank == 0 and world == 1 and Bt == 1 and base is LLAMA32_3B and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_decode_sample(dec, layers, cfg, w8, sc, P, out[:, 0].cpu().tolist(),
+                                                 args.cpu_seconds)
     dec.graph = None
     if world > 1:
         torch.cuda.synchronize()
