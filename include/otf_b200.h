@@ -112,10 +112,13 @@ OTF_API int otf2b_linear(const void* x, int64_t ldx,
 /*
  * Batched and prefill 2-bit linear on the 5th-generation tensor cores: same arguments,
  * layouts and semantics as otf2b_linear, any M >= 1, any codebook.  The weights are
- * dequantised per 64-code tile to fp16 exactly as the reference's LUT path does
- * (fp16(c[q] * s), or fp32 s*c[q] + z rounded to fp16 for the asymmetric layout) and
- * multiplied by tcgen05.mma (fp32 accumulation in tensor memory); the fp16 anchors are
- * extra K tiles of the same accumulation.  otf2b_linear routes M >= 32 here by itself.
+ * dequantised to fp16 exactly as the reference's LUT path does (fp16(c[q] * s), or fp32
+ * s*c[q] + z rounded to fp16 for the asymmetric layout) and multiplied by tcgen05.mma
+ * (fp32 accumulation in tensor memory).  Symmetric layers with G in {32, 64} write the
+ * dequantised weights into tensor memory and feed them as the MMA's A operand (TMA brings
+ * codes, scales and x); the others stage fp16 tiles in shared memory.  The fp16 anchors
+ * are extra K tiles of the same accumulation.  otf2b_linear routes M >= 9 here by itself
+ * (the tensor-memory form; the shared-memory form from M >= 32).
  * Needs 16-byte aligned x rows (ldx % 8 == 0), code rows (ld_packed % 16 == 0) and mask,
  * even scale strides and G in {32, 64, 128, 256}; OTF_ERR_UNSUPPORTED otherwise.
  * Replaces: the LUT dequant + torch matmul of triton_symmetric_2bit_gemm for M > 1
