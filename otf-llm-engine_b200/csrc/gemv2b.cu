@@ -201,12 +201,21 @@ __device__ __forceinline__ float gemv_stage_x(const LinearArgs& a, const XSlice&
   // Anchor columns (independent of the predecessor): thread j < n_out holds column j.
   int kcol = 0;
   if (tid < a.n_out) kcol = (int)__ldg(a.oidx + tid);
+  const bool norm = a.xop == OTF_XOP_RMSNORM;
+  const bool ar_cons = a.ar_mode == OTF_AR_CONSUME;
+  // RMSNorm weight and mask of this thread's first 8-value piece of the slice: constants, so
+  // they are requested before the wait and the normalising pass below reads registers.
+  const uint4 kOnes4 = make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);
+  uint4 w_pre = kOnes4, m_pre = kOnes4;
+  if (norm && tid < c.nbs * BLK / 8) {
+    if (a.xaux) w_pre = __ldg(reinterpret_cast<const uint4*>(a.xaux + c.kbeg) + tid);
+    if (a.mask) m_pre = __ldg(reinterpret_cast<const uint4*>(a.mask + c.kbeg) + tid);
+  }
   // Weights, scales and bias are in flight; from here on we read the predecessor's output.
   pdl_wait();
   if (fin_ok && a.res) ep += h2f(ldg_u16(a.res + frow));
   // Tensor-parallel consumer: x is the sum of every rank's rows in the receive buffer,
   // each word polled until it carries this exchange's tag (bounded per thread).
-  const bool ar_cons = a.ar_mode == OTF_AR_CONSUME;
   const unsigned ar_tg = ar_cons ? ar_tag(a.ar, a.ar_buf) : 0u;
   uint32_t ar_budget = kArSpinLimit;
   int ar_err = 0;
@@ -220,11 +229,44 @@ __device__ __forceinline__ float gemv_stage_x(const LinearArgs& a, const XSlice&
   }
   ld_u16_pred(xaux_k, a.xaux + kcol, tid < a.n_out && a.xaux != nullptr && a.xop != OTF_XOP_NONE);
   // Stage my slice of x (fp16); padded tail = 0.  The SiLU gate and the mask apply on the
-  // way in; RMSNorm first needs the sum of squares of all K, combined across the cluster
-  // (the K slices partition K) over distributed shared memory, then a second pass.
-  const bool norm = a.xop == OTF_XOP_RMSNORM;
+  // way in; RMSNorm first needs the sum of squares of all K, then a second pass.  Every CTA
+  // sums the squares of the whole vector itself (the extra reads hit L2 and travel with the
+  // slice's), so no cluster exchange sits in the chain; the tensor-parallel consumer, whose x
+  // is a sum over the ranks' buffers, combines its slices' partial sums across the cluster.
+  const bool ssq_local = norm && !ar_cons;
   float ssq = 0.0f;
-  {
+  if (ssq_local) {
+    // The slice pieces this thread stages (v = t, t + 256) are requested first, then the whole
+    // vector in the same fixed thread order in every CTA (pieces t, t + 256, ...), so all loads
+    // are in flight together and every CTA sums the squares in one order (the same rnorm bits).
+    const uint4* xsl = reinterpret_cast<const uint4*>(a.x + c.kbeg);
+    const uint4* xall = reinterpret_cast<const uint4*>(a.x);
+    const int nv = a.K / 8, nsl = c.nbs * BLK / 8;
+    const uint4 z4 = make_uint4(0, 0, 0, 0);
+    const uint4 s0 = tid < nsl ? __ldg(xsl + tid) : z4;
+    const uint4 s1 = tid + kCThreads < nsl ? __ldg(xsl + tid + kCThreads) : z4;
+    for (int v = tid; v < nv; v += 2 * kCThreads) {
+      const uint4 x0 = __ldg(xall + v);
+      const uint4 x1 = v + kCThreads < nv ? __ldg(xall + v + kCThreads) : z4;
+      const __half2* h0 = reinterpret_cast<const __half2*>(&x0);
+      const __half2* h1 = reinterpret_cast<const __half2*>(&x1);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h0[i]);
+        ssq = fmaf(f.x, f.x, fmaf(f.y, f.y, ssq));
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h1[i]);
+        ssq = fmaf(f.x, f.x, fmaf(f.y, f.y, ssq));
+      }
+    }
+    uint4* xsd = reinterpret_cast<uint4*>(c.xs);
+    if (tid < c.nbs_pad * BLK / 8) xsd[tid] = s0;
+    if (tid + kCThreads < c.nbs_pad * BLK / 8) xsd[tid + kCThreads] = s1;
+    for (int v = tid + 2 * kCThreads; v < c.nbs_pad * BLK / 8; v += kCThreads) xsd[v] = v < nsl ? __ldg(xsl + v) : z4;
+  }
+  if (!ssq_local) {
     const uint4* xsrc = reinterpret_cast<const uint4*>(a.x + c.kbeg);
     for (int v = tid; v < c.nbs_pad * BLK / 8; v += kCThreads) {
       uint4 xv = make_uint4(0, 0, 0, 0);
@@ -270,26 +312,33 @@ __device__ __forceinline__ float gemv_stage_x(const LinearArgs& a, const XSlice&
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ssq += __shfl_xor_sync(0xffffffffu, ssq, o);
     if (lane == 0) c.nrm[kMaxCluster + warp] = ssq;
-    named_barrier_sync(1, kCThreads);
-    if (tid == 0) {
-      float part = 0.0f;
-      for (int w = 0; w < kCWarps; ++w) part += c.nrm[kMaxCluster + w];
-      for (int q = 0; q < c.S; ++q) st_cluster_f32_plain(mapa_shared(smem_u32(c.nrm + c.rank), (uint32_t)q), part);
-    }
-    cluster_sync_all();
     float tot = 0.0f;
-    for (int q = 0; q < c.S; ++q) tot += c.nrm[q];
+    if (ssq_local) {
+      named_barrier_sync(1, kCThreads);
+      for (int w = 0; w < kCWarps; ++w) tot += c.nrm[kMaxCluster + w];
+    } else {
+      named_barrier_sync(1, kCThreads);
+      if (tid == 0) {
+        float part = 0.0f;
+        for (int w = 0; w < kCWarps; ++w) part += c.nrm[kMaxCluster + w];
+        for (int q = 0; q < c.S; ++q) st_cluster_f32_plain(mapa_shared(smem_u32(c.nrm + c.rank), (uint32_t)q), part);
+      }
+      cluster_sync_all();
+      for (int q = 0; q < c.S; ++q) tot += c.nrm[q];
+    }
     rnorm = rsqrtf(tot / (float)a.K + a.eps);
     for (int v = tid; v < c.nbs * BLK / 8; v += kCThreads) {
       uint4 xv = reinterpret_cast<uint4*>(c.xs)[v];
       __half* e = reinterpret_cast<__half*>(&xv);
-      uint4 wv = make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);  // ones
-      if (a.xaux) wv = __ldg(reinterpret_cast<const uint4*>(a.xaux + c.kbeg) + v);
+      uint4 wv = w_pre, mv = m_pre;                // ones where there is no weight / mask
+      if (v != tid) {
+        if (a.xaux) wv = __ldg(reinterpret_cast<const uint4*>(a.xaux + c.kbeg) + v);
+        if (a.mask) mv = __ldg(reinterpret_cast<const uint4*>(a.mask + c.kbeg) + v);
+      }
       const __half* wh = reinterpret_cast<const __half*>(&wv);
 #pragma unroll
       for (int i = 0; i < 8; ++i) e[i] = __hmul(wh[i], __float2half_rn(__half2float(e[i]) * rnorm));
       if (a.mask) {
-        const uint4 mv = __ldg(reinterpret_cast<const uint4*>(a.mask + c.kbeg) + v);
         __half2* xh = reinterpret_cast<__half2*>(&xv);
         const __half2* mh = reinterpret_cast<const __half2*>(&mv);
 #pragma unroll
