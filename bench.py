@@ -521,7 +521,10 @@ def run_e2e(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         pg = dist.group.WORLD
     peer_ar = None
-    if world > 1 and args.tp_exchange == "peer":
+    Bt = args.e2e_batch
+    # the fused peer exchange lives in the batch-1 grouped launches; batched steps use NCCL
+    exchange = (args.tp_exchange if Bt == 1 else "nccl") if world > 1 else None
+    if exchange == "peer":
         from otf_llm.tp_allreduce import PeerAllReduce
         peer_ar = PeerAllReduce(cfg.hidden, group=pg, device=dev)
     std = 0.015 if base is LLAMA3_70B else 0.02
@@ -554,12 +557,10 @@ def run_e2e(args):
         head = QuantizedLinearHead(cfg.hidden, r1 - r0)
     emb.weight_int8, emb.scales = w8, sc
     head.weight_int8, head.scales = w8[r0:r1], sc[r0:r1]
-    Bt = args.e2e_batch
     if Bt > 1:
-        if world > 1:
-            raise SystemExit("--e2e-batch > 1 runs on one GPU")
         from otf_llm.decode_model import BatchedGreedyDecoder
-        dec = BatchedGreedyDecoder(cfg, layers, [(ones, ones)] * cfg.layers, emb, head, ones, dev, Bt)
+        dec = BatchedGreedyDecoder(cfg, layers, [(ones, ones)] * cfg.layers, emb, head, ones, dev, Bt, rank=rank,
+                                   world=world, process_group=pg, head_row0=r0)
     else:
         dec = GreedyDecoder(cfg, layers, [(ones, ones)] * cfg.layers, emb, head, ones, dev, rank=rank, world=world,
                             process_group=pg, peer_ar=peer_ar, head_row0=r0)
@@ -610,7 +611,7 @@ def run_e2e(args):
                        "intermediate": cfg.intermediate, "heads": cfg.heads, "kv_heads": cfg.kv_heads,
                        "vocab": cfg.vocab, "rope": "default, theta 5e5", "group_size": 64, "outlier_ratio": 0.005,
                        "parallelism": f"tp{world}" if world > 1 else "single",
-                       "tp_exchange": args.tp_exchange if world > 1 else None},
+                       "tp_exchange": exchange},
             "gpu_launches_per_step": (11 * cfg.layers + 4) if Bt > 1 else (5 * cfg.layers + 5 + (1 if peer_ar is not None else 0)),
             "clocks": clk.summary(), "device_error": _native.device_error(),
             "first_tokens": [int(t) for t in out[:8, 0].cpu()]}
@@ -699,7 +700,7 @@ def main():
     ap.add_argument("--e2e", action="store_true", help="greedy decode of a Llama-3.2-3B-architecture 2-bit model")
     ap.add_argument("--e2e-model", choices=("llama3.2-3b", "llama3-70b"), default="llama3.2-3b")
     ap.add_argument("--e2e-prompt", type=int, default=512)
-    ap.add_argument("--e2e-batch", type=int, default=1, help="sequences decoded in lockstep (one GPU)")
+    ap.add_argument("--e2e-batch", type=int, default=1, help="sequences decoded in lockstep (tensor-parallel batches exchange by NCCL)")
     ap.add_argument("--e2e-layers", type=int, default=0,
                     help="decoder layers of the e2e model (default: the architecture's; fewer for a profiling case)")
     ap.add_argument("--e2e-tokens", type=int, default=256)

@@ -298,40 +298,56 @@ class BatchedGreedyDecoder:
     moves every sequence by one position.  Per layer: RMSNorm, q/k/v, batched RoPE + KV-cache
     write + attention (each sequence its own caches and position), o + residual, RMSNorm,
     gate/up, SiLU gate, down + residual; the 2-bit projections run with M = batch rows (the
-    batched integer-MMA kernel up to 8 rows per weight pass, the tcgen05 GEMM from 32).  The
-    reference has no batched decoder; HF's generate with a padded batch does the same math."""
+    batched integer-MMA kernel up to 8 rows per weight pass, the tensor-memory tcgen05 GEMM
+    from 9).  Under tensor parallelism (``world`` > 1, layers from ``shard_layers``) each rank
+    runs its query / KV heads, gate/up rows and o/down K slices; o and down write partial sums
+    (rank 0 adds the residual) that one NCCL all-reduce per projection sums, and the INT8 head
+    is vocabulary-parallel (rows from ``head_row0``), each sequence's greedy pick one all-gather
+    of (max logit, global row) pairs.  The reference has no batched decoder; HF's generate with a
+    padded batch does the same math."""
 
     def __init__(self, cfg: ModelConfig, layers: Sequence[Dict[str, SymmetricOTF2BitLinear]],
                  norms: Sequence[Tuple[torch.Tensor, torch.Tensor]], embed: QuantizedEmbedding,
-                 head: QuantizedLinearHead, final_norm: Optional[torch.Tensor], device, batch: int):
+                 head: QuantizedLinearHead, final_norm: Optional[torch.Tensor], device, batch: int, *,
+                 rank: int = 0, world: int = 1, process_group=None, head_row0: int = 0):
         dev = torch.device(device)
         B = int(batch)
         if B < 1:
             raise ValueError("batch must be >= 1")
         self.cfg, self.device, self.batch = cfg, dev, B
+        self.rank, self.world, self.pg, self.head_row0 = rank, world, process_group, int(head_row0)
         self.layers = [dict(l) for l in layers]
         for l in self.layers:
             missing = [n for n in PROJ if n not in l]
             if missing:
                 raise ValueError(f"decoder layer lacks {missing}")
+        l0 = self.layers[0]
+        self.heads = l0["q_proj"].out_features // cfg.head_dim      # this rank's query / KV heads
+        self.kv_heads = l0["k_proj"].out_features // cfg.head_dim
+        if world == 1 and (self.heads, self.kv_heads) != (cfg.heads, cfg.kv_heads):
+            raise ValueError("q/k projections do not match the configured head counts")
         f16 = dict(dtype=torch.float16, device=dev)
         self.in_norms = [a.to(**f16).contiguous() for a, _ in norms]
         self.post_norms = [b.to(**f16).contiguous() for _, b in norms]
         self.embed, self.head = embed, head
         self.final_norm = (final_norm if final_norm is not None else torch.ones(cfg.hidden)).to(**f16).contiguous()
-        qd, kvd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+        qd, kvd = self.heads * cfg.head_dim, self.kv_heads * cfg.head_dim
         self.kc = [torch.zeros(B, cfg.max_pos, kvd, **f16) for _ in self.layers]
         self.vc = [torch.zeros(B, cfg.max_pos, kvd, **f16) for _ in self.layers]
         self.cos_sin = rope_table(cfg, dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
         self.ids = torch.zeros(B, dtype=torch.int64, device=dev)
-        n = _native.lib().otf_attn_workspace_bytes_batch(cfg.kv_heads, cfg.head_dim, cfg.max_pos, B)
+        n = _native.lib().otf_attn_workspace_bytes_batch(self.kv_heads, cfg.head_dim, cfg.max_pos, B)
         self.attn_ws = torch.zeros(int(n), dtype=torch.uint8, device=dev)
         inter = self.layers[0]["gate_proj"].out_features
         self.b = {n_: torch.zeros(B, w, **f16) for n_, w in (("h", cfg.hidden), ("h1", cfg.hidden), ("xn", cfg.hidden),
                                                                ("q", qd), ("k", kvd), ("v", kvd), ("attn", qd),
                                                                ("g", inter), ("u", inter), ("a", inter))}
         self.logits = torch.zeros(B, head.weight_int8.shape[0], dtype=torch.float32, device=dev)
+        if world > 1:
+            self.loc_idx = torch.zeros(B, dtype=torch.int64, device=dev)
+            self.pairs = torch.zeros(world * B, 2, dtype=torch.float64, device=dev)
+            self.seq = torch.arange(B, device=dev)
         self.graph = None
 
     @staticmethod
@@ -345,8 +361,9 @@ class BatchedGreedyDecoder:
     def _step(self) -> None:
         cfg, b, L, B = self.cfg, self.b, _native.lib(), self.batch
         st = _native._stream(self.device)
+        tp, lead = self.world > 1, self.rank == 0
         b["h"].copy_(self.embed(self.ids).view(B, -1))
-        kvd = cfg.kv_heads * cfg.head_dim
+        kvd = self.kv_heads * cfg.head_dim
         for li, layer in enumerate(self.layers):
             _native.rmsnorm(b["h"], self.in_norms[li], cfg.rms_eps, out=b["xn"])
             for n, o in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v")):
@@ -354,20 +371,35 @@ class BatchedGreedyDecoder:
             _native._check(L.otf_attn_rope_decode_batch(
                 b["q"].data_ptr(), b["q"].stride(0), b["k"].data_ptr(), b["v"].data_ptr(), b["k"].stride(0),
                 self.cos_sin.data_ptr(), self.pos.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
-                cfg.max_pos * kvd, b["attn"].data_ptr(), b["attn"].stride(0), 1.0 / math.sqrt(cfg.head_dim), cfg.heads,
-                cfg.kv_heads, cfg.head_dim, cfg.max_pos, B, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
+                cfg.max_pos * kvd, b["attn"].data_ptr(), b["attn"].stride(0), 1.0 / math.sqrt(cfg.head_dim), self.heads,
+                self.kv_heads, cfg.head_dim, cfg.max_pos, B, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
                 "otf_attn_rope_decode_batch")
-            self._lin(layer["o_proj"], b["attn"], b["h1"], residual=b["h"])
+            # row-parallel o / down: partial sums, the residual on rank 0 only, then one all-reduce
+            self._lin(layer["o_proj"], b["attn"], b["h1"], residual=b["h"] if lead else None)
+            if tp:
+                torch.distributed.all_reduce(b["h1"], group=self.pg)
             _native.rmsnorm(b["h1"], self.post_norms[li], cfg.rms_eps, out=b["xn"])
             self._lin(layer["gate_proj"], b["xn"], b["g"])
             self._lin(layer["up_proj"], b["xn"], b["u"])
             _native.silu_mul(b["g"], b["u"], out=b["a"])
-            self._lin(layer["down_proj"], b["a"], b["h"], residual=b["h1"])
+            self._lin(layer["down_proj"], b["a"], b["h"], residual=b["h1"] if lead else None)
+            if tp:
+                torch.distributed.all_reduce(b["h"], group=self.pg)
         _native.rmsnorm(b["h"], self.final_norm, cfg.rms_eps, out=b["xn"])
         w, s = self.head.weight_int8, self.head.scales.reshape(-1)
+        dst = self.loc_idx if tp else self.ids
         _native._check(L.otf_i8_head_argmax(b["xn"].data_ptr(), b["xn"].stride(0), w.data_ptr(), w.stride(0),
                                             s.data_ptr(), self.logits.data_ptr(), self.logits.shape[1],
-                                            self.ids.data_ptr(), B, w.shape[0], w.shape[1], st), "otf_i8_head_argmax")
+                                            dst.data_ptr(), B, w.shape[0], w.shape[1], st), "otf_i8_head_argmax")
+        if tp:
+            # every rank's (max logit, global row) per sequence; the first rank holding the maximum
+            # wins, i.e. the lowest vocabulary index on ties (rows ascend with rank), as torch.argmax
+            vmax = self.logits.gather(1, self.loc_idx.view(B, 1)).to(torch.float64)
+            pair = torch.cat([vmax, (self.loc_idx + self.head_row0).to(torch.float64).view(B, 1)], dim=1)
+            torch.distributed.all_gather_into_tensor(self.pairs, pair, group=self.pg)
+            pr = self.pairs.view(self.world, B, 2)
+            best = torch.argmax(pr[:, :, 0], dim=0)
+            self.ids.copy_(pr[best, self.seq, 1].to(torch.int64))
         _native._check(L.otf_pos_advance_batch(self.pos.data_ptr(), B, st), "otf_pos_advance_batch")
 
     def capture(self) -> None:

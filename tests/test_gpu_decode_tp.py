@@ -145,3 +145,87 @@ def test_tp2_decoder_matches_single_gpu(exchange):
             assert rel_err(lg, ref_logits) < 2e-2, (rank, mode)
             assert np.array_equal(ids, lg.argmax(axis=1)), (rank, mode)   # combined pick = argmax
         assert np.array_equal(out["graph"][0], out["eager"][0]), rank
+
+
+def _teacher_forced_batch(dec, prompts):
+    logits, ids = [], []
+    dec.reset()
+    for i in range(prompts.shape[1]):
+        dec.ids.copy_(prompts[:, i])
+        dec.step()
+        logits.append(dec.logits.clone())
+        ids.append(dec.ids.clone())
+    return torch.stack(logits), torch.stack(ids)            # [T, B, V_rank], [T, B]
+
+
+def _worker_batch(rank, world, port, q):
+    try:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        from otf_llm import _native
+        from otf_llm.decode_model import BatchedGreedyDecoder, shard_layers
+        from otf_llm.decoder_stack import split_bounds
+        cfg, layers, norms, emb, fnorm = _model(dev)
+        B = 3
+        r0, r1 = split_bounds(cfg.vocab, rank, world)
+        dec = BatchedGreedyDecoder(cfg, shard_layers(layers, cfg, rank, world), norms, emb, _head_rows(emb, r0, r1),
+                                   fnorm, dev, B, rank=rank, world=world, process_group=dist.group.WORLD, head_row0=r0)
+        prompts = torch.from_numpy(np.random.default_rng(4).integers(0, cfg.vocab, (B, 10))).to(dev)
+        sizes = [split_bounds(cfg.vocab, r, world)[1] - split_bounds(cfg.vocab, r, world)[0] for r in range(world)]
+        out = {}
+        for mode in ("eager", "graph"):
+            if mode == "graph":
+                dec.capture()
+            lg, ids = _teacher_forced_batch(dec, prompts)
+            parts = [torch.empty(lg.shape[0], B, n, dtype=lg.dtype, device=dev) for n in sizes]
+            dist.all_gather(parts, lg.contiguous())
+            out[mode] = (torch.cat(parts, dim=2).cpu().numpy(), ids.cpu().numpy())
+        torch.cuda.synchronize()
+        err = _native.device_error(clear=True)
+        full = None
+        if rank == 0:
+            one = BatchedGreedyDecoder(cfg, layers, norms, emb, _head_rows(emb, 0, cfg.vocab), fnorm, dev, B)
+            lg, ids = _teacher_forced_batch(one, prompts)
+            full = (lg.cpu().numpy(), ids.cpu().numpy())
+        dec.graph = None
+        dist.barrier()
+        torch.cuda.synchronize()
+        q.put((rank, out, full, err))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, e, None, -1))
+        raise
+
+
+def test_tp2_batched_decoder_matches_single_gpu():
+    """BatchedGreedyDecoder over 2 ranks (NCCL exchange, vocabulary-parallel head): every
+    sequence's teacher-forced logits against the one-GPU batched decoder, the picks the argmax
+    of the gathered logits, graph = eager bit for bit."""
+    import torch.multiprocessing as mp
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_batch, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(world)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=120)
+    for r in res:
+        assert not isinstance(r[1], Exception), r
+    ref_logits, ref_ids = res[0][2]
+    for rank, out, _, err in res:
+        assert err == 0
+        for mode, (lg, ids) in out.items():
+            assert lg.shape == ref_logits.shape
+            assert rel_err(lg, ref_logits) < 2e-2, (rank, mode)
+            assert np.array_equal(ids, lg.argmax(axis=2)), (rank, mode)
+        assert np.array_equal(out["graph"][0], out["eager"][0]), rank
