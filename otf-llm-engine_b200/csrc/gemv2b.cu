@@ -203,12 +203,12 @@ __device__ __forceinline__ float gemv_stage_x(const LinearArgs& a, const XSlice&
   if (tid < a.n_out) kcol = (int)__ldg(a.oidx + tid);
   const bool norm = a.xop == OTF_XOP_RMSNORM;
   const bool ar_cons = a.ar_mode == OTF_AR_CONSUME;
-  // RMSNorm weight and mask of this thread's first 8-value piece of the slice: constants, so
-  // they are requested before the wait and the normalising pass below reads registers.
+  // Mask (and RMSNorm weight) of this thread's first 8-value piece of the slice: constants, so
+  // they are requested before the wait and the staging passes below read registers.
   const uint4 kOnes4 = make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);
   uint4 w_pre = kOnes4, m_pre = kOnes4;
-  if (norm && tid < c.nbs * BLK / 8) {
-    if (a.xaux) w_pre = __ldg(reinterpret_cast<const uint4*>(a.xaux + c.kbeg) + tid);
+  if (tid < c.nbs * BLK / 8) {
+    if (norm && a.xaux) w_pre = __ldg(reinterpret_cast<const uint4*>(a.xaux + c.kbeg) + tid);
     if (a.mask) m_pre = __ldg(reinterpret_cast<const uint4*>(a.mask + c.kbeg) + tid);
   }
   // Weights, scales and bias are in flight; from here on we read the predecessor's output.
@@ -296,7 +296,7 @@ __device__ __forceinline__ float gemv_stage_x(const LinearArgs& a, const XSlice&
             }
           }
           if (a.mask) {
-            const uint4 mv = __ldg(reinterpret_cast<const uint4*>(a.mask + c.kbeg) + v);
+            const uint4 mv = v == tid ? m_pre : __ldg(reinterpret_cast<const uint4*>(a.mask + c.kbeg) + v);
             const __half2* mh = reinterpret_cast<const __half2*>(&mv);
 #pragma unroll
             for (int i = 0; i < 4; ++i) xh[i] = __hmul2(xh[i], mh[i]);
