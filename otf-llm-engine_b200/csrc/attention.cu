@@ -12,7 +12,9 @@
 // softmax(q k^T / sqrt(d)) v.  Here the dot products and the softmax run in fp32 (as the
 // fused SDPA kernels do); RoPE rounds like HF's fp16 elementwise ops.
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "otf_common.cuh"
 
@@ -429,6 +431,191 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
   if (threadIdx.x == 0) tickets[g] = 0u;  // re-armed for the next call
 }
 
+// The same fused step with the split merge inside a thread-block cluster: the S CTAs of one KV
+// head (S <= 8, one cluster, split index = cluster rank) each take a contiguous 1/S of the cached
+// positions, and push their (max, sum, weighted values) per query head into rank 0's shared
+// memory over DSMEM; after one cluster barrier rank 0 combines the S partials in rank order.
+// No global partials, fences or tickets sit in the chain.  Also: the query rows are requested
+// together with the position (they do not depend on it), and each warp's first batch of cached
+// rows before the rotations (the new position's row is never read from the cache in this call:
+// its rotated k and its v reach this CTA's warps through shared memory).  Every CTA of a cluster
+// runs the same path to the barrier (an empty range contributes max -inf, sum 0).
+constexpr int kAttnClMax = 8;
+
+template <int PL>
+__device__ __forceinline__ void rope_vals(const uint16_t (&xr)[PL], const uint16_t* cs, int D, int lane, __half (&o)[PL]) {
+#pragma unroll
+  for (int i = 0; i < PL; ++i) {
+    const __half xv = __ushort_as_half(xr[i]);
+    const __half pv = __ushort_as_half((uint16_t)__shfl_xor_sync(0xffffffffu, (int)xr[i], 16));
+    const int dim = lane * PL + i;
+    const __half c = __ushort_as_half(cs[dim]), sn = __ushort_as_half(cs[D + dim]);
+    const __half t = lane < 16 ? __hmul_rn(__hneg(pv), sn) : __hmul_rn(pv, sn);
+    o[i] = __hadd_rn(__hmul_rn(xv, c), t);
+  }
+}
+
+template <int D, int REP>
+__global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode_cl(
+    const uint16_t* q, const uint16_t* knew, const uint16_t* vnew, const uint16_t* cos_sin, const int* pos,
+    uint16_t* kc, uint16_t* vc, uint16_t* out, float scale, int kv_heads, int max_pos, int64_t ldq, int64_t ldkv,
+    int64_t cache_stride, int64_t ldo) {
+  constexpr int PL = D / 32;
+  static_assert(REP >= 1 && REP <= kAttnMaxRep, "query heads per KV head");
+  extern __shared__ __align__(16) float cl_part[];  // rank 0: [S][REP][D + 2] (max, sum, values)
+  __shared__ float sm_m[kAttn2Warps][REP], sm_l[kAttn2Warps][REP];
+  __shared__ float sm_acc[kAttn2Warps][REP][D];
+  __shared__ float s_knew[D], s_vnew[D];
+  pdl_trigger();
+  cluster_arrive_relaxed();  // paired with cluster_wait() before the first DSMEM store
+  pdl_wait();
+  {
+    const int b = blockIdx.z;
+    q += b * ldq;
+    knew += b * ldkv;
+    vnew += b * ldkv;
+    kc += b * cache_stride;
+    vc += b * cache_stride;
+    out += b * ldo;
+    pos += b;
+  }
+  const int S = (int)gridDim.x, sp = (int)blockIdx.x, g = (int)blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint16_t qraw[REP][PL];
+#pragma unroll
+  for (int r = 0; r < REP; ++r)
+#pragma unroll
+    for (int i = 0; i < PL; ++i) qraw[r][i] = q[(int64_t)(g * REP + r) * D + lane * PL + i];
+  const int p = *pos;
+  if (p < 0 || p >= max_pos) {  // the same position for every CTA of the cluster: all leave here
+    if (blockIdx.z == 0) report_bad_position();
+    return;
+  }
+  const int L = p + 1;
+  const int per = (L + S - 1) / S;
+  const int p0 = min(L, sp * per), p1 = min(L, p0 + per);
+  const uint16_t* cs = cos_sin + (int64_t)p * 2 * D;
+  const int64_t stride = (int64_t)kv_heads * D;
+  float kf[kAttn2Batch][PL], vf[kAttn2Batch][PL];
+  auto load_batch = [&](int base) {
+#pragma unroll
+    for (int j = 0; j < kAttn2Batch; ++j) {
+      const int pp = base + j * kAttn2Warps;
+      const int pc = (pp < p1 && pp != p) ? pp : 0;  // row 0 always exists; its values are not used
+      const uint16_t* kr = kc + pc * stride + (int64_t)g * D + lane * PL;
+      const uint16_t* vr = vc + pc * stride + (int64_t)g * D + lane * PL;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) {
+        kf[j][i] = h2f(kr[i]);
+        vf[j][i] = h2f(vr[i]);
+      }
+    }
+  };
+  load_batch(p0 + warp);
+  if (p0 <= p && p < p1 && warp == 0) {
+    __half kr[PL];
+    rope_lane<PL>(knew + (int64_t)g * D, cs, D, lane, kr);
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      const uint16_t vv = vnew[(int64_t)g * D + lane * PL + i];
+      kc[p * stride + (int64_t)g * D + lane * PL + i] = __half_as_ushort(kr[i]);
+      vc[p * stride + (int64_t)g * D + lane * PL + i] = vv;
+      s_knew[lane * PL + i] = __half2float(kr[i]);
+      s_vnew[lane * PL + i] = h2f(vv);
+    }
+  }
+  __syncthreads();  // the new position's k and v are in shared memory
+  float qv[REP][PL];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    __half qr[PL];
+    rope_vals<PL>(qraw[r], cs, D, lane, qr);
+#pragma unroll
+    for (int i = 0; i < PL; ++i) qv[r][i] = __half2float(qr[i]) * scale;
+  }
+  float m[REP], l[REP], acc[REP][PL];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) acc[r][i] = 0.0f;
+  }
+  for (int base = p0 + warp; base < p1; base += kAttn2Warps * kAttn2Batch) {
+    if (base != p0 + warp) load_batch(base);
+#pragma unroll
+    for (int j = 0; j < kAttn2Batch; ++j) {
+      const int pp = base + j * kAttn2Warps;
+      if (pp >= p1) break;
+      if (pp == p) {
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {
+          kf[j][i] = s_knew[lane * PL + i];
+          vf[j][i] = s_vnew[lane * PL + i];
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < REP; ++r) {
+        float d = 0.0f;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) d = fmaf(qv[r][i], kf[j][i], d);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        const float mn = fmaxf(m[r], d);
+        const float corr = __expf(m[r] - mn), w = __expf(d - mn);
+        l[r] = l[r] * corr + w;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) acc[r][i] = fmaf(acc[r][i], corr, w * vf[j][i]);
+        m[r] = mn;
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    if (lane == 0) {
+      sm_m[warp][r] = m[r];
+      sm_l[warp][r] = l[r];
+    }
+#pragma unroll
+    for (int i = 0; i < PL; ++i) sm_acc[warp][r][lane * PL + i] = acc[r][i];
+  }
+  __syncthreads();
+  cluster_wait();  // every CTA of the cluster is running: rank 0's shared memory is live
+  const uint32_t part0 = smem_u32(cl_part) + (uint32_t)(sp * REP * (D + 2)) * 4u;
+  for (int e = threadIdx.x; e < REP * D; e += kAttn2Threads) {
+    const int r = e / D, dd = e - r * D;
+    float mm = -INFINITY;
+    for (int w = 0; w < kAttn2Warps; ++w) mm = fmaxf(mm, sm_m[w][r]);
+    float ll = 0.0f, aa = 0.0f;
+    for (int w = 0; w < kAttn2Warps; ++w) {
+      const float c = sm_m[w][r] == -INFINITY ? 0.0f : __expf(sm_m[w][r] - mm);
+      ll += sm_l[w][r] * c;
+      aa += sm_acc[w][r][dd] * c;
+    }
+    const uint32_t pr = part0 + (uint32_t)(r * (D + 2)) * 4u;
+    st_cluster_f32_plain(mapa_shared(pr + (uint32_t)(2 + dd) * 4u, 0u), aa);
+    if (dd == 0) {
+      st_cluster_f32_plain(mapa_shared(pr, 0u), mm);
+      st_cluster_f32_plain(mapa_shared(pr + 4u, 0u), ll);
+    }
+  }
+  cluster_sync_all();  // every partial has landed in rank 0
+  if (sp != 0) return;
+  for (int e = threadIdx.x; e < REP * D; e += kAttn2Threads) {
+    const int r = e / D, dd = e - r * D;
+    float mm = -INFINITY;
+    for (int q2 = 0; q2 < S; ++q2) mm = fmaxf(mm, cl_part[(q2 * REP + r) * (D + 2)]);
+    float ll = 0.0f, aa = 0.0f;
+    for (int q2 = 0; q2 < S; ++q2) {
+      const float* pq = cl_part + (q2 * REP + r) * (D + 2);
+      const float c = pq[0] == -INFINITY ? 0.0f : __expf(pq[0] - mm);
+      ll += pq[1] * c;
+      aa += pq[2 + dd] * c;
+    }
+    out[(int64_t)(g * REP + r) * D + dd] = f2h(aa / ll);
+  }
+}
+
 __global__ void k_pos_advance(int* pos, int n) {
   pdl_trigger();
   pdl_wait();
@@ -449,6 +636,55 @@ static decltype(&k_attn_rope_decode<D, 0>) attn2_kernel(int64_t rep) {
     case 8: return k_attn_rope_decode<D, 8>;
     default: return k_attn_rope_decode<D, 0>;
   }
+}
+}  // namespace otf
+
+namespace otf {
+// The cluster form of the fused attention for the common query-per-KV-head ratios; null for
+// the others (they keep the ticket-merge kernel).
+template <int D>
+static decltype(&k_attn_rope_decode_cl<D, 1>) attn_cl_kernel(int64_t rep) {
+  switch (rep) {
+    case 1: return k_attn_rope_decode_cl<D, 1>;
+    case 2: return k_attn_rope_decode_cl<D, 2>;
+    case 3: return k_attn_rope_decode_cl<D, 3>;
+    case 4: return k_attn_rope_decode_cl<D, 4>;
+    case 8: return k_attn_rope_decode_cl<D, 8>;
+    default: return nullptr;
+  }
+}
+
+// Launch the cluster form: grid (S, kv_heads, batch), clusters of S along x, S = the split count
+// the ticket form would use at max_pos, at most 8.  Returns false when the ratio has no cluster
+// form (the caller launches the ticket form).
+template <int D>
+static bool launch_attn_cl(int64_t rep, cudaStream_t s, cudaError_t& err, const uint16_t* q, const uint16_t* kn,
+                           const uint16_t* vn, const uint16_t* cs, const int* pp, uint16_t* kc, uint16_t* vc,
+                           uint16_t* o, float scale, int kv_heads, int max_pos, int64_t batch, int64_t ldq,
+                           int64_t ldkv, int64_t cache_stride, int64_t ldo) {
+  auto* k = attn_cl_kernel<D>(rep);
+  if (!k) return false;
+  const int S = (int)std::max<int64_t>(1, std::min<int64_t>(kAttnClMax, (max_pos + kAttnSplitPos - 1) / kAttnSplitPos));
+  const size_t dyn = (size_t)S * rep * (D + 2) * sizeof(float);
+  // The shared-memory opt-in once per kernel, device and size (the first call is an eager one:
+  // the decoders run warm-up steps before they capture a graph).
+  {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int>, size_t> done;
+    int dev = 0;
+    err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return true;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& have = done[std::make_tuple(reinterpret_cast<const void*>(k), dev)];
+    if (have < dyn) {
+      err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+      if (err != cudaSuccess) return true;
+      have = dyn;
+    }
+  }
+  err = launch_pdl(k, dim3((unsigned)S, (unsigned)kv_heads, (unsigned)batch), dim3(kAttn2Threads), dyn, s,
+                   (unsigned)S, q, kn, vn, cs, pp, kc, vc, o, scale, kv_heads, max_pos, ldq, ldkv, cache_stride, ldo);
+  return true;
 }
 }  // namespace otf
 
@@ -532,7 +768,13 @@ extern "C" OTF_API int otf_attn_rope_decode(const void* q, const void* k, const 
   auto* vc = static_cast<uint16_t*>(v_cache);
   auto* o = static_cast<uint16_t*>(out);
   const int64_t z = 0;
-  cudaError_t e = head_dim == 128
+  cudaError_t e = cudaSuccess;
+  if (head_dim == 128 ? otf::launch_attn_cl<128>(heads / kv_heads, s, e, qq, kn, vn, cs, pp, kc, vc, o, scale,
+                                                 (int)kv_heads, (int)max_pos, 1, z, z, z, z)
+                      : otf::launch_attn_cl<64>(heads / kv_heads, s, e, qq, kn, vn, cs, pp, kc, vc, o, scale,
+                                                (int)kv_heads, (int)max_pos, 1, z, z, z, z))
+    return set_cuda_error(e);
+  e = head_dim == 128
                       ? otf::launch_pdl(otf::attn2_kernel<128>(heads / kv_heads), grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
                                         vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
                                         tickets, max_split, z, z, z, z, z)
@@ -581,7 +823,13 @@ extern "C" OTF_API int otf_attn_rope_decode_batch(const void* q, int64_t ldq, co
   auto* kc = static_cast<uint16_t*>(k_cache);
   auto* vc = static_cast<uint16_t*>(v_cache);
   auto* o = static_cast<uint16_t*>(out);
-  cudaError_t e = head_dim == 128
+  cudaError_t e = cudaSuccess;
+  if (head_dim == 128 ? otf::launch_attn_cl<128>(heads / kv_heads, s, e, qq, kn, vn, cs, pp, kc, vc, o, scale,
+                                                 (int)kv_heads, (int)max_pos, batch, ldq, ldkv, cache_stride, ldo)
+                      : otf::launch_attn_cl<64>(heads / kv_heads, s, e, qq, kn, vn, cs, pp, kc, vc, o, scale,
+                                                (int)kv_heads, (int)max_pos, batch, ldq, ldkv, cache_stride, ldo))
+    return set_cuda_error(e);
+  e = head_dim == 128
                       ? otf::launch_pdl(otf::attn2_kernel<128>(heads / kv_heads), grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
                                         vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
                                         tickets, max_split, ldq, ldkv, cache_stride, ldo, ws_stride)
