@@ -376,9 +376,10 @@ OTF_API int otf_pos_advance(int32_t* pos, void* stream);
  * otf_rope_kv followed by otf_attn_decode in one launch: q, k, v as the q/k/v projections
  * wrote them (unrotated), the caches get row pos (rotated k, v), out as otf_attn_decode.
  * Same workspace (otf_attn_workspace_bytes).  With 1, 2, 3, 4 or 8 query heads per KV head the
- * splits of a KV head form one thread-block cluster of at most 8 CTAs and merge over
- * distributed shared memory (the workspace is then not touched); the other ratios merge
- * through the workspace.  Both forms give the same results within fp32 rounding.
+ * splits of a KV head form one thread-block cluster (at most 16 CTAs, 8 for 8 query heads per
+ * KV head) and merge over distributed shared memory (the workspace is then not touched); the
+ * other ratios, and the batched form, merge through the workspace.  Both merges give the same
+ * results within fp32 rounding.
  */
 OTF_API int otf_attn_rope_decode(const void* q, const void* k, const void* v, const void* cos_sin, const int32_t* pos,
                                  void* k_cache, void* v_cache, void* out, float scale, int64_t heads,

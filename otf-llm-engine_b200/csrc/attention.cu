@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
 }
 
 // The same fused step with the split merge inside a thread-block cluster: the S CTAs of one KV
-// head (S <= 8, one cluster, split index = cluster rank) each take a contiguous 1/S of the cached
+// head (S <= 16, one cluster, split index = cluster rank) each take a contiguous 1/S of the cached
 // positions, and push their (max, sum, weighted values) per query head into rank 0's shared
 // memory over DSMEM; after one cluster barrier rank 0 combines the S partials in rank order.
 // No global partials, fences or tickets sit in the chain.  Also: the query rows are requested
@@ -440,7 +440,7 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
 // rows before the rotations (the new position's row is never read from the cache in this call:
 // its rotated k and its v reach this CTA's warps through shared memory).  Every CTA of a cluster
 // runs the same path to the barrier (an empty range contributes max -inf, sum 0).
-constexpr int kAttnClMax = 8;
+constexpr int kAttnClMax = 16;
 
 template <int PL>
 __device__ __forceinline__ void rope_vals(const uint16_t (&xr)[PL], const uint16_t* cs, int D, int lane, __half (&o)[PL]) {
@@ -655,16 +655,19 @@ static decltype(&k_attn_rope_decode_cl<D, 1>) attn_cl_kernel(int64_t rep) {
 }
 
 // Launch the cluster form: grid (S, kv_heads, batch), clusters of S along x, S = the split count
-// the ticket form would use at max_pos, at most 8.  Returns false when the ratio has no cluster
-// form (the caller launches the ticket form).
+// the ticket form would use at max_pos, at most 16 CTAs (a non-portable cluster size) for up to 4
+// query heads per KV head and at most 8 for 8 (whose CTAs hold 150 registers a thread: one per
+// SM).  Single sequences only: a batch keeps the ticket form, whose CTAs fill the GPU already.
+// Returns false when the form does not apply (the caller launches the ticket form).
 template <int D>
 static bool launch_attn_cl(int64_t rep, cudaStream_t s, cudaError_t& err, const uint16_t* q, const uint16_t* kn,
                            const uint16_t* vn, const uint16_t* cs, const int* pp, uint16_t* kc, uint16_t* vc,
                            uint16_t* o, float scale, int kv_heads, int max_pos, int64_t batch, int64_t ldq,
                            int64_t ldkv, int64_t cache_stride, int64_t ldo) {
   auto* k = attn_cl_kernel<D>(rep);
-  if (!k) return false;
-  const int S = (int)std::max<int64_t>(1, std::min<int64_t>(kAttnClMax, (max_pos + kAttnSplitPos - 1) / kAttnSplitPos));
+  if (!k || batch != 1) return false;
+  const int64_t cap = rep <= 4 ? kAttnClMax : 8;
+  const int S = (int)std::max<int64_t>(1, std::min<int64_t>(cap, (max_pos + kAttnSplitPos - 1) / kAttnSplitPos));
   const size_t dyn = (size_t)S * rep * (D + 2) * sizeof(float);
   // The shared-memory opt-in once per kernel, device and size (the first call is an eager one:
   // the decoders run warm-up steps before they capture a graph).
@@ -678,6 +681,8 @@ static bool launch_attn_cl(int64_t rep, cudaStream_t s, cudaError_t& err, const 
     size_t& have = done[std::make_tuple(reinterpret_cast<const void*>(k), dev)];
     if (have < dyn) {
       err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+      if (err != cudaSuccess) return true;
+      err = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       if (err != cudaSuccess) return true;
       have = dyn;
     }
