@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
   }
   const int p = *pos;
   if (p < 0 || p >= max_pos) {  // the host sized the cache; out of range writes nothing
-    if (blockIdx.z == 0) report_bad_position();
+    report_bad_position();  // one thread of each sequence's first CTA
     return;
   }
   const int rep = REP > 0 ? REP : heads / kv_heads;
@@ -488,7 +488,7 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode_cl(
     for (int i = 0; i < PL; ++i) qraw[r][i] = q[(int64_t)(g * REP + r) * D + lane * PL + i];
   const int p = *pos;
   if (p < 0 || p >= max_pos) {  // the same position for every CTA of the cluster: all leave here
-    if (blockIdx.z == 0) report_bad_position();
+    report_bad_position();  // one thread of each sequence's first CTA
     return;
   }
   const int L = p + 1;
