@@ -433,9 +433,11 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode(
 
 // The same fused step with the split merge inside a thread-block cluster: the S CTAs of one KV
 // head (S <= 16, one cluster, split index = cluster rank) each take a contiguous 1/S of the cached
-// positions, and push their (max, sum, weighted values) per query head into rank 0's shared
-// memory over DSMEM; after one cluster barrier rank 0 combines the S partials in rank order.
-// No global partials, fences or tickets sit in the chain.  Also: the query rows are requested
+// positions.  The query-head x dimension outputs are dealt to the S CTAs in contiguous runs; each
+// CTA stores the weighted sums of every run into the run owner's shared memory over DSMEM and
+// its (max, sum) per query head into every CTA's, and after one cluster barrier each CTA
+// combines the S partials of its own run in rank order.  No global partials, fences or tickets
+// sit in the chain, and no CTA receives more than its share.  Also: the query rows are requested
 // together with the position (they do not depend on it), and each warp's first batch of cached
 // rows before the rotations (the new position's row is never read from the cache in this call:
 // its rotated k and its v reach this CTA's warps through shared memory).  Every CTA of a cluster
@@ -462,7 +464,7 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode_cl(
     int64_t cache_stride, int64_t ldo) {
   constexpr int PL = D / 32;
   static_assert(REP >= 1 && REP <= kAttnMaxRep, "query heads per KV head");
-  extern __shared__ __align__(16) float cl_part[];  // rank 0: [S][REP][D + 2] (max, sum, values)
+  extern __shared__ __align__(16) float cl_part[];  // [S][chunk] values, then [S][REP][2] (max, sum)
   __shared__ float sm_m[kAttn2Warps][REP], sm_l[kAttn2Warps][REP];
   __shared__ float sm_acc[kAttn2Warps][REP][D];
   __shared__ float s_knew[D], s_vnew[D];
@@ -580,9 +582,16 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode_cl(
     for (int i = 0; i < PL; ++i) sm_acc[warp][r][lane * PL + i] = acc[r][i];
   }
   __syncthreads();
-  cluster_wait();  // every CTA of the cluster is running: rank 0's shared memory is live
-  const uint32_t part0 = smem_u32(cl_part) + (uint32_t)(sp * REP * (D + 2)) * 4u;
-  for (int e = threadIdx.x; e < REP * D; e += kAttn2Threads) {
+  cluster_wait();  // every CTA of the cluster is running: its peers' shared memory is live
+  // The REP*D outputs are dealt to the S CTAs in contiguous runs of `chunk`: each CTA sends the
+  // weighted sums of every run to the run's owner and its (max, sum) per head to every CTA, then
+  // combines the S partials of its own run in rank order.
+  constexpr int E = REP * D;
+  const int chunk = (E + S - 1) / S;
+  float* const recv = cl_part;               // [S][chunk]
+  float* const mls = cl_part + S * chunk;    // [S][REP][2]
+  const uint32_t recv0 = smem_u32(recv), mls0 = smem_u32(mls);
+  for (int e = threadIdx.x; e < E; e += kAttn2Threads) {
     const int r = e / D, dd = e - r * D;
     float mm = -INFINITY;
     for (int w = 0; w < kAttn2Warps; ++w) mm = fmaxf(mm, sm_m[w][r]);
@@ -592,25 +601,29 @@ __global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode_cl(
       ll += sm_l[w][r] * c;
       aa += sm_acc[w][r][dd] * c;
     }
-    const uint32_t pr = part0 + (uint32_t)(r * (D + 2)) * 4u;
-    st_cluster_f32_plain(mapa_shared(pr + (uint32_t)(2 + dd) * 4u, 0u), aa);
+    const int owner = e / chunk;
+    st_cluster_f32_plain(mapa_shared(recv0 + (uint32_t)(sp * chunk + (e - owner * chunk)) * 4u, (uint32_t)owner), aa);
     if (dd == 0) {
-      st_cluster_f32_plain(mapa_shared(pr, 0u), mm);
-      st_cluster_f32_plain(mapa_shared(pr + 4u, 0u), ll);
+      const uint32_t a = mls0 + (uint32_t)((sp * REP + r) * 2) * 4u;
+      for (int q2 = 0; q2 < S; ++q2) {
+        st_cluster_f32_plain(mapa_shared(a, (uint32_t)q2), mm);
+        st_cluster_f32_plain(mapa_shared(a + 4u, (uint32_t)q2), ll);
+      }
     }
   }
-  cluster_sync_all();  // every partial has landed in rank 0
-  if (sp != 0) return;
-  for (int e = threadIdx.x; e < REP * D; e += kAttn2Threads) {
+  cluster_sync_all();  // every partial has landed with its owner
+  for (int el = threadIdx.x; el < chunk; el += kAttn2Threads) {
+    const int e = sp * chunk + el;
+    if (e >= E) break;
     const int r = e / D, dd = e - r * D;
     float mm = -INFINITY;
-    for (int q2 = 0; q2 < S; ++q2) mm = fmaxf(mm, cl_part[(q2 * REP + r) * (D + 2)]);
+    for (int q2 = 0; q2 < S; ++q2) mm = fmaxf(mm, mls[(q2 * REP + r) * 2]);
     float ll = 0.0f, aa = 0.0f;
     for (int q2 = 0; q2 < S; ++q2) {
-      const float* pq = cl_part + (q2 * REP + r) * (D + 2);
-      const float c = pq[0] == -INFINITY ? 0.0f : __expf(pq[0] - mm);
-      ll += pq[1] * c;
-      aa += pq[2 + dd] * c;
+      const float ms = mls[(q2 * REP + r) * 2];
+      const float c = ms == -INFINITY ? 0.0f : __expf(ms - mm);
+      ll += mls[(q2 * REP + r) * 2 + 1] * c;
+      aa += recv[q2 * chunk + el] * c;
     }
     out[(int64_t)(g * REP + r) * D + dd] = f2h(aa / ll);
   }
@@ -668,7 +681,8 @@ static bool launch_attn_cl(int64_t rep, cudaStream_t s, cudaError_t& err, const 
   if (!k || batch != 1) return false;
   const int64_t cap = rep <= 4 ? kAttnClMax : 8;
   const int S = (int)std::max<int64_t>(1, std::min<int64_t>(cap, (max_pos + kAttnSplitPos - 1) / kAttnSplitPos));
-  const size_t dyn = (size_t)S * rep * (D + 2) * sizeof(float);
+  const int64_t chunk = (rep * D + S - 1) / S;
+  const size_t dyn = (size_t)(S * chunk + S * rep * 2) * sizeof(float);
   // The shared-memory opt-in once per kernel, device and size (the first call is an eager one:
   // the decoders run warm-up steps before they capture a graph).
   {
