@@ -457,8 +457,10 @@ __device__ __forceinline__ void rope_vals(const uint16_t (&xr)[PL], const uint16
   }
 }
 
+// Up to 4 query heads per KV head the kernel is compiled for two CTAs per SM (measured 4% faster
+// on the 3B decode); with 8 it keeps its registers (one CTA per SM, no spills).
 template <int D, int REP>
-__global__ void __launch_bounds__(kAttn2Threads) k_attn_rope_decode_cl(
+__global__ void __launch_bounds__(kAttn2Threads, REP <= 4 ? 2 : 1) k_attn_rope_decode_cl(
     const uint16_t* q, const uint16_t* knew, const uint16_t* vnew, const uint16_t* cos_sin, const int* pos,
     uint16_t* kc, uint16_t* vc, uint16_t* out, float scale, int kv_heads, int max_pos, int64_t ldq, int64_t ldkv,
     int64_t cache_stride, int64_t ldo) {
