@@ -116,11 +116,15 @@ class ClockSampler:
                 "samples": len(sms)}
 
 
+_CPU_SAMPLE: dict = {}
+
+
 def cpu_reference_sample(cfg, target_s: float, threads: int = 0):
     """Time the reference's CPU algorithm (oracle port) on whole layers of the stack.
 
     Inputs are synthetic codes/scales/anchors of the stack's shapes (the CPU cost does
-    not depend on the values).  Returns (GB/s, cores, sample description, seconds).
+    not depend on the values), built once per configuration and reused, so a call after the
+    first times warm buffers.  Returns (GB/s, cores, sample description, seconds).
     """
     import numpy as np
     from oracle import oracle
@@ -129,22 +133,25 @@ def cpu_reference_sample(cfg, target_s: float, threads: int = 0):
     if threads:
         oracle.set_num_threads(threads)
     cores = oracle.num_threads()
-    rng = np.random.default_rng(0)
     shapes = cfg.shapes()
-    layer = []
-    for name in PROJECTIONS:
-        N, K = shapes[name]
-        k = max(1, int(K * cfg.outlier_ratio))
-        layer.append(dict(
-            x=rng.standard_normal((1, K)).astype(np.float16),
-            packed=rng.integers(0, 256, (N, K // 4), dtype=np.uint8),
-            scales=(rng.random((N, K // cfg.group_size)) * 0.03 + 0.002).astype(np.float16),
-            idx=rng.choice(K, k, replace=False).astype(np.int64),
-            ov=(rng.standard_normal((N, k)) * 0.05).astype(np.float16),
-            mask=np.ones(K, dtype=np.float16), N=N, K=K, k=k))
-    wbuf = np.empty(max(d["N"] * d["K"] for d in layer), dtype=np.float16)
-    for d in layer:
-        d["mask"][d["idx"]] = 0
+    key = (tuple(sorted(shapes.items())), cfg.group_size, cfg.outlier_ratio)
+    if _CPU_SAMPLE.get("key") != key:     # one synthetic layer per configuration, reused by every call
+        rng = np.random.default_rng(0)
+        layer = []
+        for name in PROJECTIONS:
+            N, K = shapes[name]
+            k = max(1, int(K * cfg.outlier_ratio))
+            layer.append(dict(
+                x=rng.standard_normal((1, K)).astype(np.float16),
+                packed=rng.integers(0, 256, (N, K // 4), dtype=np.uint8),
+                scales=(rng.random((N, K // cfg.group_size)) * 0.03 + 0.002).astype(np.float16),
+                idx=rng.choice(K, k, replace=False).astype(np.int64),
+                ov=(rng.standard_normal((N, k)) * 0.05).astype(np.float16),
+                mask=np.ones(K, dtype=np.float16), N=N, K=K, k=k))
+        for d in layer:
+            d["mask"][d["idx"]] = 0
+        _CPU_SAMPLE.update(key=key, layer=layer, wbuf=np.empty(max(d["N"] * d["K"] for d in layer), dtype=np.float16))
+    layer, wbuf = _CPU_SAMPLE["layer"], _CPU_SAMPLE["wbuf"]
     nbytes, reps = 0, 0
     t0 = time.perf_counter()
     while True:
