@@ -36,6 +36,65 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const uint16_t* x, int64_t ldx,
   }
 }
 
+// The same op for rows of K = 8k halves on 16-byte boundaries (every Llama width): thread t
+// holds the row's 16-byte pieces t, t + 256, ... (PER of them) in registers, all requested at
+// once, and the weight's pieces are requested before the dependency wait, so a row costs one
+// memory round trip instead of one per strided element.
+template <int PER>
+__global__ void __launch_bounds__(256) k_rmsnorm_v(const uint16_t* x, int64_t ldx, const uint16_t* w, float eps,
+                                                   uint16_t* out, int64_t ldo, int K) {
+  pdl_trigger();
+  __shared__ float red[8];
+  const int tid = threadIdx.x, nv = K >> 3;
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  uint4 wv[PER], xv[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int v = tid + i * 256;
+    wv[i] = (w && v < nv) ? __ldg(reinterpret_cast<const uint4*>(w) + v) : z4;
+  }
+  pdl_wait();
+  const uint4* xr = reinterpret_cast<const uint4*>(x + blockIdx.x * ldx);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int v = tid + i * 256;
+    xv[i] = v < nv ? __ldg(xr + v) : z4;
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const __half2* h = reinterpret_cast<const __half2*>(&xv[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float r = rsqrtf(tot / (float)K + eps);
+  uint4* orow = reinterpret_cast<uint4*>(out + blockIdx.x * ldo);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int v = tid + i * 256;
+    if (v >= nv) break;
+    __half* e = reinterpret_cast<__half*>(&xv[i]);
+    const __half* wh = reinterpret_cast<const __half*>(&wv[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      __half y = __float2half_rn(__half2float(e[j]) * r);
+      if (w) y = __hmul(wh[j], y);
+      e[j] = y;
+    }
+    orow[v] = xv[i];
+  }
+}
+
 __global__ void k_silu_mul(const uint16_t* g, const uint16_t* u, uint16_t* out, int64_t n) {
   pdl_trigger();
   pdl_wait();
@@ -56,9 +115,21 @@ extern "C" OTF_API int otf_rmsnorm(const void* x, int64_t ldx, const void* w, fl
   if (M > INT32_MAX || K > INT32_MAX) return OTF_ERR_UNSUPPORTED;
   int st = check_device();
   if (st != OTF_OK) return st;
-  return set_cuda_error(launch_pdl(k_rmsnorm, dim3((unsigned)M), dim3(256), 0, static_cast<cudaStream_t>(stream), 1u,
-                                   static_cast<const uint16_t*>(x), ldx, static_cast<const uint16_t*>(w), eps,
-                                   static_cast<uint16_t*>(out), ldo, (int)K));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint16_t* xp = static_cast<const uint16_t*>(x);
+  const uint16_t* wp = static_cast<const uint16_t*>(w);
+  uint16_t* op = static_cast<uint16_t*>(out);
+  const bool vec = K % 8 == 0 && ldx % 8 == 0 && ldo % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(out) % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0;
+  if (vec && K <= 2048)
+    return set_cuda_error(launch_pdl(k_rmsnorm_v<1>, dim3((unsigned)M), dim3(256), 0, s, 1u, xp, ldx, wp, eps, op, ldo, (int)K));
+  if (vec && K <= 4096)
+    return set_cuda_error(launch_pdl(k_rmsnorm_v<2>, dim3((unsigned)M), dim3(256), 0, s, 1u, xp, ldx, wp, eps, op, ldo, (int)K));
+  if (vec && K <= 8192)
+    return set_cuda_error(launch_pdl(k_rmsnorm_v<4>, dim3((unsigned)M), dim3(256), 0, s, 1u, xp, ldx, wp, eps, op, ldo, (int)K));
+  if (vec && K <= 16384)
+    return set_cuda_error(launch_pdl(k_rmsnorm_v<8>, dim3((unsigned)M), dim3(256), 0, s, 1u, xp, ldx, wp, eps, op, ldo, (int)K));
+  return set_cuda_error(launch_pdl(k_rmsnorm, dim3((unsigned)M), dim3(256), 0, s, 1u, xp, ldx, wp, eps, op, ldo, (int)K));
 }
 
 extern "C" OTF_API int otf_silu_mul(const void* g, const void* u, void* out, int64_t n, void* stream) {

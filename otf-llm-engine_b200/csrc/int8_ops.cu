@@ -416,6 +416,46 @@ __global__ void k_i8_embed(const int64_t* ids, int n, const int8_t* w, int64_t l
     o[d] = __half_as_ushort(__hmul(__int2half_rn((int)wr[d]), s));
 }
 
+// The same gather for rows of D = 16k bytes on 16-byte boundaries: thread t converts the row's
+// 16-byte pieces t, t + 256, ... (at most 4), all requested together with the row's scale once
+// the id is known, so a row costs two memory round trips (id, then row) instead of one per
+// strided byte.
+__global__ void __launch_bounds__(256) k_i8_embed_v(const int64_t* ids, int n, const int8_t* __restrict__ w,
+                                                    int64_t ldw, const uint16_t* __restrict__ scales,
+                                                    uint16_t* __restrict__ out, int64_t ldo, int64_t V, int D,
+                                                    int32_t* bad) {
+  pdl_trigger();
+  pdl_wait();
+  const int tok = blockIdx.x;
+  if (tok >= n) return;
+  const int64_t id = ids[tok];
+  const int nv = D >> 4, tid = threadIdx.x;
+  uint4* o = reinterpret_cast<uint4*>(out + (int64_t)tok * ldo);
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  if (id < 0 || id >= V) {
+    for (int v = tid; v < nv; v += 256) o[2 * v] = o[2 * v + 1] = z4;
+    if (bad && tid == 0) *bad = 1;
+    return;
+  }
+  const uint4* wr = reinterpret_cast<const uint4*>(w + id * ldw);
+  uint4 wv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) wv[i] = tid + i * 256 < nv ? __ldg(wr + tid + i * 256) : z4;
+  const __half s = __ushort_as_half(__ldg(scales + id));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int v = tid + i * 256;
+    if (v >= nv) break;
+    const int8_t* b = reinterpret_cast<const int8_t*>(&wv[i]);
+    uint4 r[2];
+    __half* e = reinterpret_cast<__half*>(r);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) e[j] = __hmul(__int2half_rn((int)b[j]), s);
+    o[2 * v] = r[0];
+    o[2 * v + 1] = r[1];
+  }
+}
+
 }  // namespace otf
 
 using namespace otf;
@@ -538,6 +578,11 @@ extern "C" OTF_API int otf_i8_embed(const int64_t* ids, int64_t n, const int8_t*
   if (n > INT32_MAX || D > INT32_MAX) return OTF_ERR_UNSUPPORTED;
   int st = check_device();
   if (st != OTF_OK) return st;
+  if (D % 16 == 0 && D <= 4 * 256 * 16 && ldw % 16 == 0 && ldo % 8 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(out) % 16 == 0)
+    return set_cuda_error(launch_pdl(k_i8_embed_v, dim3((unsigned)n), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                                     1u, ids, (int)n, w, ldw, static_cast<const uint16_t*>(scales),
+                                     static_cast<uint16_t*>(out), ldo, V, (int)D, bad_ids));
   return set_cuda_error(launch_pdl(k_i8_embed, dim3((unsigned)n), dim3(128), 0, static_cast<cudaStream_t>(stream), 1u,
                                    ids, (int)n, w, ldw, static_cast<const uint16_t*>(scales),
                                    static_cast<uint16_t*>(out), ldo, V, (int)D, bad_ids));

@@ -442,8 +442,9 @@ def i8_head_argmax(x2d: torch.Tensor, w_i8: torch.Tensor, scales: torch.Tensor,
 
 
 def i8_embed(ids: torch.Tensor, w_i8: torch.Tensor, scales: torch.Tensor,
-             bad_flag: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """fp16 [n, D] rows of the INT8 embedding (bit-identical to the reference gather)."""
+             bad_flag: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp16 [n, D] rows of the INT8 embedding (bit-identical to the reference gather), into
+    ``out`` (n rows of D fp16, row stride a multiple of 8 for the 16-byte-piece form) if given."""
     _need_cuda(ids, "input_ids")
     flat = ids.reshape(-1)
     if flat.dtype != torch.int64:
@@ -454,9 +455,15 @@ def i8_embed(ids: torch.Tensor, w_i8: torch.Tensor, scales: torch.Tensor,
     s = scales.reshape(-1)
     if s.dtype != torch.float16 or s.numel() != V or not s.is_contiguous():
         raise ValueError("scales must hold V contiguous fp16 values")
-    out = torch.empty((flat.numel(), D), dtype=torch.float16, device=ids.device)
+    if w_i8.device != ids.device or s.device != ids.device:
+        raise ValueError(f"weight_int8 and scales must be on {ids.device}")
+    if out is None:
+        out = torch.empty((flat.numel(), D), dtype=torch.float16, device=ids.device)
+    elif out.dim() != 2 or out.shape[0] != flat.numel() or out.device != ids.device:
+        raise ValueError(f"out must be [{flat.numel()}, {D}] on {ids.device}")
+    ldo = _rows(out, "out", torch.float16, D)
     with torch.cuda.device(ids.device):
-        st = lib().otf_i8_embed(_ptr(flat), flat.numel(), _ptr(w_i8), ldw, _ptr(s), _ptr(out), D, V, D,
+        st = lib().otf_i8_embed(_ptr(flat), flat.numel(), _ptr(w_i8), ldw, _ptr(s), _ptr(out), ldo, V, D,
                                 _ptr(bad_flag), _stream(ids.device))
     _check(st, "otf_i8_embed")
     return out

@@ -203,8 +203,7 @@ class GreedyDecoder:
         cfg, b, L = self.cfg, self.b, _native.lib()
         G = _native.GroupItem
         st = _native._stream(self.device)
-        h = self.embed(self.ids.view(1)).view(1, -1)
-        b["h"].copy_(h)
+        _embed_into(self.embed, self.ids.view(1), b["h"].view(1, -1))
         if self.world > 1:
             cur = self._layers_tp(b["h"])
             xn = _native.rmsnorm(cur, self.final_norm, cfg.rms_eps, out=b["xn"])
@@ -276,6 +275,7 @@ class GreedyDecoder:
     def generate(self, prompt: torch.Tensor, new_tokens: int, logits_out: Optional[List[torch.Tensor]] = None
                  ) -> torch.Tensor:
         """Greedy continuation of prompt (int64 ids on the device) by new_tokens tokens."""
+        _check_prompt(prompt, self.embed.weight_int8.shape[0])
         self.reset()
         out = torch.empty(new_tokens, dtype=torch.int64, device=self.device)
         n = prompt.numel()
@@ -291,6 +291,20 @@ class GreedyDecoder:
                 if logits_out is not None:
                     logits_out.append(self.logits.clone())
         return out
+
+
+def _embed_into(embed, ids: torch.Tensor, out: torch.Tensor) -> None:
+    """The INT8 embedding rows of ids written straight into the residual stream buffer (no
+    intermediate tensor, no copy launch).  Ids come from the head's argmax or from prompts
+    checked by ``_check_prompt``."""
+    _native.i8_embed(ids, embed.weight_int8, embed.scales.reshape(-1), None, out=out)
+
+
+def _check_prompt(prompt: torch.Tensor, vocab: int) -> None:
+    """Prompt ids outside [0, vocab) raise IndexError before any step, as the reference's
+    F.embedding does (the token steps themselves run without a host sync)."""
+    if prompt.numel() and (int(prompt.min()) < 0 or int(prompt.max()) >= vocab):
+        raise IndexError("index out of range in self")
 
 
 class BatchedGreedyDecoder:
@@ -362,7 +376,7 @@ class BatchedGreedyDecoder:
         cfg, b, L, B = self.cfg, self.b, _native.lib(), self.batch
         st = _native._stream(self.device)
         tp, lead = self.world > 1, self.rank == 0
-        b["h"].copy_(self.embed(self.ids).view(B, -1))
+        _embed_into(self.embed, self.ids.view(B), b["h"].view(B, -1))
         kvd = self.kv_heads * cfg.head_dim
         for li, layer in enumerate(self.layers):
             _native.rmsnorm(b["h"], self.in_norms[li], cfg.rms_eps, out=b["xn"])
@@ -432,6 +446,7 @@ class BatchedGreedyDecoder:
         new_tokens tokens per sequence; returns int64 [batch, new_tokens]."""
         if prompts.dim() != 2 or prompts.shape[0] != self.batch:
             raise ValueError(f"prompts must be [{self.batch}, P]")
+        _check_prompt(prompts, self.embed.weight_int8.shape[0])
         self.reset()
         out = torch.empty(self.batch, new_tokens, dtype=torch.int64, device=self.device)
         for i in range(prompts.shape[1]):

@@ -48,6 +48,23 @@ def test_embedding_large_vocab_bit_exact(cuda_dev):
     assert int(bad.item()) == 1 and bool((out[1:] == 0).all())
 
 
+@pytest.mark.parametrize("D", [100, 256, 8192, 16384, 16400])
+def test_embedding_widths_bit_exact(D, cuda_dev):
+    """Row widths on both sides of the 16-byte-piece gather (D a multiple of 16 up to 16384)
+    and the strided form beyond it, bit for bit against the oracle."""
+    from otf_llm import _native
+    V = 300
+    g = torch.Generator().manual_seed(D)
+    w = torch.randint(-127, 128, (V, D), generator=g, dtype=torch.int32).to(torch.int8)
+    s = (torch.rand(V, 1, generator=g) * 2e-3 + 1e-5).half()
+    ids = torch.tensor([0, V - 1, 7, 7, 123], dtype=torch.int64)
+    bad = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    out = _native.i8_embed(ids.to(cuda_dev), w.to(cuda_dev), s.to(cuda_dev), bad).cpu().numpy()
+    ref = oracle.i8_embed(ids.numpy(), w.numpy(), s.numpy())
+    assert np.array_equal(out.view(np.uint16), ref.view(np.uint16))
+    assert int(bad.item()) == 0
+
+
 def test_head_golden(cuda_dev):
     from otf_llm.symmetric_2bit_engine import QuantizedEmbedding, QuantizedLinearHead
     gd = load_golden("int8_v1000_d256")

@@ -55,6 +55,24 @@ def test_fused_rmsnorm_and_silu(cuda_dev):
     assert rel_err(out.float().cpu().numpy(), ref.float().cpu().numpy()) < 1e-3
 
 
+@pytest.mark.parametrize("K", [3072, 4100, 8192, 16384, 20000])
+def test_rmsnorm_widths(K, cuda_dev):
+    """otf_rmsnorm at widths served by the register-held 16-byte pieces (K = 8k up to 16384)
+    and by the strided form (4100, 20000), against HF's Llama RMSNorm in fp32."""
+    from otf_llm import _native
+    g = torch.Generator(device=cuda_dev).manual_seed(K)
+    h = (torch.randn(3, K, generator=g, device=cuda_dev) * 2).half()
+    h[1, 5] = 300.0
+    w = (torch.rand(K, generator=g, device=cuda_dev) + 0.5).half()
+    for weight in (w, None):
+        got = _native.rmsnorm(h, weight, 1e-5).float().cpu().numpy()
+        xf = h.float()
+        ref = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)).half()
+        if weight is not None:
+            ref = weight * ref
+        assert rel_err(got, ref.float().cpu().numpy()) < 1e-3
+
+
 def _cpu_step(stack, h):
     """The decode step restated on the CPU: HF RMSNorm / SiLU in torch, linears by the oracle."""
     def lin(m, x):
