@@ -495,6 +495,9 @@ def silu_mul(g: torch.Tensor, u: torch.Tensor, out: Optional[torch.Tensor] = Non
         raise ValueError("gate and up must be contiguous")
     if out is None:
         out = torch.empty_like(g)
+    elif (out.dtype != torch.float16 or out.numel() != g.numel() or not out.is_contiguous()
+          or out.device != g.device):
+        raise ValueError("out must be a contiguous fp16 tensor with gate's element count on its device")
     with torch.cuda.device(g.device):
         st = lib().otf_silu_mul(_ptr(g), _ptr(u), _ptr(out), g.numel(), _stream(g.device))
     _check(st, "otf_silu_mul")

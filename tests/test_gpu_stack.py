@@ -73,6 +73,22 @@ def test_rmsnorm_widths(K, cuda_dev):
         assert rel_err(got, ref.float().cpu().numpy()) < 1e-3
 
 
+def test_silu_mul_piece_and_strided_forms_agree(cuda_dev):
+    """otf_silu_mul on 16-byte pieces (element count a multiple of 8) equals the per-element
+    form bit for bit (an odd count takes that form), and both are within an fp16 ulp of torch's
+    fp32 silu rounded to fp16 times up."""
+    from otf_llm import _native
+    g0 = torch.Generator(device=cuda_dev).manual_seed(3)
+    n = 8 * 4001
+    g = (torch.randn(n + 1, generator=g0, device=cuda_dev) * 4).half()
+    u = torch.randn(n + 1, generator=g0, device=cuda_dev).half()
+    odd = _native.silu_mul(g, u)
+    vec = _native.silu_mul(g[:n].clone(), u[:n].clone())
+    assert torch.equal(vec, odd[:n])
+    ref = (torch.nn.functional.silu(g.float()).half() * u).float()
+    assert rel_err(odd.float().cpu().numpy(), ref.cpu().numpy()) < 1e-3
+
+
 def _cpu_step(stack, h):
     """The decode step restated on the CPU: HF RMSNorm / SiLU in torch, linears by the oracle."""
     def lin(m, x):
