@@ -232,6 +232,9 @@ OTF_API int otf2b_unpack_codes(const uint8_t* packed, int64_t ld_packed, int64_t
  *   logits[m,v] = scales[v] * sum_d x[m,d] * w[v,d]   (fp32, NaN -> 0, clamped to +-65504)
  * Replaces QuantizedLinearHead.forward (otf_llm/symmetric_2bit_engine.py:75-91).
  * x: fp16 [M, ldx]; w: int8 [V, ldw]; scales: fp16 [V]; logits: fp32 [M, ldl].
+ * With 16-byte aligned weight rows (D a multiple of 16) one launch serves up to 8 rows of x
+ * (4 at D = 8192), reading the weights once for all of them; each row's logits are
+ * bit-identical to a call with that row alone.
  */
 OTF_API int otf_i8_head(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const void* scales,
                         float* logits, int64_t ldl, int64_t M, int64_t V, int64_t D, void* stream);

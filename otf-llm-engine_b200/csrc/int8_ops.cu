@@ -35,6 +35,7 @@ struct HeadArgs {
   float* out;                 // logits (may be null when only the argmax is wanted)
   unsigned long long* amax;   // packed (ordered logit, ~index) maximum, or null
   int V, D;
+  int64_t ldx, ldl;           // row strides of x and of the logits (multi-row TMA head)
 };
 
 // Order-preserving 64-bit key of (logit, index): larger logit wins, then the smaller index
@@ -227,13 +228,25 @@ struct alignas(64) HeadTmaArgs {
   HeadArgs a;
 };
 
-__host__ __device__ inline int64_t head_tma_smem_bytes(int D) {
-  return 1024 + 2 * kHTSlots * kHTBoxBytes + 128 + head_smem_bytes(D);
+// One activation row's fixed-point table and block factors (the layout head_smem_bytes
+// describes, without the zero block).
+__host__ __device__ inline int64_t head_row_table_bytes(int D) {
+  const int nb = D / 16;
+  return align_up(align_up((int64_t)nb * kHeadSB, 16) + (int64_t)nb * 4, 16);
+}
+
+// R activation rows per launch share every weight box: R tables, then the zero block.
+__host__ __device__ inline int64_t head_tma_smem_bytes(int D, int R) {
+  return 1024 + 2 * kHTSlots * kHTBoxBytes + 128 + (int64_t)R * head_row_table_bytes(D) + 16;
 }
 
 __device__ __forceinline__ void head_wait_failed() { atomicExch(&g_head_device_error, 1); }
 
-__global__ void __launch_bounds__(kHTThreads, 2) k_i8_head_tma(const __grid_constant__ HeadTmaArgs p) {
+// R activation rows (x rows a.x + r * a.ldx) per launch: each weight box feeds every row's MMAs,
+// so the weights stream once for R rows; each row's arithmetic (table, MMA sets, flush order,
+// reduction) is the single-row kernel's, so its logits are bit-identical to a launch of its own.
+template <int R>
+__global__ void __launch_bounds__(kHTThreads, R <= 2 ? 2 : 1) k_i8_head_tma(const __grid_constant__ HeadTmaArgs p) {
   const HeadArgs& a = p.a;
   pdl_trigger();
   // Dynamic shared memory rounded up to the 1024-byte period of the swizzle (1 KB of slack).
@@ -244,8 +257,9 @@ __global__ void __launch_bounds__(kHTThreads, 2) k_i8_head_tma(const __grid_cons
   const uint32_t empty = full + 8 * 2 * kHTSlots;
   uint8_t* const tbl = smem + 2 * kHTSlots * kHTBoxBytes + 128;
   const int nb = a.D / 16;
-  float* const metaF = reinterpret_cast<float*>(tbl + align_up((int64_t)nb * kHeadSB, 16));
-  uint8_t* const zblk = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(metaF + nb), 16));
+  const int64_t tstride = head_row_table_bytes(a.D);              // row rr's table at tbl + rr * tstride
+  const int64_t moff = align_up((int64_t)nb * kHeadSB, 16);        // its block factors after the table
+  uint8_t* const zblk = tbl + R * tstride;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nq = ceil_div(a.V, kHTRows), nch = ceil_div(a.D, kHeadChunk);
   const int q_beg = (int)((int64_t)blockIdx.x * nq / gridDim.x);
@@ -286,14 +300,18 @@ __global__ void __launch_bounds__(kHTThreads, 2) k_i8_head_tma(const __grid_cons
   }
 
   pdl_wait();
-  // Activation table for the whole D (every CTA builds its own; its rows amortise it).
-  for (int it = tid; it < 2 * nb; it += kHTConsumers * 32) {
-    const int b = it >> 1, limb = it & 1;
+  // Activation tables for the whole D, one per row (every CTA builds its own; its vocabulary
+  // rows amortise them).
+  for (int it = tid; it < 2 * nb * R; it += kHTConsumers * 32) {
+    const int rr = it / (2 * nb), b = (it >> 1) - rr * nb, limb = it & 1;
+    const uint16_t* const xr = a.x + rr * a.ldx;
+    uint8_t* const trow = tbl + rr * tstride;
+    float* const metaF = reinterpret_cast<float*>(trow + moff);
     float xv[16];
     float mx = 0.0f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      xv[i] = h2f(a.x[b * 16 + i]);
+      xv[i] = h2f(xr[b * 16 + i]);
       mx = fmaxf(mx, fabsf(xv[i]));
     }
     const int E = fixed_point_exp(mx);
@@ -305,7 +323,7 @@ __global__ void __launch_bounds__(kHTThreads, 2) k_i8_head_tma(const __grid_cons
       split_limbs(__float2int_rn(__fmul_rn(xv[i], sc)), hi, lo);
       wd[i >> 2] |= (uint32_t)((limb == 0 ? hi : lo) & 0xff) << (8 * (i & 3));
     }
-    uint2* dst = reinterpret_cast<uint2*>(tbl + b * kHeadSB + limb * kHeadSL);
+    uint2* dst = reinterpret_cast<uint2*>(trow + b * kHeadSB + limb * kHeadSL);
     dst[0] = make_uint2(wd[0], wd[1]);
     dst[1] = make_uint2(wd[2], wd[3]);
     if (limb == 0) metaF[b] = ldexpf(1.0f, -E);
@@ -321,7 +339,9 @@ __global__ void __launch_bounds__(kHTThreads, 2) k_i8_head_tma(const __grid_cons
   const int my_nq = team ? nq1 : nq0;
   for (int qi = 0; qi < my_nq; ++qi) {
     const int quad = q_beg + team + 2 * qi;
-    float acc0 = 0.0f, acc1 = 0.0f;
+    float acc0[R], acc1[R];
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) acc0[rr] = acc1[rr] = 0.0f;
     for (int cc = 0; cc < nch; ++cc, ++i) {
       const int sl = team * kHTSlots + (i & (kHTSlots - 1));
       if (!mbar_wait_spin(full + 8 * sl, (uint32_t)(i / kHTSlots) & 1u)) head_wait_failed();
@@ -334,39 +354,50 @@ __global__ void __launch_bounds__(kHTThreads, 2) k_i8_head_tma(const __grid_cons
         const uint4 cw8 = *reinterpret_cast<const uint4*>(pa + 8 * kHeadChunk);
         const int blk = cc * 8 + 2 * t + set;          // my block (this quad's)
         const int bblk = cc * 8 + 2 * (g >> 1) + set;  // the block whose B rows this lane supplies
-        const uint8_t* bp = (breal && bblk < nb) ? (tbl + bblk * kHeadSB + (g & 1) * kHeadSL) : zblk;
-        const uint2 b01 = *reinterpret_cast<const uint2*>(bp);
-        const uint2 b23 = *reinterpret_cast<const uint2*>(bp + 8);
-        int C[4] = {0, 0, 0, 0};
-        mma_s8s8(C, cw.x, cw8.x, cw.y, cw8.y, b01.x, b01.y);
-        mma_s8s8(C, cw.z, cw8.z, cw.w, cw8.w, b23.x, b23.y);
-        if (blk < nb) {
-          const float F = metaF[blk];
-          acc0 = fmaf((float)(256 * C[0] + C[1]), F, acc0);
-          acc1 = fmaf((float)(256 * C[2] + C[3]), F, acc1);
+        const bool bok = breal && bblk < nb;
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+          const uint8_t* const trow = tbl + rr * tstride;
+          const uint8_t* bp = bok ? (trow + bblk * kHeadSB + (g & 1) * kHeadSL) : zblk;
+          const uint2 b01 = *reinterpret_cast<const uint2*>(bp);
+          const uint2 b23 = *reinterpret_cast<const uint2*>(bp + 8);
+          int C[4] = {0, 0, 0, 0};
+          mma_s8s8(C, cw.x, cw8.x, cw.y, cw8.y, b01.x, b01.y);
+          mma_s8s8(C, cw.z, cw8.z, cw.w, cw8.w, b23.x, b23.y);
+          if (blk < nb) {
+            const float F = reinterpret_cast<const float*>(trow + moff)[blk];
+            acc0[rr] = fmaf((float)(256 * C[0] + C[1]), F, acc0[rr]);
+            acc1[rr] = fmaf((float)(256 * C[2] + C[3]), F, acc1[rr]);
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty + 8 * sl);
     }
-    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
     const int rg = quad * kHTRows + r, rg8 = rg + 8;
-    const float l0 = rg < a.V ? head_finish(acc0, h2f(a.scales[rg])) : 0.0f;
-    const float l1 = rg8 < a.V ? head_finish(acc1, h2f(a.scales[rg8])) : 0.0f;
-    if (t == 0 && a.out) {
-      if (rg < a.V) a.out[rg] = l0;
-      if (rg8 < a.V) a.out[rg8] = l1;
-    }
-    if (a.amax) {
-      unsigned long long key = 0ull;
-      if (rg < a.V) key = argmax_key(l0, rg);
-      if (rg8 < a.V) key = max(key, argmax_key(l1, rg8));
+    const float s0 = rg < a.V ? h2f(a.scales[rg]) : 0.0f, s8 = rg8 < a.V ? h2f(a.scales[rg8]) : 0.0f;
 #pragma unroll
-      for (int o = 4; o < 32; o <<= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
-      if (lane == 0) atomicMax(a.amax, key);
+    for (int rr = 0; rr < R; ++rr) {
+      float v0 = acc0[rr], v1 = acc1[rr];
+      v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+      v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
+      v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+      v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
+      const float l0 = rg < a.V ? head_finish(v0, s0) : 0.0f;
+      const float l1 = rg8 < a.V ? head_finish(v1, s8) : 0.0f;
+      float* const out = a.out ? a.out + rr * a.ldl : nullptr;
+      if (t == 0 && out) {
+        if (rg < a.V) out[rg] = l0;
+        if (rg8 < a.V) out[rg8] = l1;
+      }
+      if (a.amax) {
+        unsigned long long key = 0ull;
+        if (rg < a.V) key = argmax_key(l0, rg);
+        if (rg8 < a.V) key = max(key, argmax_key(l1, rg8));
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+        if (lane == 0) atomicMax(a.amax + rr, key);
+      }
     }
   }
 }
@@ -473,30 +504,50 @@ int otf::head_device_error(int clear) {
   return v;
 }
 
-// The TMA-fed head for rows of 16-byte aligned int8 weights (D a multiple of 16); false if
-// the layout does not qualify (the caller then runs the copy-stage kernel).
-static bool head_launch_tma(const HeadArgs& a, cudaStream_t s, cudaError_t& err) {
-  const int64_t smem = head_tma_smem_bytes(a.D);
-  if (a.D % 16 || a.ldw % 16 || reinterpret_cast<uintptr_t>(a.w) % 16 || smem > 227 * 1024) return false;
+// Rows per launch of the TMA-fed head: the most (1, 2, 4 or 8, at most the rows left) whose
+// activation tables fit in shared memory beside the weight rings.
+static int head_tma_rows(int64_t left, int D) {
+  int R = 8;
+  while (R > 1 && (R > left || head_tma_smem_bytes(D, R) > 227 * 1024)) R >>= 1;
+  return R;
+}
+
+template <int R>
+static cudaError_t launch_head_tma(const HeadTmaArgs& p, int dev, int sms, cudaStream_t s) {
   static thread_local int configured_dev[64] = {};
+  if (!configured_dev[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_i8_head_tma<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    configured_dev[dev] = 1;
+  }
+  const int64_t smem = head_tma_smem_bytes(p.a.D, R);
+  const int per_sm = (R <= 2 && smem <= 113 * 1024) ? 2 : 1;
+  const int ctas = std::max(1, std::min(ceil_div(p.a.V, kHTRows), per_sm * std::max(1, sms)));
+  return launch_pdl(k_i8_head_tma<R>, dim3((unsigned)ctas), dim3(kHTThreads), (size_t)smem, s, 1u, p);
+}
+
+// The TMA-fed head for R rows (x rows a.x + r * a.ldx, logits a.out + r * a.ldl, keys
+// a.amax + r) of 16-byte aligned int8 weights (D a multiple of 16); false if the layout does
+// not qualify (the caller then runs the copy-stage kernel row by row).
+static bool head_launch_tma(const HeadArgs& a, int R, cudaStream_t s, cudaError_t& err) {
+  const int64_t smem = head_tma_smem_bytes(a.D, R);
+  if (a.D % 16 || a.ldw % 16 || reinterpret_cast<uintptr_t>(a.w) % 16 || smem > 227 * 1024) return false;
   static thread_local int sms_of[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return false;
-  if (!configured_dev[dev]) {
-    err = cudaFuncSetAttribute(k_i8_head_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (err != cudaSuccess) return true;
-    cudaDeviceGetAttribute(&sms_of[dev], cudaDevAttrMultiProcessorCount, dev);
-    configured_dev[dev] = 1;
-  }
+  if (!sms_of[dev]) cudaDeviceGetAttribute(&sms_of[dev], cudaDevAttrMultiProcessorCount, dev);
   static thread_local HeadTmaArgs p;  // 128-byte tensor map + arguments, kept off the stack
   if (!encode_tiled_2d(&p.wmap, 1, a.w, (uint64_t)a.D, (uint64_t)a.V, (uint64_t)a.ldw, (uint32_t)kHeadChunk,
                        (uint32_t)kHTRows, true))
     return false;
   p.a = a;
-  const int per_sm = smem <= 113 * 1024 ? 2 : 1;
-  const int ctas = std::max(1, std::min(ceil_div(a.V, kHTRows), per_sm * std::max(1, sms_of[dev])));
-  err = launch_pdl(k_i8_head_tma, dim3((unsigned)ctas), dim3(kHTThreads), (size_t)smem, s, 1u, p);
+  switch (R) {
+    case 1: err = launch_head_tma<1>(p, dev, sms_of[dev], s); break;
+    case 2: err = launch_head_tma<2>(p, dev, sms_of[dev], s); break;
+    case 4: err = launch_head_tma<4>(p, dev, sms_of[dev], s); break;
+    default: err = launch_head_tma<8>(p, dev, sms_of[dev], s); break;
+  }
   return true;
 }
 
@@ -515,7 +566,7 @@ static int head_launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw,
     }
   }
   int sms = 148;
-  for (int64_t m = 0; m < M; ++m) {
+  for (int64_t m = 0; m < M;) {
     HeadArgs a;
     a.x = static_cast<const uint16_t*>(x) + m * ldx;
     a.w = w;
@@ -525,11 +576,16 @@ static int head_launch(const void* x, int64_t ldx, const int8_t* w, int64_t ldw,
     a.amax = keys ? keys + m : nullptr;
     a.V = (int)V;
     a.D = (int)D;
+    a.ldx = ldx;
+    a.ldl = ldl;
     cudaError_t e = cudaSuccess;
-    if (head_launch_tma(a, s, e)) {
+    const int R = head_tma_rows(M - m, (int)D);
+    if (head_launch_tma(a, R, s, e)) {
       if (e != cudaSuccess) return set_cuda_error(e);
+      m += R;
       continue;
     }
+    ++m;
     const int ctas_per_sm = head_pipe_smem_bytes((int)D) <= 110 * 1024 ? 2 : 1;
     e = fast ? launch_pdl(k_i8_head_imma,
                                       dim3(std::max(1, std::min(ceil_div(ceil_div((int)V, 16), kHeadWarps),

@@ -95,6 +95,32 @@ def test_head_shapes(V, D, M, cuda_dev):
     assert rel_err(lg, ref) < 1e-3
 
 
+@pytest.mark.parametrize("V,D,M", [(5000, 3072, 16), (3000, 8192, 16), (777, 272, 11), (4097, 64, 3)])
+def test_head_rows_share_weight_boxes(V, D, M, cuda_dev):
+    """Several activation rows per head launch (up to 8, as shared memory allows) read every
+    weight box once for all of them; each row's logits and greedy pick are bit-identical to a
+    launch of that row alone, with strided x and logits rows."""
+    from otf_llm import _native
+    g = torch.Generator().manual_seed(V * 7 + M)
+    w = torch.randint(-127, 128, (V, D), generator=g, dtype=torch.int32).to(torch.int8).to(cuda_dev)
+    s = (torch.rand(V, 1, generator=g) * 2e-3 + 1e-4).half().to(cuda_dev)
+    xb = (torch.randn(M, D + 24, generator=g) * 2).half().to(cuda_dev)
+    xb[M // 2, 7] = 900.0                            # a hot channel in one row only
+    x = xb[:, :D]
+    lb = torch.full((M, V + 5), -1.0, dtype=torch.float32, device=cuda_dev)
+    logits = lb[:, :V]
+    ids = _native.i8_head_argmax(x, w, s, logits)
+    for m in range(M):
+        one = torch.empty(1, V, dtype=torch.float32, device=cuda_dev)
+        idm = _native.i8_head_argmax(x[m:m + 1].contiguous(), w, s, one)
+        assert torch.equal(logits[m:m + 1], one), m
+        assert int(ids[m]) == int(idm[0]), m
+    assert bool((lb[:, V:] == -1.0).all())
+    ref = oracle.i8_head(x.float().cpu().numpy().astype(np.float16), w.cpu().numpy(), s.cpu().numpy())
+    assert rel_err(logits.cpu().numpy(), ref) < 1e-3
+    assert _native.device_error() == 0
+
+
 def test_head_graph_replay(cuda_dev):
     """The head's launch (its weight tensor map travels in the kernel parameters) replays
     from a CUDA graph exactly as it ran eagerly."""
