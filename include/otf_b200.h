@@ -406,6 +406,22 @@ OTF_API int otf_attn_rope_decode_batch(const void* q, int64_t ldq, const void* k
 OTF_API int otf_pos_advance_batch(int32_t* pos, int64_t n, void* stream);
 
 /*
+ * Prompt prefill for one sequence, after its q/k/v projections ran at M = rows prompt rows:
+ * row r sits at position *pos + r (pos: one device int32, the first prompt position; it is not
+ * advanced).  Two launches: q and k of every row rotated in place (as otf_rope_kv), k and v
+ * written to cache rows *pos .. *pos + rows - 1; then causal attention of row r over cache rows
+ * [0, *pos + r], out + r*ldo as otf_attn_decode's layout.  Rows past max_pos write nothing and
+ * raise the otf_device_error flag.  No workspace.  Replaces the prompt forward of HF's
+ * LlamaAttention that the reference runner keeps around its projections (RoPE, cache update,
+ * causal softmax(q k^T / sqrt(d)) v; otf_llm/run_symmetric_2bit.py:150-187), one prompt pass
+ * instead of one decode step per prompt token.
+ */
+OTF_API int otf_attn_prefill(void* q, int64_t ldq, void* k, const void* v, int64_t ldkv, const void* cos_sin,
+                             const int32_t* pos, void* k_cache, void* v_cache, void* out, int64_t ldo, float scale,
+                             int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t max_pos, int64_t rows,
+                             void* stream);
+
+/*
  * otf_attn_decode without a workspace argument, for callers that cannot allocate device
  * memory (a plugin host that passes only the op's own tensors, an allocator frozen after
  * warm-up, code that must not call cudaMalloc).  No counterpart in the reference.

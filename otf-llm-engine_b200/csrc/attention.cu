@@ -637,6 +637,131 @@ __global__ void k_pos_advance(int* pos, int n) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) pos[i] += 1;
 }
 
+// Prompt prefill, rows r = 0..P-1 (grid.y) at positions *pos + r: q and k of row r rotated in
+// place (k_rope_kv's arithmetic), k and v copied into the caches at row *pos + r.  A row whose
+// position falls outside [0, max_pos) writes nothing and raises the position flag.
+__global__ void k_rope_kv_rows(uint16_t* q, int64_t ldq, uint16_t* k, const uint16_t* v, int64_t ldkv,
+                               const uint16_t* cos_sin, const int* pos, uint16_t* kc, uint16_t* vc, int heads,
+                               int kv_heads, int D, int max_pos) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.y, p0 = *pos;
+  if (p0 < 0 || p0 >= max_pos || r >= max_pos - p0) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(&g_attn_device_error, 1);
+    return;
+  }
+  const int p = p0 + r, half = D / 2;
+  q += (int64_t)r * ldq;
+  k += (int64_t)r * ldkv;
+  v += (int64_t)r * ldkv;
+  const uint16_t* cs = cos_sin + (int64_t)p * 2 * D;
+  const int nvec = (heads + kv_heads) * half;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < nvec; e += gridDim.x * blockDim.x) {
+    const int hh = e / half, i = e - hh * half;
+    uint16_t* x = hh < heads ? q + (int64_t)hh * D : k + (int64_t)(hh - heads) * D;
+    const __half a = __ushort_as_half(x[i]), b = __ushort_as_half(x[i + half]);
+    const __half c0 = __ushort_as_half(cs[i]), c1 = __ushort_as_half(cs[i + half]);
+    const __half s0 = __ushort_as_half(cs[D + i]), s1 = __ushort_as_half(cs[D + i + half]);
+    const __half lo = __hadd_rn(__hmul_rn(a, c0), __hmul_rn(__hneg(b), s0));
+    const __half hi = __hadd_rn(__hmul_rn(b, c1), __hmul_rn(a, s1));
+    x[i] = __half_as_ushort(lo);
+    x[i + half] = __half_as_ushort(hi);
+    if (hh >= heads) {
+      uint16_t* krow = kc + (int64_t)p * kv_heads * D + (int64_t)(hh - heads) * D;
+      krow[i] = __half_as_ushort(lo);
+      krow[i + half] = __half_as_ushort(hi);
+    }
+  }
+  const int nv = kv_heads * D;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < nv; e += gridDim.x * blockDim.x)
+    vc[(int64_t)p * nv + e] = v[e];
+}
+
+// Causal attention of prompt row r (grid.y; position p = *pos + r) over cache rows [0, p] for
+// the query heads of KV head g (grid.x): the decode kernel's per-warp online softmax (fp32,
+// the same dot-product and rescale arithmetic) with the positions dealt to 8 warps, merged in
+// shared memory by one CTA, so no workspace.  The rows were written by k_rope_kv_rows.
+constexpr int kPfWarps = 8;
+template <int D>
+__global__ void __launch_bounds__(kPfWarps * 32) k_attn_prefill(const uint16_t* q, int64_t ldq, const uint16_t* kc,
+                                                                const uint16_t* vc, const int* pos, uint16_t* out,
+                                                                int64_t ldo, float scale, int heads, int kv_heads,
+                                                                int max_pos) {
+  constexpr int PL = D / 32;
+  pdl_trigger();
+  pdl_wait();
+  const int g = blockIdx.x, r = blockIdx.y, p0 = *pos;
+  if (p0 < 0 || p0 >= max_pos || r >= max_pos - p0) return;  // flagged by k_rope_kv_rows
+  const int p = p0 + r, rep = heads / kv_heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float sm_m[kPfWarps][kAttnMaxRep], sm_l[kPfWarps][kAttnMaxRep];
+  __shared__ float sm_acc[kPfWarps][kAttnMaxRep][D];
+  q += (int64_t)r * ldq;
+  out += (int64_t)r * ldo;
+  float qv[kAttnMaxRep][PL];
+#pragma unroll
+  for (int h = 0; h < kAttnMaxRep; ++h)
+#pragma unroll
+    for (int i = 0; i < PL; ++i) qv[h][i] = h < rep ? h2f(q[(int64_t)(g * rep + h) * D + lane * PL + i]) * scale : 0.0f;
+  float m[kAttnMaxRep], l[kAttnMaxRep], acc[kAttnMaxRep][PL];
+#pragma unroll
+  for (int h = 0; h < kAttnMaxRep; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) acc[h][i] = 0.0f;
+  }
+  const int64_t stride = (int64_t)kv_heads * D;
+  for (int pp = warp; pp <= p; pp += kPfWarps) {
+    const uint16_t* kr = kc + pp * stride + (int64_t)g * D + lane * PL;
+    const uint16_t* vr = vc + pp * stride + (int64_t)g * D + lane * PL;
+    float kf[PL], vf[PL];
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      kf[i] = h2f(kr[i]);
+      vf[i] = h2f(vr[i]);
+    }
+#pragma unroll
+    for (int h = 0; h < kAttnMaxRep; ++h) {
+      if (h >= rep) break;
+      float d = 0.0f;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) d = fmaf(qv[h][i], kf[i], d);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      const float mn = fmaxf(m[h], d);
+      const float corr = __expf(m[h] - mn), w = __expf(d - mn);
+      l[h] = l[h] * corr + w;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) acc[h][i] = fmaf(acc[h][i], corr, w * vf[i]);
+      m[h] = mn;
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < kAttnMaxRep; ++h) {
+    if (h >= rep) break;
+    if (lane == 0) {
+      sm_m[warp][h] = m[h];
+      sm_l[warp][h] = l[h];
+    }
+#pragma unroll
+    for (int i = 0; i < PL; ++i) sm_acc[warp][h][lane * PL + i] = acc[h][i];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < rep * D; e += kPfWarps * 32) {
+    const int h = e / D, dd = e - h * D;
+    float mm = -INFINITY;
+    for (int w = 0; w < kPfWarps; ++w) mm = fmaxf(mm, sm_m[w][h]);
+    float ll = 0.0f, aa = 0.0f;
+    for (int w = 0; w < kPfWarps; ++w) {
+      const float c = sm_m[w][h] == -INFINITY ? 0.0f : __expf(sm_m[w][h] - mm);
+      ll += sm_l[w][h] * c;
+      aa += sm_acc[w][h][dd] * c;
+    }
+    out[(int64_t)(g * rep + h) * D + dd] = f2h(aa / ll);
+  }
+}
+
 }  // namespace otf
 
 namespace otf {
@@ -857,6 +982,40 @@ extern "C" OTF_API int otf_attn_rope_decode_batch(const void* q, int64_t ldq, co
                       : otf::launch_pdl(otf::attn2_kernel<64>(heads / kv_heads), grid, dim3(otf::kAttn2Threads), 0, s, 1u, qq, kn,
                                         vn, cs, pp, kc, vc, o, scale, (int)heads, (int)kv_heads, (int)max_pos, ws,
                                         tickets, max_split, ldq, ldkv, cache_stride, ldo, ws_stride);
+  return set_cuda_error(e);
+}
+
+extern "C" OTF_API int otf_attn_prefill(void* q, int64_t ldq, void* k, const void* v, int64_t ldkv,
+                                        const void* cos_sin, const int32_t* pos, void* k_cache, void* v_cache,
+                                        void* out, int64_t ldo, float scale, int64_t heads, int64_t kv_heads,
+                                        int64_t head_dim, int64_t max_pos, int64_t rows, void* stream) {
+  if (!q || !k || !v || !cos_sin || !pos || !k_cache || !v_cache || !out) return OTF_ERR_INVALID;
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads || heads / kv_heads > otf::kAttnMaxRep || max_pos <= 0)
+    return OTF_ERR_INVALID;
+  if (rows <= 0 || rows > max_pos || rows > 65535) return OTF_ERR_INVALID;
+  if (head_dim != 64 && head_dim != 128) return OTF_ERR_UNSUPPORTED;
+  if (ldq < heads * head_dim || ldo < heads * head_dim || ldkv < kv_heads * head_dim) return OTF_ERR_INVALID;
+  int st = check_device();
+  if (st != OTF_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* qq = static_cast<uint16_t*>(q);
+  auto* kc = static_cast<uint16_t*>(k_cache);
+  auto* vc = static_cast<uint16_t*>(v_cache);
+  const int* pp = reinterpret_cast<const int*>(pos);
+  const int nvec = (int)((heads + kv_heads) * head_dim / 2);
+  const dim3 rgrid((unsigned)std::max(1, std::min(otf::ceil_div(nvec, 256), 8)), (unsigned)rows);
+  cudaError_t e = otf::launch_pdl(otf::k_rope_kv_rows, rgrid, dim3(256), 0, s, 1u, qq, ldq, static_cast<uint16_t*>(k),
+                             static_cast<const uint16_t*>(v), ldkv, static_cast<const uint16_t*>(cos_sin), pp, kc, vc,
+                             (int)heads, (int)kv_heads, (int)head_dim, (int)max_pos);
+  if (e != cudaSuccess) return set_cuda_error(e);
+  const dim3 agrid((unsigned)kv_heads, (unsigned)rows);
+  e = head_dim == 128
+          ? otf::launch_pdl(otf::k_attn_prefill<128>, agrid, dim3(otf::kPfWarps * 32), 0, s, 1u, (const uint16_t*)qq, ldq,
+                       (const uint16_t*)kc, (const uint16_t*)vc, pp, static_cast<uint16_t*>(out), ldo, scale,
+                       (int)heads, (int)kv_heads, (int)max_pos)
+          : otf::launch_pdl(otf::k_attn_prefill<64>, agrid, dim3(otf::kPfWarps * 32), 0, s, 1u, (const uint16_t*)qq, ldq,
+                       (const uint16_t*)kc, (const uint16_t*)vc, pp, static_cast<uint16_t*>(out), ldo, scale,
+                       (int)heads, (int)kv_heads, (int)max_pos);
   return set_cuda_error(e);
 }
 

@@ -111,6 +111,7 @@ EXPORTS = (
     "otf_attn_workspace_bytes_batch",
     "otf_attn_rope_decode_batch",
     "otf_pos_advance_batch",
+    "otf_attn_prefill",
 )
 
 
@@ -189,6 +190,9 @@ def lib() -> ctypes.CDLL:
     L.otf_attn_rope_decode_batch.restype = i32
     L.otf_pos_advance_batch.argtypes = [vp, i64, vp]
     L.otf_pos_advance_batch.restype = i32
+    L.otf_attn_prefill.argtypes = [vp, i64, vp, vp, i64, vp, vp, vp, vp, vp, i64, ctypes.c_float, i64, i64, i64, i64,
+                                   i64, vp]
+    L.otf_attn_prefill.restype = i32
     L.otf2b_quantize_workspace_bytes.argtypes = [i64, i64]
     L.otf2b_quantize_workspace_bytes.restype = i64
     L.otf2b_quantize.argtypes = [vp, i32, i64, i64, i64, i64, vp, i64, vp, vp, i64, vp, i64, vp, i64, vp, i64, vp,

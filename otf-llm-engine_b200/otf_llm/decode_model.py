@@ -272,13 +272,69 @@ class GreedyDecoder:
         else:
             self._step()
 
-    def generate(self, prompt: torch.Tensor, new_tokens: int, logits_out: Optional[List[torch.Tensor]] = None
-                 ) -> torch.Tensor:
-        """Greedy continuation of prompt (int64 ids on the device) by new_tokens tokens."""
+    def prefill(self, prompt: torch.Tensor) -> None:
+        """The prompt's P tokens as one pass of P rows from the current position, as the
+        reference runner's HF generate runs a prompt in one forward: every projection at M = P
+        rows (the tensor-memory GEMM from 9 rows), RoPE + KV-cache write + causal attention of
+        the P rows (``otf_attn_prefill``), the MLP at M = P, then the final norm and the greedy
+        pick of the last row into ``ids`` (its logits in ``logits``); the position advances by
+        P.  One GPU (the tensor-parallel decoder feeds prompts token by token).  A prompt that
+        would run past the cache writes nothing and raises the otf_device_error flag."""
+        if self.world > 1:
+            raise NotImplementedError("prefill runs on one GPU; tensor-parallel decoders step the prompt")
+        cfg, L = self.cfg, _native.lib()
+        ids = prompt.reshape(-1).to(device=self.device, dtype=torch.int64)
+        P = int(ids.numel())
+        if P == 0:
+            return
+        if P > cfg.max_pos:
+            raise ValueError(f"prompt of {P} tokens exceeds the cache of {cfg.max_pos} positions")
+        f16 = dict(dtype=torch.float16, device=self.device)
+        qd, kvd = self.heads * cfg.head_dim, self.kv_heads * cfg.head_dim
+        inter = self.layers[0]["gate_proj"].out_features
+        h, h1, xn = (torch.empty(P, cfg.hidden, **f16) for _ in range(3))
+        q, attn = torch.empty(P, qd, **f16), torch.empty(P, qd, **f16)
+        k, v = torch.empty(P, kvd, **f16), torch.empty(P, kvd, **f16)
+        g, u, a = (torch.empty(P, inter, **f16) for _ in range(3))
+        st = _native._stream(self.device)
+        lin = BatchedGreedyDecoder._lin
+        _embed_into(self.embed, ids, h)
+        for li, layer in enumerate(self.layers):
+            _native.rmsnorm(h, self.in_norms[li], cfg.rms_eps, out=xn)
+            for n, o in (("q_proj", q), ("k_proj", k), ("v_proj", v)):
+                lin(layer[n], xn, o)
+            _native._check(L.otf_attn_prefill(
+                q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), k.stride(0), self.cos_sin.data_ptr(),
+                self.pos.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(), attn.data_ptr(), attn.stride(0),
+                1.0 / math.sqrt(cfg.head_dim), self.heads, self.kv_heads, cfg.head_dim, cfg.max_pos, P, st),
+                "otf_attn_prefill")
+            lin(layer["o_proj"], attn, h1, residual=h)
+            _native.rmsnorm(h1, self.post_norms[li], cfg.rms_eps, out=xn)
+            lin(layer["gate_proj"], xn, g)
+            lin(layer["up_proj"], xn, u)
+            _native.silu_mul(g, u, out=a)
+            lin(layer["down_proj"], a, h, residual=h1)
+        xl = self.b["xn"]
+        _native.rmsnorm(h[P - 1:P], self.final_norm, cfg.rms_eps, out=xl)
+        self._argmax(xl)
+        self.pos.add_(P)
+
+    def generate(self, prompt: torch.Tensor, new_tokens: int, logits_out: Optional[List[torch.Tensor]] = None,
+                 prefill: Optional[bool] = None) -> torch.Tensor:
+        """Greedy continuation of prompt (int64 ids on the device) by new_tokens tokens.  The
+        prompt runs as one ``prefill`` pass on one GPU unless per-token logits are asked for
+        (``logits_out``) or ``prefill=False``; otherwise token by token."""
         _check_prompt(prompt, self.embed.weight_int8.shape[0])
+        if prefill is None:
+            prefill = logits_out is None and self.world == 1
         self.reset()
         out = torch.empty(new_tokens, dtype=torch.int64, device=self.device)
         n = prompt.numel()
+        if prefill and n:
+            self.prefill(prompt)
+            if logits_out is not None:
+                logits_out.append(self.logits.clone())
+            n = 0
         for i in range(n):
             self.ids.copy_(prompt[i:i + 1])
             self.step()
