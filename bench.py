@@ -582,8 +582,8 @@ def run_e2e(args):
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     with ClockSampler(local) as clk:
         e0.record()
-        if Bt == 1 and world == 1:
-            dec.prefill(prompt[0])          # the prompt as one pass of P rows
+        if world == 1:
+            dec.prefill(prompt[0] if Bt == 1 else prompt)   # the prompt as one pass of Bt x P rows
         else:
             for i in range(P):
                 dec.ids.copy_(prompt[:, i])
@@ -611,7 +611,7 @@ def run_e2e(args):
             "value": round(Bt * T / t_dec, 1), "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
             "batch": Bt, "prompt_tokens": P, "new_tokens": T, "ms_per_step": round(t_dec / T * 1e3, 4),
             "prefill_tokens_per_s": round(Bt * P / t_pre, 1),
-            "prefill": ("one pass of P rows (tensor-memory GEMM, causal prefill attention)" if Bt == 1 and world == 1
+            "prefill": ("one pass of batch x P rows (tensor-memory GEMM, causal prefill attention)" if world == 1
                         else "token by token (graph replays)"),
             "hbm_gbs_per_gpu": round(rank_gbs, 1), "frac_of_peak_per_gpu": round(rank_gbs / peak, 4),
             "peak_gbs": peak, "peak_kind": peak_kind,

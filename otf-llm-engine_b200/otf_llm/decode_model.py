@@ -496,16 +496,80 @@ class BatchedGreedyDecoder:
         else:
             self._step()
 
-    def generate(self, prompts: torch.Tensor, new_tokens: int, logits_out: Optional[List[torch.Tensor]] = None
-                 ) -> torch.Tensor:
+    def prefill(self, prompts: torch.Tensor) -> None:
+        """Every sequence's P prompt tokens as one pass of batch x P rows from the current
+        positions (``GreedyDecoder.prefill`` for a batch): the projections at M = batch x P rows,
+        ``otf_attn_prefill`` per sequence on its own caches, then the last row of each sequence
+        through the final norm and the head + argmax into ``ids``; every position advances by
+        P.  One GPU."""
+        if self.world > 1:
+            raise NotImplementedError("prefill runs on one GPU; tensor-parallel decoders step the prompt")
+        if prompts.dim() != 2 or prompts.shape[0] != self.batch:
+            raise ValueError(f"prompts must be [{self.batch}, P]")
+        cfg, L, B = self.cfg, _native.lib(), self.batch
+        P = int(prompts.shape[1])
+        if P == 0:
+            return
+        if P > cfg.max_pos:
+            raise ValueError(f"prompts of {P} tokens exceed the cache of {cfg.max_pos} positions")
+        ids = prompts.reshape(-1).to(device=self.device, dtype=torch.int64)
+        R = B * P
+        f16 = dict(dtype=torch.float16, device=self.device)
+        qd, kvd = self.heads * cfg.head_dim, self.kv_heads * cfg.head_dim
+        inter = self.layers[0]["gate_proj"].out_features
+        h, h1, xn = (torch.empty(R, cfg.hidden, **f16) for _ in range(3))
+        q, attn = torch.empty(R, qd, **f16), torch.empty(R, qd, **f16)
+        k, v = torch.empty(R, kvd, **f16), torch.empty(R, kvd, **f16)
+        g, u, a = (torch.empty(R, inter, **f16) for _ in range(3))
+        st = _native._stream(self.device)
+        scale = 1.0 / math.sqrt(cfg.head_dim)
+        _embed_into(self.embed, ids, h)
+        for li, layer in enumerate(self.layers):
+            _native.rmsnorm(h, self.in_norms[li], cfg.rms_eps, out=xn)
+            for n, o in (("q_proj", q), ("k_proj", k), ("v_proj", v)):
+                self._lin(layer[n], xn, o)
+            for sb in range(B):
+                r0 = sb * P
+                _native._check(L.otf_attn_prefill(
+                    q[r0].data_ptr(), q.stride(0), k[r0].data_ptr(), v[r0].data_ptr(), k.stride(0),
+                    self.cos_sin.data_ptr(), self.pos[sb].data_ptr(), self.kc[li][sb].data_ptr(),
+                    self.vc[li][sb].data_ptr(), attn[r0].data_ptr(), attn.stride(0), scale, self.heads,
+                    self.kv_heads, cfg.head_dim, cfg.max_pos, P, st), "otf_attn_prefill")
+            self._lin(layer["o_proj"], attn, h1, residual=h)
+            _native.rmsnorm(h1, self.post_norms[li], cfg.rms_eps, out=xn)
+            self._lin(layer["gate_proj"], xn, g)
+            self._lin(layer["up_proj"], xn, u)
+            _native.silu_mul(g, u, out=a)
+            self._lin(layer["down_proj"], a, h, residual=h1)
+        last = self.b["h"]
+        last.copy_(h.view(B, P, cfg.hidden)[:, P - 1])
+        _native.rmsnorm(last, self.final_norm, cfg.rms_eps, out=self.b["xn"])
+        w, s = self.head.weight_int8, self.head.scales.reshape(-1)
+        _native._check(L.otf_i8_head_argmax(self.b["xn"].data_ptr(), self.b["xn"].stride(0), w.data_ptr(), w.stride(0),
+                                            s.data_ptr(), self.logits.data_ptr(), self.logits.shape[1],
+                                            self.ids.data_ptr(), B, w.shape[0], w.shape[1], st), "otf_i8_head_argmax")
+        self.pos.add_(P)
+
+    def generate(self, prompts: torch.Tensor, new_tokens: int, logits_out: Optional[List[torch.Tensor]] = None,
+                 prefill: Optional[bool] = None) -> torch.Tensor:
         """Greedy continuation of prompts (int64 [batch, P] on the device, equal lengths) by
-        new_tokens tokens per sequence; returns int64 [batch, new_tokens]."""
+        new_tokens tokens per sequence; returns int64 [batch, new_tokens].  On one GPU the
+        prompts run as one ``prefill`` pass unless per-token logits are asked for
+        (``logits_out``) or ``prefill=False``."""
         if prompts.dim() != 2 or prompts.shape[0] != self.batch:
             raise ValueError(f"prompts must be [{self.batch}, P]")
         _check_prompt(prompts, self.embed.weight_int8.shape[0])
+        if prefill is None:
+            prefill = logits_out is None and self.world == 1
         self.reset()
         out = torch.empty(self.batch, new_tokens, dtype=torch.int64, device=self.device)
-        for i in range(prompts.shape[1]):
+        n = prompts.shape[1]
+        if prefill and n:
+            self.prefill(prompts)
+            if logits_out is not None:
+                logits_out.append(self.logits.clone())
+            n = 0
+        for i in range(n):
             self.ids.copy_(prompts[:, i])
             self.step()
             if logits_out is not None:

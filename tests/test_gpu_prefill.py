@@ -129,3 +129,31 @@ def test_decoder_prefill_matches_token_steps(P, cuda_dev):
     tc = b.generate(prompt, 2, logits_out=lg, prefill=True)
     assert len(lg) == 2 and torch.equal(tc, tb[:2])
     assert rel_err(lg[0].cpu().numpy(), la[-1].cpu().numpy()) < 2e-2
+
+
+@pytest.mark.parametrize("B,P", [(3, 7), (16, 5)])
+def test_batched_prefill_matches_batch1_prefill(B, P, cuda_dev):
+    """BatchedGreedyDecoder.prefill (projections at M = B x P rows, prefill attention per
+    sequence on its own caches) against the batch-1 decoder's prefill of each sequence."""
+    from test_gpu_decode_model import _tiny_model
+    from otf_llm import _native
+    from otf_llm.decode_model import BatchedGreedyDecoder, GreedyDecoder
+    cfg, layers, norms, emb, head, fnorm = _tiny_model(cuda_dev, seed=6, max_pos=64)
+    bat = BatchedGreedyDecoder(cfg, layers, norms, emb, head, fnorm, cuda_dev, B)
+    one = GreedyDecoder(cfg, layers, norms, emb, head, fnorm, cuda_dev)
+    prompts = torch.from_numpy(np.random.default_rng(B + P).integers(0, cfg.vocab, (B, P))).to(cuda_dev)
+    _native.device_error(clear=True)
+    bat.prefill(prompts)
+    torch.cuda.synchronize()
+    assert _native.device_error(clear=True) == 0
+    assert bool((bat.pos == P).all())
+    assert torch.equal(bat.ids, torch.argmax(bat.logits, dim=1))
+    for s in (0, B // 2, B - 1):
+        one.reset()
+        one.prefill(prompts[s])
+        assert rel_err(bat.logits[s].cpu().numpy(), one.logits[0].cpu().numpy()) < 2e-2, s
+        for li in range(cfg.layers):
+            assert rel_err(bat.kc[li][s][:P].float().cpu().numpy(), one.kc[li][:P].float().cpu().numpy()) < 2e-2
+    bat.capture()
+    out = bat.generate(prompts, 4)                  # prefill + graph steps
+    assert out.shape == (B, 4) and bool((bat.pos == P + 3).all())
