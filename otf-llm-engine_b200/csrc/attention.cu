@@ -712,29 +712,50 @@ __global__ void __launch_bounds__(kPfWarps * 32) k_attn_prefill(const uint16_t* 
     for (int i = 0; i < PL; ++i) acc[h][i] = 0.0f;
   }
   const int64_t stride = (int64_t)kv_heads * D;
-  for (int pp = warp; pp <= p; pp += kPfWarps) {
-    const uint16_t* kr = kc + pp * stride + (int64_t)g * D + lane * PL;
-    const uint16_t* vr = vc + pp * stride + (int64_t)g * D + lane * PL;
-    float kf[PL], vf[PL];
+  // Warp w takes positions w, w + 8, w + 16, ... in that order; the k/v rows of the next
+  // kPfBatch of them are requested together (raw fp16 pairs) before they are used.
+  constexpr int kPfBatch = 4;
+  for (int base = warp; base <= p; base += kPfBatch * kPfWarps) {
+    uint32_t kraw[kPfBatch][PL / 2], vraw[kPfBatch][PL / 2];
 #pragma unroll
-    for (int i = 0; i < PL; ++i) {
-      kf[i] = h2f(kr[i]);
-      vf[i] = h2f(vr[i]);
+    for (int j = 0; j < kPfBatch; ++j) {
+      const int pp = base + j * kPfWarps;
+      const uint32_t* kr = reinterpret_cast<const uint32_t*>(kc + (pp <= p ? pp : 0) * stride + (int64_t)g * D + lane * PL);
+      const uint32_t* vr = reinterpret_cast<const uint32_t*>(vc + (pp <= p ? pp : 0) * stride + (int64_t)g * D + lane * PL);
+#pragma unroll
+      for (int i = 0; i < PL / 2; ++i) {
+        kraw[j][i] = kr[i];
+        vraw[j][i] = vr[i];
+      }
     }
 #pragma unroll
-    for (int h = 0; h < kAttnMaxRep; ++h) {
-      if (h >= rep) break;
-      float d = 0.0f;
+    for (int j = 0; j < kPfBatch; ++j) {
+      if (base + j * kPfWarps > p) break;
+      float kf[PL], vf[PL];
 #pragma unroll
-      for (int i = 0; i < PL; ++i) d = fmaf(qv[h][i], kf[i], d);
+      for (int i = 0; i < PL / 2; ++i) {
+        const float2 kk = __half22float2(*reinterpret_cast<const __half2*>(&kraw[j][i]));
+        const float2 vv = __half22float2(*reinterpret_cast<const __half2*>(&vraw[j][i]));
+        kf[2 * i] = kk.x;
+        kf[2 * i + 1] = kk.y;
+        vf[2 * i] = vv.x;
+        vf[2 * i + 1] = vv.y;
+      }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-      const float mn = fmaxf(m[h], d);
-      const float corr = __expf(m[h] - mn), w = __expf(d - mn);
-      l[h] = l[h] * corr + w;
+      for (int h = 0; h < kAttnMaxRep; ++h) {
+        if (h >= rep) break;
+        float d = 0.0f;
 #pragma unroll
-      for (int i = 0; i < PL; ++i) acc[h][i] = fmaf(acc[h][i], corr, w * vf[i]);
-      m[h] = mn;
+        for (int i = 0; i < PL; ++i) d = fmaf(qv[h][i], kf[i], d);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        const float mn = fmaxf(m[h], d);
+        const float corr = __expf(m[h] - mn), w = __expf(d - mn);
+        l[h] = l[h] * corr + w;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) acc[h][i] = fmaf(acc[h][i], corr, w * vf[i]);
+        m[h] = mn;
+      }
     }
   }
 #pragma unroll
