@@ -572,6 +572,8 @@ def run_e2e(args):
         dec = GreedyDecoder(cfg, layers, [(ones, ones)] * cfg.layers, emb, head, ones, dev, rank=rank, world=world,
                             process_group=pg, peer_ar=peer_ar, head_row0=r0)
     dec.capture()
+    if world == 1 and Bt == 1:
+        dec.capture_prefill(P)              # the timed prompt's prefill replays as one CUDA graph
     prompt = torch.randint(0, cfg.vocab, (Bt, P), generator=torch.Generator().manual_seed(5)).to(dev)
     for _ in range(max(1, args.warmup // 2)):
         dec.generate(prompt[:, :16] if Bt > 1 else prompt[0, :16], 8)
@@ -611,7 +613,8 @@ def run_e2e(args):
             "value": round(Bt * T / t_dec, 1), "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
             "batch": Bt, "prompt_tokens": P, "new_tokens": T, "ms_per_step": round(t_dec / T * 1e3, 4),
             "prefill_tokens_per_s": round(Bt * P / t_pre, 1),
-            "prefill": ("one pass of batch x P rows (tensor-memory GEMM, causal prefill attention)" if world == 1
+            "prefill": ("one pass of batch x P rows (tensor-memory GEMM, causal prefill attention" +
+                        ("; one CUDA graph)" if Bt == 1 else ")") if world == 1
                         else "token by token (graph replays)"),
             "hbm_gbs_per_gpu": round(rank_gbs, 1), "frac_of_peak_per_gpu": round(rank_gbs / peak, 4),
             "peak_gbs": peak, "peak_kind": peak_kind,

@@ -139,6 +139,7 @@ class GreedyDecoder:
             self.loc_idx = torch.zeros(1, dtype=torch.int64, device=dev)
             self.pairs = torch.zeros(world, 2, dtype=torch.float64, device=dev)
         self.graph = None
+        self._pf_graphs: Dict[int, Tuple[torch.cuda.CUDAGraph, torch.Tensor]] = {}
 
     # -- one token step (capturable) ----------------------------------------------------
     def _attention(self, li: int) -> None:
@@ -282,13 +283,44 @@ class GreedyDecoder:
         would run past the cache writes nothing and raises the otf_device_error flag."""
         if self.world > 1:
             raise NotImplementedError("prefill runs on one GPU; tensor-parallel decoders step the prompt")
-        cfg, L = self.cfg, _native.lib()
         ids = prompt.reshape(-1).to(device=self.device, dtype=torch.int64)
         P = int(ids.numel())
         if P == 0:
             return
-        if P > cfg.max_pos:
-            raise ValueError(f"prompt of {P} tokens exceeds the cache of {cfg.max_pos} positions")
+        if P > self.cfg.max_pos:
+            raise ValueError(f"prompt of {P} tokens exceeds the cache of {self.cfg.max_pos} positions")
+        rec = self._pf_graphs.get(P)
+        if rec is not None:                  # recorded by capture_prefill for this length
+            rec[1].copy_(ids)
+            rec[0].replay()
+            return
+        self._prefill_rows(ids)
+
+    def capture_prefill(self, P: int) -> None:
+        """Record the prefill of P-token prompts as one CUDA graph, which ``prefill`` then
+        replays for every prompt of that length (the ids are copied into the graph's input
+        first); one eager pass runs before the capture, and the position is reset afterwards."""
+        if self.world > 1:
+            raise NotImplementedError("prefill runs on one GPU")
+        if not 0 < P <= self.cfg.max_pos:
+            raise ValueError(f"prompt length {P} outside 1..{self.cfg.max_pos}")
+        ids = torch.zeros(P, dtype=torch.int64, device=self.device)
+        cur = torch.cuda.current_stream(self.device)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            self._prefill_rows(ids)
+        cur.wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._prefill_rows(ids)
+        self._pf_graphs[P] = (g, ids)
+        self.reset()
+
+    def _prefill_rows(self, ids: torch.Tensor) -> None:
+        cfg, L = self.cfg, _native.lib()
+        P = int(ids.numel())
         f16 = dict(dtype=torch.float16, device=self.device)
         qd, kvd = self.heads * cfg.head_dim, self.kv_heads * cfg.head_dim
         inter = self.layers[0]["gate_proj"].out_features

@@ -157,3 +157,28 @@ def test_batched_prefill_matches_batch1_prefill(B, P, cuda_dev):
     bat.capture()
     out = bat.generate(prompts, 4)                  # prefill + graph steps
     assert out.shape == (B, 4) and bool((bat.pos == P + 3).all())
+
+
+def test_prefill_graph_matches_eager(cuda_dev):
+    """capture_prefill records the prefill of one prompt length as a CUDA graph; replays give
+    the eager prefill's logits, pick, caches and position bit for bit, for any prompt of that
+    length."""
+    from test_gpu_decode_model import _tiny_model
+    from otf_llm.decode_model import GreedyDecoder
+    cfg, layers, norms, emb, head, fnorm = _tiny_model(cuda_dev, seed=8, max_pos=64)
+    a = GreedyDecoder(cfg, layers, norms, emb, head, fnorm, cuda_dev)
+    b = GreedyDecoder(cfg, layers, norms, emb, head, fnorm, cuda_dev)
+    P = 11
+    b.capture_prefill(P)
+    assert int(b.pos.item()) == 0
+    for seed in (1, 2):
+        prompt = torch.from_numpy(np.random.default_rng(seed).integers(0, cfg.vocab, P)).to(cuda_dev)
+        a.reset()
+        b.reset()
+        a.prefill(prompt)
+        b.prefill(prompt)
+        torch.cuda.synchronize()
+        assert torch.equal(a.logits, b.logits) and torch.equal(a.ids, b.ids)
+        assert int(b.pos.item()) == P
+        for li in range(cfg.layers):
+            assert torch.equal(a.kc[li][:P], b.kc[li][:P]) and torch.equal(a.vc[li][:P], b.vc[li][:P])
